@@ -1,0 +1,327 @@
+"""Benchmark: Tsetlin Machine training (and inference) samples/s on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2] [--impl ours|reference]
+
+Default workload: configuration 2 (coalesced TM, 10k shared clauses, 784
+features, 10 classes, T=1000, s=15, mini-batch 256) on seeded synthetic
+prototype data.  A step is one mini-batch: clause evaluation of the batch,
+class sums (all-reduced over ranks when N > 1: clauses are sharded), and the
+Type I/II feedback.  N > 1 runs under torchrun, one rank per GPU, NCCL.
+
+--impl reference times the CPU restatement of the reference algorithm
+(oracle/, OpenMP over all host cores) on the same workload, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "train & infer samples/s (1/2/4/8 B200) + % of HBM/INT-pipe roofline vs CPU"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows if len(r) > 8 for n, v in zip(names, r[5:9]) if v == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def workload(name, n):
+    from ytm_b200 import synthetic
+    X, y = synthetic.make(name, n)
+    return X, y
+
+
+def cpu_sample(name, kw, B, budget_s=20.0, threads=None):
+    """Oracle (CPU restatement, OpenMP) training throughput on a bounded sample
+    of the workload: whole batches until ~budget_s of work."""
+    from oracle import oracle as O
+    if threads:
+        O.set_threads(threads)
+    o = O.Oracle(seed=42, **kw)
+    nb = max(1, min(B, 64))
+    X, y = workload(name, 4 * B if B > 1 else 256)
+    lits = o.encode(X)
+    Y = O.encode_Y_multiclass(y, kw["n_classes"], kw["T"])
+    ta, w, pw = o.init_state(), o.init_weights(), np.zeros((o.C, o.P), np.int32)
+    done, t0, t = 0, time.perf_counter(), 0
+    i = 0
+    while True:
+        b = B if B > 1 else 1
+        s = (i * b) % len(lits)
+        o.train_batch(ta, w, pw, lits[s:s + b], Y[s:s + b], t)
+        t += b
+        done += b
+        i += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or (B > 1 and done >= 4 * B) or (B == 1 and done >= 256):
+            break
+    del nb
+    return done / el, done, el, O.get_threads()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from ytm_b200 import synthetic
+    kw = synthetic.MODELS[args.workload]
+    B = synthetic.BATCH[args.workload]
+    from oracle import oracle as O
+    O.build()
+    threads = os.cpu_count()
+    O.set_threads(threads)
+    o = O.Oracle(seed=42, **kw)
+    b = B
+    X, y = workload(args.workload, b * max(2, args.steps + args.warmup))
+    lits = o.encode(X)
+    Y = O.encode_Y_multiclass(y, kw["n_classes"], kw["T"])
+    ta, w, pw = o.init_state(), o.init_weights(), np.zeros((o.C, o.P), np.int32)
+    t = 0
+    for i in range(args.warmup):
+        o.train_batch(ta, w, pw, lits[t:t + b], Y[t:t + b], t)
+        t += b
+    t_start = time.perf_counter()
+    for i in range(args.steps):
+        s = t % len(lits)
+        o.train_batch(ta, w, pw, lits[s:s + b], Y[s:s + b], t)
+        t += b
+    el = time.perf_counter() - t_start
+    v = args.steps * b / el
+    out = {"metric": METRIC, "impl": "reference", "value": v, "unit": "samples/s", "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * el / args.steps,
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u32",
+           "data": "synthetic", "config": {"workload": args.workload, "global_batch": b, **_cfgjson(kw)},
+           "cpu_baseline": {"value": v, "unit": "samples/s", "cores": O.get_threads(), "kind": "port",
+                            "sample": f"{args.steps} batches of {b} samples of {args.workload}, oracle/ytm_oracle.c "
+                                      f"(restatement of kernel.cu), OpenMP"},
+           "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def _cfgjson(kw):
+    return {k: (list(v) if isinstance(v, tuple) else v) for k, v in kw.items()}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--infer-samples", type=int, default=None)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    from ytm_b200 import synthetic
+    from ytm_b200.cutm import MultiClassTM
+
+    name = args.workload
+    kw = synthetic.MODELS[name]
+    B = synthetic.BATCH[name]
+    n_train = B * (args.steps + args.warmup)
+    X, y = workload(name, n_train)
+    tm = MultiClassTM(seed=42, device=dev, **kw)
+    eng = tm.engine
+    lits = tm._encode_device(X)
+    Yd = torch.from_numpy(tm.encode_Y(y)).to(dev)
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def step(i, ev=None):
+        lb, yb = lits[i * B:(i + 1) * B], Yd[i * B:(i + 1) * B]
+        t = tm.sample_counter
+        cs = eng.train_eval(lb, t, None, add_bias=rank == 0)
+        cs = tm._allreduce(cs)
+        if ev:
+            ev[0].record()
+        eng.train_update(cs, yb, lb, t, None)
+        if ev:
+            ev[1].record()
+        tm.sample_counter += B
+
+    for i in range(args.warmup):
+        step(i)
+    barrier()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    upd = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        barrier()
+        for j in range(args.steps):
+            flush.zero_()  # L2 flush between timed steps (outside the step events)
+            starts[j].record()
+            step(args.warmup + j, upd[j])
+            ends[j].record()
+        barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    upd_ms = [a.elapsed_time(b) for a, b in upd]
+    total_ms = sum(step_ms)
+    if world > 1:
+        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    value = args.steps * B / (total_ms / 1000.0)
+
+    # roofline of the dominant kernel (feedback): the state's read-modify-write
+    cfg = eng.cfg
+    chunks = (B + 31) // 32
+    alg_bytes = cfg.clause_count * chunks * cfg.planes * cfg.words * 4 * 2 + B * cfg.words * 4 * cfg.patches
+    upd_s = statistics.mean(upd_ms) / 1000.0
+    peak, peak_kind = load_peaks()
+    achieved = alg_bytes / upd_s / 1e9
+
+    # inference samples/s on the trained state
+    ni = args.infer_samples or (65536 if name in ("c1", "c2") else 4096)
+    Xi, _ = workload(name, ni)
+    lits_i = tm._encode_device(Xi)
+    for _ in range(2):
+        tm._score_device(lits_i)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    flush.zero_()
+    e0.record()
+    tm._score_device(lits_i)
+    e1.record()
+    barrier()
+    infer_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([infer_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        infer_ms = float(t.item())
+    infer_value = ni / (infer_ms / 1000.0)
+    word_tests = ni * cfg.clauses * cfg.patches * cfg.words
+
+    # end to end through the public API: pinned host inputs, H2D, encode, train,
+    # D2H of the batch's class sums
+    Xh = torch.from_numpy(X.view(np.int32)).pin_memory()
+    yh = y
+    for i in range(2):
+        tm.fit(Xh[i * B:(i + 1) * B], yh[i * B:(i + 1) * B], batch_size=B)
+    barrier()
+    a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for j in range(args.steps):
+        i = (args.warmup + j) % (n_train // B)
+        tm.fit(Xh[i * B:(i + 1) * B], yh[i * B:(i + 1) * B], batch_size=B)
+        tm.last_class_sums.cpu()
+    b_.record()
+    barrier()
+    e2e_ms = a.elapsed_time(b_)
+    if world > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": args.steps * B / (e2e_ms / 1000.0), "unit": "samples/s",
+           "h2d_bytes_per_step": int(B * X.shape[1] * 4 + B * kw["n_classes"] * 4),
+           "d2h_bytes_per_step": int(B * kw["n_classes"] * 4)}
+
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "u32", "data": "synthetic",
+            "config": {"workload": name, "global_batch": B, "parallelism": f"clause-shard{world}",
+                       "l2": "flushed between timed steps (2x L2 write)", **_cfgjson(kw)},
+            "e2e": e2e,
+            "gpu_launches": 7 * args.steps,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "kernel": "k_update (feedback)",
+                         "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg_bytes,
+                         "launch_ms": statistics.mean(upd_ms)},
+            "infer": {"value": infer_value, "unit": "samples/s", "samples": ni,
+                      "dense_word_tests_per_s": word_tests / (infer_ms / 1000.0)},
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu:
+            v, done, el, thr = cpu_sample(name, kw, B)
+            out["cpu_baseline"] = {"value": v, "unit": "samples/s", "cores": thr, "kind": "port",
+                                   "sample": f"{done} samples of {name} in {el:.1f}s, oracle/ytm_oracle.c, OpenMP"}
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

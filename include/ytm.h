@@ -1,0 +1,199 @@
+/*
+ * ytm.h — C ABI of libytm.so, the B200 (sm_100a) Tsetlin Machine engine.
+ *
+ * This ABI replaces the pycuda launch boundary of the reference engine
+ * (Mayur1009/YTM, src/cutm/base.py:128-206 builds a macro preamble, JIT-compiles
+ * src/cutm/cuda/kernel.cu and launches its extern "C" kernels through
+ * `prepared_call`).  Every entry point here is a host function taking plain
+ * device pointers, sizes and a CUDA stream (`void *stream`, a cudaStream_t);
+ * no torch or pycuda type crosses the boundary.
+ *
+ * Conventions
+ *  - The caller owns every buffer.  Functions that need scratch memory take a
+ *    `workspace` pointer whose size is given by ytm_workspace_bytes().
+ *  - Launches are asynchronous on `stream`; nothing synchronises the device.
+ *  - Every function returns a ytm_status; on failure ytm_last_error() returns a
+ *    message (thread-local).  Nothing calls exit() or abort().
+ *  - Hyper-parameters are runtime values in ytm_config (the reference bakes them
+ *    into #defines and compiles one kernel module per model, base.py:129-152).
+ *
+ * Data layouts in device memory (C = cfg->clause_count clauses held by this
+ * process, K = classes, L = literals, W = literal words, P = patches):
+ *  - literals   u32 [N][P][W]   bit j of word w = literal 32*w+j of a patch;
+ *                               identical to the reference's encoded X
+ *                               (kernel.cu:76-152, base.py:238).
+ *  - state      u32 [B][C][W]   bit-sliced TA states, B = cfg->planes.  Bit j of
+ *                               plane b, word w of clause c is bit b of
+ *                               (state + cfg->state_offset) of literal 32*w+j.
+ *                               Plane B-1 is the include mask.
+ *  - weights    i32 [C][K]      clause weights (reference: f32, base.py:190).
+ *  - class sums i32 [N][K].
+ *  - patch_w    i32 [C][P]      patch selection counts (base.py:191).
+ */
+#ifndef YTM_H_
+#define YTM_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int ytm_status;
+#define YTM_OK 0
+#define YTM_ERR_ARG 1         /* bad argument: shape, null pointer, range      */
+#define YTM_ERR_CUDA 2        /* a CUDA runtime call failed                    */
+#define YTM_ERR_UNSUPPORTED 3 /* configuration outside what the engine builds  */
+
+/* Model configuration.  Filled by ytm_config_init() from the reference's
+ * constructor arguments (base.py:42-125); the derived fields follow
+ * base.py:94-121. */
+typedef struct ytm_config {
+    /* reference constructor arguments */
+    int32_t clauses_per_class; /* number_of_clauses_per_class                  */
+    int32_t T;                 /* threshold (THRESH, base.py:131)               */
+    double s;                  /* specificity (S)                               */
+    double q;                  /* min(q, n_classes) (base.py:81)                */
+    int32_t dim0, dim1, dim2;
+    int32_t n_classes;
+    int32_t patch_dim0, patch_dim1;
+    int32_t number_of_ta_states; /* MAX_TA_STATE (base.py:146)                */
+    int32_t max_included_literals; /* MAX_INCLUDED_LITERALS (base.py:141)     */
+    int32_t append_negated, init_neg_weights, negative_polarity;
+    int32_t encode_loc, coalesced;
+    uint64_t seed;
+    /* derived sizes (base.py:94-121) */
+    int32_t clause_banks;      /* 1 if coalesced else n_classes                 */
+    int32_t clauses;           /* clause_banks * clauses_per_class (global)     */
+    int32_t literals;          /* L                                             */
+    int32_t words;             /* W = (L-1)/32 + 1                              */
+    int32_t patches;           /* P                                             */
+    int32_t half_literals;     /* L/2 (first negated literal when appended)     */
+    int32_t loc_literals;      /* (D1-P1) + (D0-P0) location literals           */
+    /* bit-sliced TA state encoding */
+    int32_t max_state;         /* = number_of_ta_states                         */
+    int32_t half_state;        /* = max_state / 2; include iff state > half     */
+    int32_t planes;            /* bits per counter                              */
+    int32_t state_offset;      /* stored value = state + state_offset           */
+    int32_t state_top;         /* largest representable state                  */
+    /* decision thresholds (fractions of 2^32 or 2^16) */
+    uint32_t s_threshold16;    /* literal mask Bernoulli(1/s) = thr / 65536     */
+    uint64_t q_threshold;      /* negative-class selection, thr / 2^32          */
+    /* clause shard held by this process */
+    int32_t clause_lo;         /* first global clause index                     */
+    int32_t clause_count;      /* clauses held (C above)                        */
+} ytm_config;
+
+/* Fill *cfg.  Arguments mirror BaseTM.__init__ (base.py:42-92) and its defaults
+ * (base.py:60-74); max_included_literals < 0 means "None" (= literals).
+ * The whole clause range is held (clause_lo = 0, clause_count = clauses). */
+ytm_status ytm_config_init(ytm_config *cfg, int32_t clauses_per_class, int32_t T, double s,
+                           int32_t dim0, int32_t dim1, int32_t dim2, int32_t n_classes,
+                           double q, int32_t patch_dim0, int32_t patch_dim1,
+                           int32_t number_of_ta_states, int32_t max_included_literals,
+                           int32_t append_negated, int32_t init_neg_weights,
+                           int32_t negative_polarity, int32_t encode_loc, int32_t coalesced,
+                           uint64_t seed);
+
+/* Restrict *cfg to the contiguous clause shard of `rank` out of `world`
+ * processes (no reference counterpart: the reference is single-GPU). */
+ytm_status ytm_config_shard(ytm_config *cfg, int32_t rank, int32_t world);
+
+/* Scratch sizes.  op is one of the YTM_OP_* values, n the sample count of the
+ * call (batch size for training). */
+#define YTM_OP_ENCODE 1
+#define YTM_OP_INFER 2
+#define YTM_OP_TRANSFORM 3
+#define YTM_OP_TRAIN 4
+uint64_t ytm_workspace_bytes(const ytm_config *cfg, int32_t op, int64_t n);
+
+/* Encode raw inputs into per-patch literal words.
+ * Replaces encode_batch (kernel.cu:76-152) as driven by BaseTM.encode
+ * (base.py:224-263).  X: u32 [N][dim0*dim1*dim2] (any nonzero value is a 1);
+ * lits: u32 [N][P][W].  workspace: ytm_workspace_bytes(cfg, YTM_OP_ENCODE, N). */
+ytm_status ytm_encode(const ytm_config *cfg, const uint32_t *X, int64_t N, uint32_t *lits,
+                      void *workspace, void *stream);
+
+/* Set every TA state of the shard to number_of_ta_states/2.
+ * Replaces _reset_clauses (base.py:208-209). */
+ytm_status ytm_state_init(const ytm_config *cfg, uint32_t *state, void *stream);
+
+/* Convert flat u32 TA states [C][L] (the reference's ta_state layout,
+ * base.py:189, get_state_dict base.py:561-582) into bit-sliced planes and back.
+ * from_u32 saturates values above cfg->state_top; callers validate first. */
+ytm_status ytm_state_from_u32(const ytm_config *cfg, const uint32_t *ta, uint32_t *state,
+                              void *stream);
+ytm_status ytm_state_to_u32(const ytm_config *cfg, const uint32_t *state, uint32_t *ta,
+                            void *stream);
+
+/* Include masks u32 [C][W] and include counts i32 [C] of the shard.
+ * Replaces pack_clauses (kernel.cu:155-204). */
+ytm_status ytm_include_mask(const ytm_config *cfg, const uint32_t *state, uint32_t *inc,
+                            int32_t *num_includes, void *stream);
+
+/* Initial clause weights i32 [C][K] of the shard.
+ * Replaces init_weights (kernel.cu:46-73) via _reset_weights (base.py:211-222). */
+ytm_status ytm_weights_init(const ytm_config *cfg, int32_t *weights, void *stream);
+
+/* Inference class sums: cs[n][k] = bias[k] + sum of weights[c][k] over the
+ * non-empty clauses c of the shard that match at least one patch of sample n.
+ * Replaces calc_class_sums_infer_batch (kernel.cu:319-343) as driven by
+ * _score_batch (base.py:375-420).  bias may be NULL (zero).  cs: i32 [N][K],
+ * fully overwritten.  workspace: ytm_workspace_bytes(cfg, YTM_OP_INFER, N). */
+ytm_status ytm_infer(const ytm_config *cfg, const uint32_t *state, const int32_t *weights,
+                     const int32_t *bias, const uint32_t *lits, int64_t N, int32_t *cs,
+                     void *workspace, void *stream);
+
+/* Clause outputs u32 [N][C] (1 if any patch matches; empty clauses give 1).
+ * Replaces transform (kernel.cu:346-368, base.py:465-502).
+ * workspace: ytm_workspace_bytes(cfg, YTM_OP_TRANSFORM, N). */
+ytm_status ytm_transform(const ytm_config *cfg, const uint32_t *state, const uint32_t *lits,
+                         int64_t N, uint32_t *out, void *workspace, void *stream);
+
+/* Per-patch clause outputs u32 [N][C][P] (empty clauses give 1).
+ * Replaces transform_patchwise (kernel.cu:370-394, base.py:504-542). */
+ytm_status ytm_transform_patchwise(const ytm_config *cfg, const uint32_t *state,
+                                   const uint32_t *lits, int64_t N, uint32_t *out,
+                                   void *stream);
+
+/* Training, part 1, for a batch of B samples whose first global sample
+ * counter is t0: freeze include counts, evaluate every clause of the shard on
+ * every patch (training semantics: empty clause matches, dropped clause never
+ * fires), pick one matching patch per (sample, clause), count it in patch_w,
+ * and write the shard's partial class sums cs i32 [B][K] (bias added when
+ * add_bias != 0).  Replaces pack_clauses + fast_eval + select_active
+ * (kernel.cu:155-204, 255-316) of the per-sample loop (base.py:305-337).
+ * drop: u32 [C] clause-drop mask or NULL.  workspace holds the batch's
+ * selections for ytm_train_update: ytm_workspace_bytes(cfg, YTM_OP_TRAIN, B). */
+ytm_status ytm_train_eval(const ytm_config *cfg, const uint32_t *state, const int32_t *weights,
+                          const int32_t *bias, const uint32_t *drop, const uint32_t *lits,
+                          int32_t B, uint64_t t0, int32_t add_bias, int32_t *cs,
+                          int32_t *patch_w, void *workspace, void *stream);
+
+/* Training, part 2: Type I / Type II feedback of the batch, applied clause by
+ * clause in sample order with the class sums cs i32 [B][K] (summed over all
+ * shards) and targets Y i32 [B][K] (+T / -T).  Replaces clause_update and
+ * type1a_fb / type1b_fb / type2_fb (kernel.cu:397-613, base.py:339-357).
+ * sel_override: i32 [B][C] patch picks to use instead of the ones
+ * ytm_train_eval chose (-1 = clause did not fire), or NULL. */
+ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, int32_t *weights,
+                            const int32_t *cs, const int32_t *Y, const uint32_t *drop,
+                            const uint32_t *lits, int32_t B, uint64_t t0,
+                            const int32_t *sel_override, void *workspace, void *stream);
+
+/* Read back the patch picks of the last ytm_train_eval on this workspace:
+ * sel i32 [B][C] (-1 = not fired).  Device-to-device copy on `stream`. */
+ytm_status ytm_train_selection(const ytm_config *cfg, int32_t B, const void *workspace,
+                               int32_t *sel, void *stream);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char *ytm_last_error(void);
+
+/* Library version string. */
+const char *ytm_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* YTM_H_ */

@@ -1,0 +1,72 @@
+"""CPU tests of the C ABI: the library loads, exports exactly what
+include/ytm.h declares, and derives the same sizes as the oracle."""
+import os
+import re
+
+import pytest
+
+from oracle.ref_build import SHAPES, derived
+from tests.helpers import lib_kwargs, oracle_for
+from ytm_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared():
+    src = open(os.path.join(ROOT, "include", "ytm.h")).read()
+    return set(re.findall(r"^\s*(?:const\s+)?[a-z0-9_]+\s*\*?\s*(ytm_[a-z0-9_]+)\s*\(", src, re.M))
+
+
+def test_header_matches_binding():
+    assert declared() == set(_lib.EXPORTS)
+
+
+def test_library_exports_all_symbols():
+    lib = _lib.load()
+    for name in declared():
+        assert hasattr(lib, name), name
+    assert lib.ytm_version().startswith(b"ytm-b200")
+
+
+@pytest.mark.parametrize("name", sorted(SHAPES))
+def test_config_matches_oracle(name):
+    kw = SHAPES[name]
+    cfg = _lib.make_config(**lib_kwargs(kw, seed=3))
+    o = oracle_for(name, seed=3)
+    d = derived(kw)
+    assert (cfg.clauses, cfg.n_classes, cfg.literals, cfg.words, cfg.patches) == (d["C"], d["K"], d["L"], d["W"], d["P"])
+    assert (cfg.clauses, cfg.literals, cfg.words, cfg.patches) == (o.C, o.L, o.W, o.P)
+    assert cfg.state_top == o.state_top and cfg.half_state == o.half_state
+    assert cfg.s_threshold16 == o.cfg.s_thr16 and cfg.q_threshold == o.cfg.q_thr
+    # include iff state > half  <=>  stored value has the top plane set
+    assert cfg.half_state + 1 + cfg.state_offset == 1 << (cfg.planes - 1)
+    assert cfg.state_top + cfg.state_offset == (1 << cfg.planes) - 1
+
+
+def test_config_errors():
+    with pytest.raises(_lib.YTMError):
+        _lib.make_config(clauses_per_class=0, T=1, s=1.0, dim=(4, 1, 1), n_classes=2)
+    with pytest.raises(_lib.YTMError):
+        _lib.make_config(clauses_per_class=4, T=1, s=1.0, dim=(4, 4, 1), n_classes=2, patch_dim=(5, 5))
+    with pytest.raises(_lib.YTMError):  # location literals outside the vector
+        _lib.make_config(clauses_per_class=4, T=1, s=1.0, dim=(28, 28, 1), n_classes=2, patch_dim=(3, 3),
+                         encode_loc=False)
+
+
+def test_shard_partition():
+    cfg = _lib.make_config(clauses_per_class=1001, T=10, s=3.0, dim=(8, 1, 1), n_classes=3)
+    parts = [_lib.shard_config(cfg, r, 4) for r in range(4)]
+    assert parts[0].clause_lo == 0
+    for a, b in zip(parts, parts[1:]):
+        assert a.clause_lo + a.clause_count == b.clause_lo
+    assert parts[-1].clause_lo + parts[-1].clause_count == cfg.clauses
+    with pytest.raises(_lib.YTMError):
+        _lib.shard_config(cfg, 4, 4)
+
+
+def test_workspace_sizes_grow_with_batch():
+    cfg = _lib.make_config(clauses_per_class=100, T=10, s=3.0, dim=(28, 28, 1), n_classes=10, patch_dim=(10, 10))
+    lib = _lib.load()
+    a = lib.ytm_workspace_bytes(cfg, _lib.YTM_OP_TRAIN, 1)
+    b = lib.ytm_workspace_bytes(cfg, _lib.YTM_OP_TRAIN, 8)
+    assert 0 < a < b and a % 256 == 0

@@ -1,0 +1,207 @@
+"""GPU parity tests: the CUDA engine (through the C ABI) against the reference
+kernels' fixtures and against the oracle.  Everything integer: bit-exact."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from oracle.ref_build import SHAPES
+from tests.helpers import golden_names, lib_kwargs, load_golden, oracle_kwargs
+from ytm_b200 import _lib
+from ytm_b200.engine import CudaEngine
+
+pytestmark = pytest.mark.gpu
+
+
+def engine_for(kw, seed=0, rank=0, world=1):
+    cfg = _lib.make_config(**lib_kwargs(kw, seed))
+    if world > 1:
+        cfg = _lib.shard_config(cfg, rank, world)
+    return CudaEngine(cfg, "cuda:0")
+
+
+def dev(a, dtype=np.uint32):
+    a = np.ascontiguousarray(a, dtype=dtype)
+    return torch.from_numpy(a.view(np.int32)).cuda()
+
+
+def host(t):
+    return t.cpu().numpy()
+
+
+# ------------------------------------------------------------ golden: reference
+
+@pytest.mark.parametrize("name", golden_names("inf_"))
+def test_inference_matches_reference_kernels(name):
+    g = load_golden(name)
+    e = engine_for(SHAPES[name])
+    lits = e.encode(dev(g["X"]))
+    np.testing.assert_array_equal(host(lits).view(np.uint32), g["lits"])
+    e.set_ta_state(g["ta"])
+    np.testing.assert_array_equal(e.get_ta_state(), g["ta"])
+    inc, ninc = e.include_mask()
+    np.testing.assert_array_equal(host(inc).view(np.uint32), g["packed"])
+    np.testing.assert_array_equal(host(ninc), g["ninc"])
+    e.weights.copy_(torch.from_numpy(g["w"].astype(np.int32)))
+    np.testing.assert_array_equal(host(e.infer(lits)), g["cs"].astype(np.int32))
+    e.bias.copy_(torch.from_numpy(g["bias"].astype(np.int32)))
+    np.testing.assert_array_equal(host(e.infer(lits)), g["cs_bias"].astype(np.int32))
+    np.testing.assert_array_equal(host(e.transform(lits)), g["transform"])
+    np.testing.assert_array_equal(host(e.transform_patchwise(lits)), g["transform_patchwise"])
+    if "init_weights" in g:
+        e.reset_weights()
+        np.testing.assert_array_equal(host(e.weights), g["init_weights"].astype(np.int32))
+
+
+@pytest.mark.parametrize("name", golden_names("tr_"))
+def test_training_step_matches_reference_kernels(name):
+    g = load_golden(name)
+    e = engine_for(SHAPES[name])
+    for i in range(g["e"].shape[0]):
+        s = int(g["e"][i])
+        lits = dev(g["lits"][i][s:s + 1])
+        Y = dev(g["Y"][i][s:s + 1], np.int32)
+        e.set_ta_state(g["ta"][i])
+        e.weights.copy_(torch.from_numpy(g["w"][i].astype(np.int32)))
+        e.patch_w.copy_(torch.from_numpy(g["pw"][i]))
+        drop = dev(g["drop"][i])
+        cs = e.train_eval(lits, 0, drop, add_bias=True)
+        np.testing.assert_array_equal(host(cs)[0], g["cs"][i].astype(np.int32), err_msg=f"case {i}")
+        sel = host(e.selection(1))
+        np.testing.assert_array_equal(sel[0] >= 0, g["sel"][i] >= 0, err_msg=f"case {i} fired")
+        sel_ref = dev(g["sel"][i][None, :], np.int32)
+        e.train_update(cs, Y, lits, 0, drop, sel_override=sel_ref)
+        np.testing.assert_array_equal(e.get_ta_state(), g["ta1"][i], err_msg=f"case {i} TA states")
+        np.testing.assert_array_equal(host(e.weights), g["w1"][i].astype(np.int32), err_msg=f"case {i} weights")
+        if g["pw"][i].shape[1] == 1:  # a single patch: the pick is forced
+            np.testing.assert_array_equal(host(e.patch_w), g["pw1"][i], err_msg=f"case {i} patch weights")
+
+
+# ------------------------------------------------------------ oracle parity
+
+TRAIN_CASES = {
+    "vanilla": (dict(number_of_clauses_per_class=12, T=15, s=4.0, dim=(40, 1, 1), n_classes=3, coalesced=False), 1),
+    "coalesced_b1": (dict(number_of_clauses_per_class=40, T=30, s=6.0, dim=(50, 1, 1), n_classes=5), 1),
+    "coalesced_b7": (dict(number_of_clauses_per_class=40, T=30, s=6.0, dim=(50, 1, 1), n_classes=5), 7),
+    "coalesced_b40": (dict(number_of_clauses_per_class=33, T=30, s=6.0, dim=(70, 1, 1), n_classes=4), 40),
+    "conv": (dict(number_of_clauses_per_class=30, T=20, s=3.0, dim=(8, 8, 1), n_classes=3, patch_dim=(4, 4)), 1),
+    "conv_rgb_b3": (dict(number_of_clauses_per_class=20, T=20, s=5.0, dim=(7, 7, 3), n_classes=3,
+                         patch_dim=(4, 3)), 3),
+    "states4096": (dict(number_of_clauses_per_class=24, T=40, s=8.0, dim=(33, 1, 1), n_classes=4,
+                        number_of_ta_states=4096), 2),
+    "states16": (dict(number_of_clauses_per_class=24, T=10, s=2.0, dim=(33, 1, 1), n_classes=9,
+                      number_of_ta_states=16), 1),
+    "maxinc_nopol": (dict(number_of_clauses_per_class=24, T=10, s=3.0, dim=(40, 1, 1), n_classes=4,
+                          max_included_literals=4, negative_polarity=False), 2),
+    "noneg_noloc": (dict(number_of_clauses_per_class=16, T=10, s=3.0, dim=(8, 8, 1), n_classes=2,
+                         patch_dim=(4, 4), encode_loc=False, append_negated=False), 1),
+    "many_classes": (dict(number_of_clauses_per_class=70, T=50, s=10.0, dim=(30, 1, 1), n_classes=70), 2),
+}
+
+
+@pytest.mark.parametrize("case", sorted(TRAIN_CASES))
+def test_training_matches_oracle(case):
+    kw, bs = TRAIN_CASES[case]
+    seed = 1234
+    o = O.Oracle(**oracle_kwargs(kw, seed))
+    e = engine_for(kw, seed)
+    rng = np.random.default_rng(7)
+    N = 24
+    D = kw["dim"][0] * kw["dim"][1] * kw["dim"][2]
+    X = (rng.random((N, D)) < 0.35).astype(np.uint32)
+    labels = rng.integers(0, kw["n_classes"], N)
+    Y = O.encode_Y_multiclass(labels, kw["n_classes"], kw["T"])
+    lits_h = o.encode(X)
+    lits = e.encode(dev(X))
+    np.testing.assert_array_equal(host(lits).view(np.uint32), lits_h)
+    ta, w = o.init_state(), o.init_weights()
+    pw = np.zeros((o.C, o.P), np.int32)
+    np.testing.assert_array_equal(host(e.weights), w)
+    drop_h = (rng.random(o.C) < 0.1).astype(np.uint32) if case == "coalesced_b7" else None
+    drop = None if drop_h is None else dev(drop_h)
+    Yd = dev(Y, np.int32)
+    t = 0
+    for epoch in range(2):
+        for i in range(0, N, bs):
+            B = min(bs, N - i)
+            cs_o, sel_o = o.train_batch(ta, w, pw, lits_h[i:i + B], Y[i:i + B], t, drop=drop_h)
+            cs = e.train_eval(lits[i:i + B], t, drop, add_bias=True)
+            np.testing.assert_array_equal(host(cs), cs_o, err_msg=f"class sums, batch at {i}")
+            np.testing.assert_array_equal(host(e.selection(B)), sel_o, err_msg=f"patch picks, batch at {i}")
+            e.train_update(cs, Yd[i:i + B], lits[i:i + B], t, drop)
+            t += B
+        np.testing.assert_array_equal(e.get_ta_state(), ta, err_msg=f"TA states after epoch {epoch}")
+        np.testing.assert_array_equal(host(e.weights), w, err_msg=f"weights after epoch {epoch}")
+        np.testing.assert_array_equal(host(e.patch_w), pw, err_msg=f"patch weights after epoch {epoch}")
+    # something happened
+    assert not np.array_equal(ta, o.init_state())
+    # inference on the trained state
+    np.testing.assert_array_equal(host(e.infer(lits)), o.infer(ta, w, lits_h))
+    np.testing.assert_array_equal(host(e.transform(lits)), o.transform(ta, lits_h))
+    np.testing.assert_array_equal(host(e.transform_patchwise(lits)), o.transform_patchwise(ta, lits_h))
+
+
+def test_sharded_engines_match_oracle():
+    """Two clause shards on one GPU, class sums summed between the halves of
+    each batch, equal the unsharded oracle (the multi-GPU schedule)."""
+    kw = dict(number_of_clauses_per_class=50, T=30, s=5.0, dim=(40, 1, 1), n_classes=4)
+    seed = 99
+    o = O.Oracle(seed=seed, **{k: v for k, v in kw.items()})
+    parts = [engine_for(kw, seed, r, 3) for r in range(3)]
+    rng = np.random.default_rng(5)
+    X = (rng.random((30, 40)) < 0.4).astype(np.uint32)
+    Y = O.encode_Y_multiclass(rng.integers(0, 4, 30), 4, 30)
+    lits_h = o.encode(X)
+    ta, w = o.init_state(), o.init_weights()
+    pw = np.zeros((o.C, o.P), np.int32)
+    lits, Yd = dev(lits_h), dev(Y, np.int32)
+    t = 0
+    for i in range(0, 30, 5):
+        o.train_batch(ta, w, pw, lits_h[i:i + 5], Y[i:i + 5], t)
+        cs = sum(p.train_eval(lits[i:i + 5], t, None, add_bias=(r == 0)) for r, p in enumerate(parts))
+        for p in parts:
+            p.train_update(cs, Yd[i:i + 5], lits[i:i + 5], t, None)
+        t += 5
+    np.testing.assert_array_equal(np.concatenate([p.get_ta_state() for p in parts]), ta)
+    np.testing.assert_array_equal(np.concatenate([host(p.weights) for p in parts]), w)
+
+
+# ------------------------------------------------------------ full-size properties
+
+def test_state_roundtrip_config5_size():
+    """state_from_u32 -> state_to_u32 is the identity on a 13-plane model with
+    W = 1024 (config-5 literal width, fewer clauses)."""
+    kw = dict(number_of_clauses_per_class=512, T=20000, s=20.0, dim=(16384, 1, 1), n_classes=100,
+              number_of_ta_states=4096)
+    e = engine_for(kw)
+    rng = np.random.default_rng(0)
+    ta = rng.integers(0, e.cfg.state_top + 1, size=(e.C, e.L), dtype=np.uint32)
+    e.set_ta_state(ta)
+    np.testing.assert_array_equal(e.get_ta_state(), ta)
+    inc, ninc = e.include_mask()
+    np.testing.assert_array_equal(host(ninc), (ta > 2048).sum(1))
+
+
+def test_infer_equals_transform_times_weights_config1_size():
+    """Config-1 model (20000 clauses, W = 49): class sums == clause outputs x
+    weights over non-empty clauses, on 2048 samples."""
+    kw = dict(number_of_clauses_per_class=2000, T=50, s=10.0, dim=(28, 28, 1), n_classes=10, coalesced=False)
+    e = engine_for(kw, seed=4)
+    rng = np.random.default_rng(1)
+    ta = rng.integers(0, 129, size=(e.C, e.L), dtype=np.uint32)
+    X = (rng.random((2048, 784)) < 0.2).astype(np.uint32)
+    lits = e.encode(dev(X))
+    lh = host(lits).view(np.uint32)
+    for c in range(e.C):  # each clause includes 1-3 literals true in some sample
+        if c % 7 == 0:
+            continue
+        bits = np.unpackbits(lh[rng.integers(2048), 0].view(np.uint8), bitorder="little")[:e.L]
+        ones = np.flatnonzero(bits)
+        ta[c, rng.choice(ones, size=rng.integers(1, 4), replace=False)] = 200
+    e.set_ta_state(ta)
+    out = host(e.transform(lits)).astype(np.int64)
+    cs = host(e.infer(lits)).astype(np.int64)
+    nonempty = (ta > 128).any(1)
+    W = host(e.weights).astype(np.int64)
+    np.testing.assert_array_equal(cs, (out * nonempty[None, :]) @ W)
+    assert 0 < out.mean() < 1

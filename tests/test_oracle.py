@@ -1,0 +1,104 @@
+"""CPU tests of the oracle: Philox known answers, the fixtures the reference's
+own kernels produced (tests/golden/*.npz), and the mini-batch definition."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from oracle.ref_build import SHAPES
+from tests.helpers import golden_names, load_golden, oracle_for
+
+
+# Known-answer vectors of Philox4x32-10 published with Random123 (Salmon et al.).
+@pytest.mark.parametrize("ctr,key,want", [
+    ([0, 0, 0, 0], [0, 0], [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]),
+    ([0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344], [0xA4093822, 0x299F31D0],
+     [0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1]),
+])
+def test_philox_kat(ctr, key, want):
+    assert list(O.philox4x32_10(ctr, key)) == want
+
+
+def test_golden_fixtures_present():
+    names = golden_names()
+    assert set(names) == set(SHAPES), f"missing fixtures: {set(SHAPES) - set(names)}"
+
+
+@pytest.mark.parametrize("name", golden_names("inf_"))
+def test_oracle_matches_reference_inference(name):
+    g = load_golden(name)
+    o = oracle_for(name)
+    np.testing.assert_array_equal(o.encode(g["X"]), g["lits"])
+    packed, ninc = o.pack(g["ta"])
+    np.testing.assert_array_equal(packed, g["packed"])
+    np.testing.assert_array_equal(ninc, g["ninc"])
+    w = g["w"].astype(np.int32)
+    np.testing.assert_array_equal(o.infer(g["ta"], w, g["lits"]), g["cs"].astype(np.int32))
+    np.testing.assert_array_equal(o.infer(g["ta"], w, g["lits"], bias=g["bias"].astype(np.int32)),
+                                  g["cs_bias"].astype(np.int32))
+    np.testing.assert_array_equal(o.transform(g["ta"], g["lits"]), g["transform"])
+    np.testing.assert_array_equal(o.transform_patchwise(g["ta"], g["lits"]), g["transform_patchwise"])
+    if "init_weights" in g:
+        np.testing.assert_array_equal(o.init_weights(), g["init_weights"].astype(np.int32))
+
+
+@pytest.mark.parametrize("name", golden_names("tr_"))
+def test_oracle_matches_reference_training_step(name):
+    """One forced-decision iteration of the reference's _fit loop, restated by
+    the oracle with the reference's own patch pick."""
+    g = load_golden(name)
+    o = oracle_for(name)
+    for i in range(g["e"].shape[0]):
+        e = int(g["e"][i])
+        lits = g["lits"][i][e:e + 1]
+        Y = g["Y"][i][e:e + 1]
+        ta = np.ascontiguousarray(g["ta"][i])
+        w = g["w"][i].astype(np.int32)
+        drop = g["drop"][i]
+        sel_ref = g["sel"][i][None, :]
+        pw = np.ascontiguousarray(g["pw"][i])
+        cs, sel, ninc = o.train_eval(0, ta, w, lits, 1, 0, drop=drop, patch_w=pw.copy())
+        np.testing.assert_array_equal(cs[0], g["cs"][i].astype(np.int32), err_msg=f"case {i} class sums")
+        np.testing.assert_array_equal(sel >= 0, sel_ref >= 0, err_msg=f"case {i} fired clauses")
+        o.train_update(0, ta, w, cs, Y, lits, 1, 0, sel_ref, ninc, drop=drop)
+        np.testing.assert_array_equal(ta, g["ta1"][i], err_msg=f"case {i} TA states")
+        np.testing.assert_array_equal(w, g["w1"][i].astype(np.int32), err_msg=f"case {i} weights")
+        pw_exp = g["pw"][i].copy()
+        for c in np.flatnonzero(sel_ref[0] >= 0):
+            pw_exp[c, sel_ref[0, c]] += 1
+        np.testing.assert_array_equal(g["pw1"][i], pw_exp, err_msg=f"case {i} patch weights")
+
+
+def test_batch_of_one_equals_per_sample_loop():
+    """fit(batch_size=1) over N samples == N single-sample batches (the
+    reference's loop); batch_size=4 is a different, documented schedule."""
+    o2 = O.Oracle(number_of_clauses_per_class=24, T=15, s=3.0, dim=(40, 1, 1), n_classes=4, seed=5)
+    rng = np.random.default_rng(3)
+    X = (rng.random((20, 40)) < 0.4).astype(np.uint32)
+    lits = o2.encode(X)
+    Y = O.encode_Y_multiclass(rng.integers(0, 4, 20), 4, 15)
+    runs = []
+    for bs in (1, 1, 4):
+        ta, w = o2.init_state(), o2.init_weights()
+        pw = np.zeros((o2.C, o2.P), np.int32)
+        if len(runs) == 1:
+            for i in range(20):
+                o2.train_batch(ta, w, pw, lits[i:i + 1], Y[i:i + 1], i)
+        else:
+            o2.fit(ta, w, pw, lits, Y, 0, batch_size=bs)
+        runs.append((ta, w, pw))
+    for a, b in zip(runs[0], runs[1]):
+        np.testing.assert_array_equal(a, b)
+    assert any(not np.array_equal(a, b) for a, b in zip(runs[0], runs[2]))
+
+
+def test_smask_rate():
+    """The literal mask is Bernoulli(round(65536/s)/65536)."""
+    o = O.Oracle(number_of_clauses_per_class=4, T=10, s=10.0, dim=(4, 1, 1), n_classes=2, seed=9)
+    ones = sum(bin(o.smask_word(c, t, 0, 0)).count("1") for c in range(4) for t in range(500))
+    rate = ones / (4 * 500 * 32)
+    assert abs(rate - 6554 / 65536) < 0.01
+
+
+def test_oracle_threads():
+    O.set_threads(2)
+    assert O.get_threads() == 2

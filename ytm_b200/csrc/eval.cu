@@ -1,0 +1,331 @@
+// eval.cu — clause evaluation: inference class sums, transforms, and the
+// evaluation half of a training batch.
+//
+// A clause matches a patch iff no included literal is 0 in it:
+//     OR_w (inc[c][w] & ~x[row][w]) == 0          (one LOP3 per word test)
+// which is the reference's clause_match (kernel.cu:207-216): its FILTER mask of
+// the last word is implied because include bits beyond L are never set.
+//
+// The match kernel treats (sample, patch) rows x clauses like a GEMM tile:
+// 64 rows x 64 clauses per CTA, 16-word K-chunks staged in shared memory, 4x4
+// (row, clause) pairs per thread held in registers.  Its epilogue writes one of
+// three outputs: any-patch fired bits, per-patch match bits, or u32 per
+// (sample, clause, patch).  Class sums are then a sparse sum of weight rows
+// over the fired bits (int32 atomics: exact and order independent).
+#include "common.cuh"
+
+namespace ytm {
+
+enum { MODE_ANY = 0, MODE_PBITS = 1, MODE_PATCHWISE = 2 };
+
+constexpr int RT = 64, CT = 64, KW = 16, XS = RT + 4;
+
+template <int MODE>
+__global__ void __launch_bounds__(256) k_match(const uint32_t *__restrict__ inc, const uint32_t *__restrict__ lits,
+                                               int64_t R, int C, int W, int P, uint32_t *__restrict__ out) {
+    __shared__ __align__(16) uint32_t xs[KW][XS];
+    __shared__ __align__(16) uint32_t is[KW][XS];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int64_t row0 = (int64_t)blockIdx.x * RT;
+    const int c0 = blockIdx.y * CT;
+    uint32_t v[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[i][j] = 0u;
+
+    for (int w0 = 0; w0 < W; w0 += KW) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            int idx = tid + q * 256;
+            int r = idx / KW, kw = idx % KW;
+            int w = w0 + kw;
+            int64_t row = row0 + r;
+            int c = c0 + r;
+            xs[kw][r] = (row < R && w < W) ? __ldg(&lits[row * W + w]) : 0xFFFFFFFFu;
+            is[kw][r] = (c < C && w < W) ? __ldg(&inc[(int64_t)c * W + w]) : 0u;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kw = 0; kw < KW; ++kw) {
+            uint4 xv = *reinterpret_cast<const uint4 *>(&xs[kw][ty * 4]);
+            uint4 iv = *reinterpret_cast<const uint4 *>(&is[kw][tx * 4]);
+            uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w};
+            uint32_t ia[4] = {iv.x, iv.y, iv.z, iv.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) v[i][j] |= ia[j] & ~xa[i];
+        }
+        __syncthreads();
+    }
+
+    const int cb = c0 + tx * 4;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        int64_t row = row0 + ty * 4 + i;
+        if (row >= R) continue;
+        int64_t n = row / P;
+        int p = (int)(row % P);
+        if (MODE == MODE_ANY) {
+            uint32_t nib = 0u;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (v[i][j] == 0u && cb + j < C) nib |= 1u << j;
+            if (nib) {
+                const int CWn = (C + 31) / 32;
+                atomicOr(&out[n * CWn + (cb >> 5)], nib << (cb & 31));
+            }
+        } else if (MODE == MODE_PBITS) {
+            const int PW = (P + 31) / 32;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (v[i][j] == 0u && cb + j < C)
+                    atomicOr(&out[(n * C + cb + j) * PW + (p >> 5)], 1u << (p & 31));
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (cb + j < C) out[(n * C + cb + j) * P + p] = v[i][j] == 0u ? 1u : 0u;
+        }
+    }
+}
+
+template <int MODE>
+static ytm_status launch_match(const uint32_t *inc, const uint32_t *lits, int64_t R, int C, int W, int P,
+                               uint32_t *out, cudaStream_t st) {
+    if (R <= 0) return YTM_OK;
+    int64_t gx = (int64_t)cdiv(R, RT), gy = (int64_t)cdiv(C, CT);
+    if (gx > 0x7FFFFFFFll || gy > 65535) return fail(YTM_ERR_UNSUPPORTED, "match grid too large; split the batch");
+    k_match<MODE><<<dim3((unsigned)gx, (unsigned)gy), 256, 0, st>>>(inc, lits, R, C, W, P, out);
+    return launch_check("clause match");
+}
+
+__global__ void k_cs_init(int32_t *__restrict__ cs, const int32_t *__restrict__ bias, int64_t N, int K) {
+    int64_t total = N * K;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x)
+        cs[i] = bias ? bias[i % K] : 0;
+}
+
+// cs[n][k] += sum over fired clauses c of w[c][k].  A warp takes 32 bitmap
+// words (1024 clauses) of one sample; lanes own classes k = lane + 32 m.
+// ninc (inference): clauses with no include are skipped (kernel.cu:328).
+// own_class (training, non-coalesced): clause c adds only to its bank's class
+// (kernel.cu:306-312).
+constexpr int CS_WARPS = 4, CS_KREG = 8;
+
+__global__ void __launch_bounds__(CS_WARPS * 32) k_class_sums(const uint32_t *__restrict__ fired,
+                                                              const int32_t *__restrict__ ninc,
+                                                              const int32_t *__restrict__ w, int C, int K,
+                                                              int64_t N, int own_class, int clause_lo, int cpc,
+                                                              int32_t *__restrict__ cs) {
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int CWn = (C + 31) / 32;
+    const int64_t chunks = (CWn + 31) / 32;
+    const int64_t units = N * chunks;
+    for (int64_t u = (int64_t)blockIdx.x * CS_WARPS + wib; u < units; u += (int64_t)gridDim.x * CS_WARPS) {
+        const int64_t n = u / chunks;
+        const int wbase = (int)(u % chunks) * 32;
+        uint32_t mine = (wbase + lane < CWn) ? fired[n * CWn + wbase + lane] : 0u;
+        if (__ballot_sync(0xFFFFFFFFu, mine != 0u) == 0u) continue;
+        for (int k0 = 0; k0 < K; k0 += 32 * CS_KREG) {
+            int32_t acc[CS_KREG];
+#pragma unroll
+            for (int m = 0; m < CS_KREG; ++m) acc[m] = 0;
+            for (int j = 0; j < 32; ++j) {
+                uint32_t bits = __shfl_sync(0xFFFFFFFFu, mine, j);
+                while (bits) {
+                    int b = __ffs(bits) - 1;
+                    bits &= bits - 1;
+                    int c = (wbase + j) * 32 + b;
+                    if (ninc && ninc[c] == 0) continue;
+                    const int32_t *wr = w + (int64_t)c * K;
+                    if (own_class) {
+                        int k = (clause_lo + c) / cpc;
+                        int m = (k - k0) >> 5;
+                        if (k >= k0 && m < CS_KREG && ((k - k0) & 31) == lane) acc[m] += wr[k];
+                    } else {
+#pragma unroll
+                        for (int m = 0; m < CS_KREG; ++m) {
+                            int k = k0 + m * 32 + lane;
+                            if (k < K) acc[m] += wr[k];
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < CS_KREG; ++m) {
+                int k = k0 + m * 32 + lane;
+                if (k < K && acc[m] != 0) atomicAdd(&cs[n * K + k], acc[m]);
+            }
+        }
+    }
+}
+
+static ytm_status launch_class_sums(const uint32_t *fired, const int32_t *ninc, const int32_t *w,
+                                    const ytm_config *cfg, int64_t N, int own_class, int32_t *cs, cudaStream_t st) {
+    const int C = cfg->clause_count;
+    int64_t chunks = (int64_t)cdiv(cdiv(C, 32), 32);
+    int64_t blocks = std::min<int64_t>((int64_t)cdiv(N * chunks, CS_WARPS), (int64_t)sm_count() * 16);
+    if (blocks < 1) blocks = 1;
+    k_class_sums<<<(unsigned)blocks, CS_WARPS * 32, 0, st>>>(fired, ninc, w, C, cfg->n_classes, N, own_class,
+                                                              cfg->clause_lo, cfg->clauses_per_class, cs);
+    return launch_check("class sums");
+}
+
+__global__ void k_expand(const uint32_t *__restrict__ fired, int64_t N, int C, uint32_t *__restrict__ out) {
+    const int CWn = (C + 31) / 32;
+    int64_t total = N * C;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t n = i / C;
+        int c = (int)(i % C);
+        out[i] = (fired[n * CWn + (c >> 5)] >> (c & 31)) & 1u;
+    }
+}
+
+// One thread per (sample, clause): pick a matching patch uniformly
+// (reference select_active, kernel.cu:285-316, reservoir sampling; here the
+// TAG_PATCH draw r gives index floor(r * count / 2^32) among the matches in
+// patch order), count it in patch_w and set the fired bit.
+__global__ void k_pick(ytm_config cfg, const uint32_t *__restrict__ mbits, const uint32_t *__restrict__ drop,
+                       int B, uint64_t t0, int32_t *__restrict__ sel, uint32_t *__restrict__ fired,
+                       int32_t *__restrict__ patch_w) {
+    const int C = cfg.clause_count, P = cfg.patches, PW = (P + 31) / 32, CWn = (C + 31) / 32;
+    int64_t total = (int64_t)B * C;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int b = (int)(i / C), c = (int)(i % C);
+        int32_t s = -1;
+        if (!(drop && drop[c] == 1u)) {
+            const uint32_t *m = mbits + i * PW;
+            int cnt = 0;
+            for (int j = 0; j < PW; ++j) cnt += __popc(m[j]);
+            if (cnt > 0) {
+                uint32_t r = draw(cfg.seed, (uint32_t)(cfg.clause_lo + c), t0 + (uint64_t)b, 0, TAG_PATCH, 0).x;
+                uint32_t idx = (uint32_t)(((uint64_t)r * (uint64_t)cnt) >> 32);
+                for (int j = 0; j < PW; ++j) {
+                    uint32_t word = m[j];
+                    uint32_t pc = (uint32_t)__popc(word);
+                    if (idx < pc) {
+                        for (uint32_t q = 0; q < idx; ++q) word &= word - 1u;
+                        s = j * 32 + __ffs(word) - 1;
+                        break;
+                    }
+                    idx -= pc;
+                }
+                atomicAdd(&patch_w[(int64_t)c * P + s], 1);
+                atomicOr(&fired[(int64_t)b * CWn + (c >> 5)], 1u << (c & 31));
+            }
+        }
+        sel[i] = s;
+    }
+}
+
+static unsigned grid1(int64_t threads) {
+    int64_t b = (int64_t)cdiv(threads, 256);
+    int64_t cap = (int64_t)sm_count() * 32;
+    if (b > cap) b = cap;
+    return (unsigned)(b < 1 ? 1 : b);
+}
+
+}  // namespace ytm
+
+using namespace ytm;
+
+extern "C" {
+
+ytm_status ytm_infer(const ytm_config *cfg, const uint32_t *state, const int32_t *weights, const int32_t *bias,
+                     const uint32_t *lits, int64_t N, int32_t *cs, void *workspace, void *stream) {
+    ytm_status rc = check_cfg(cfg);
+    if (rc) return rc;
+    if (N < 0) return fail(YTM_ERR_ARG, "N < 0");
+    if (N == 0) return YTM_OK;
+    if (!state || !weights || !lits || !cs || !workspace) return fail(YTM_ERR_ARG, "null pointer");
+    cudaStream_t st = as_stream(stream);
+    const int C = cfg->clause_count, W = cfg->words, P = cfg->patches;
+    InferWs l = infer_ws_layout(cfg, N);
+    char *ws = (char *)workspace;
+    int32_t *ninc = (int32_t *)(ws + l.ninc);
+    uint32_t *fired = (uint32_t *)(ws + l.fired);
+    const uint32_t *inc = state + (int64_t)(cfg->planes - 1) * C * W;
+    if ((rc = launch_ninc(cfg, state, ninc, st))) return rc;
+    if ((rc = cuda_check(cudaMemsetAsync(fired, 0, (size_t)N * cdiv(C, 32) * 4, st), "memset"))) return rc;
+    if ((rc = launch_match<MODE_ANY>(inc, lits, N * P, C, W, P, fired, st))) return rc;
+    k_cs_init<<<grid1(N * cfg->n_classes), 256, 0, st>>>(cs, bias, N, cfg->n_classes);
+    if ((rc = launch_check("cs init"))) return rc;
+    return launch_class_sums(fired, ninc, weights, cfg, N, 0, cs, st);
+}
+
+ytm_status ytm_transform(const ytm_config *cfg, const uint32_t *state, const uint32_t *lits, int64_t N,
+                         uint32_t *out, void *workspace, void *stream) {
+    ytm_status rc = check_cfg(cfg);
+    if (rc) return rc;
+    if (N < 0) return fail(YTM_ERR_ARG, "N < 0");
+    if (N == 0) return YTM_OK;
+    if (!state || !lits || !out || !workspace) return fail(YTM_ERR_ARG, "null pointer");
+    cudaStream_t st = as_stream(stream);
+    const int C = cfg->clause_count, W = cfg->words, P = cfg->patches;
+    InferWs l = infer_ws_layout(cfg, N);
+    uint32_t *fired = (uint32_t *)((char *)workspace + l.fired);
+    const uint32_t *inc = state + (int64_t)(cfg->planes - 1) * C * W;
+    if ((rc = cuda_check(cudaMemsetAsync(fired, 0, (size_t)N * cdiv(C, 32) * 4, st), "memset"))) return rc;
+    // empty clauses match every patch, so they come out as 1 (kernel.cu:354-357)
+    if ((rc = launch_match<MODE_ANY>(inc, lits, N * P, C, W, P, fired, st))) return rc;
+    k_expand<<<grid1(N * C), 256, 0, st>>>(fired, N, C, out);
+    return launch_check("transform expand");
+}
+
+ytm_status ytm_transform_patchwise(const ytm_config *cfg, const uint32_t *state, const uint32_t *lits, int64_t N,
+                                   uint32_t *out, void *stream) {
+    ytm_status rc = check_cfg(cfg);
+    if (rc) return rc;
+    if (N < 0) return fail(YTM_ERR_ARG, "N < 0");
+    if (N == 0) return YTM_OK;
+    if (!state || !lits || !out) return fail(YTM_ERR_ARG, "null pointer");
+    const int C = cfg->clause_count, W = cfg->words, P = cfg->patches;
+    const uint32_t *inc = state + (int64_t)(cfg->planes - 1) * C * W;
+    return launch_match<MODE_PATCHWISE>(inc, lits, N * P, C, W, P, out, as_stream(stream));
+}
+
+ytm_status ytm_train_eval(const ytm_config *cfg, const uint32_t *state, const int32_t *weights, const int32_t *bias,
+                          const uint32_t *drop, const uint32_t *lits, int32_t B, uint64_t t0, int32_t add_bias,
+                          int32_t *cs, int32_t *patch_w, void *workspace, void *stream) {
+    ytm_status rc = check_cfg(cfg);
+    if (rc) return rc;
+    if (B <= 0) return fail(YTM_ERR_ARG, "batch must be positive");
+    if (!state || !weights || !lits || !cs || !patch_w || !workspace) return fail(YTM_ERR_ARG, "null pointer");
+    cudaStream_t st = as_stream(stream);
+    const int C = cfg->clause_count, W = cfg->words, P = cfg->patches;
+    TrainWs l = train_ws_layout(cfg, B);
+    char *ws = (char *)workspace;
+    int32_t *ninc = (int32_t *)(ws + l.ninc);
+    uint32_t *mbits = (uint32_t *)(ws + l.mbits);
+    int32_t *sel = (int32_t *)(ws + l.sel);
+    uint32_t *fired = (uint32_t *)(ws + l.fired);
+    const uint32_t *inc = state + (int64_t)(cfg->planes - 1) * C * W;
+    if ((rc = launch_ninc(cfg, state, ninc, st))) return rc;
+    if ((rc = cuda_check(cudaMemsetAsync(mbits, 0, (size_t)B * C * cdiv(P, 32) * 4, st), "memset"))) return rc;
+    if ((rc = cuda_check(cudaMemsetAsync(fired, 0, (size_t)B * cdiv(C, 32) * 4, st), "memset"))) return rc;
+    // training semantics: an empty clause matches every patch (kernel.cu:273-276)
+    if ((rc = launch_match<MODE_PBITS>(inc, lits, (int64_t)B * P, C, W, P, mbits, st))) return rc;
+    k_pick<<<grid1((int64_t)B * C), 256, 0, st>>>(*cfg, mbits, drop, B, t0, sel, fired, patch_w);
+    if ((rc = launch_check("patch pick"))) return rc;
+    k_cs_init<<<grid1((int64_t)B * cfg->n_classes), 256, 0, st>>>(cs, add_bias ? bias : nullptr, B,
+                                                                    cfg->n_classes);
+    if ((rc = launch_check("cs init"))) return rc;
+    return launch_class_sums(fired, nullptr, weights, cfg, B, cfg->coalesced ? 0 : 1, cs, st);
+}
+
+ytm_status ytm_train_selection(const ytm_config *cfg, int32_t B, const void *workspace, int32_t *sel,
+                               void *stream) {
+    ytm_status rc = check_cfg(cfg);
+    if (rc) return rc;
+    if (B <= 0 || !workspace || !sel) return fail(YTM_ERR_ARG, "bad argument");
+    TrainWs l = train_ws_layout(cfg, B);
+    return cuda_check(cudaMemcpyAsync(sel, (const char *)workspace + l.sel, (size_t)B * cfg->clause_count * 4,
+                                      cudaMemcpyDeviceToDevice, as_stream(stream)),
+                      "selection copy");
+}
+
+}  // extern "C"

@@ -1,0 +1,202 @@
+// update.cu — Type I / Type II feedback of a training batch.
+//
+// Reference: clause_update with type1a_fb / type1b_fb / type2_fb
+// (kernel.cu:397-613): one thread per clause walks classes and then all L
+// literals as u32 states, drawing one curand uniform per eligible literal.
+//
+// Here a CTA owns one clause.  Per chunk of 32 samples:
+//  1. threads over classes decide, for each (sample, class), whether and which
+//     feedback fires (Q-selection and update draws from Philox, target, weight
+//     sign), updating the clause's weights in shared memory as they go;
+//  2. the decided events are compacted into a list in (sample, class) order;
+//  3. threads over literal words load the word's bit planes once, apply every
+//     event of the chunk in order with bit-parallel ripple adders (32 literals
+//     per instruction), and store the planes once.
+// The state therefore makes one read-modify-write trip through HBM per chunk,
+// however many events the chunk holds.
+#include "common.cuh"
+
+namespace ytm {
+
+constexpr int UPD_BC = 32;  // samples per chunk
+
+// thr[b][k] = floor(p * 2^32) of the update probability, bit 63 set when the
+// target is -1 (kernel.cu:544-551, 569-571).
+__global__ void k_thresholds(const int32_t *__restrict__ cs, const int32_t *__restrict__ Y, int B, int K, int T,
+                             uint64_t *__restrict__ thr) {
+    int64_t total = (int64_t)B * K;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int32_t v = cs[i];
+        v = v > T ? T : (v < -T ? -T : v);  // clip_cs, kernel.cu:397
+        int32_t y = Y[i];
+        uint64_t t = update_threshold(y, v);
+        if (v > y) t |= 1ull << 63;
+        thr[i] = t;
+    }
+}
+
+enum : uint32_t { EV_NONE = 0, EV_T1A = 1, EV_T1B = 2, EV_T2 = 3 };
+
+template <int NB>
+__global__ void __launch_bounds__(256) k_update(ytm_config cfg, uint32_t *__restrict__ state,
+                                                int32_t *__restrict__ weights, const uint64_t *__restrict__ thr,
+                                                const uint32_t *__restrict__ drop,
+                                                const uint32_t *__restrict__ lits, int B, uint64_t t0,
+                                                const int32_t *__restrict__ sel, const int32_t *__restrict__ ninc) {
+    extern __shared__ __align__(16) unsigned char smraw[];
+    const int C = cfg.clause_count, W = cfg.words, K = cfg.n_classes, P = cfg.patches;
+    const int c = blockIdx.x;
+    const uint32_t g = (uint32_t)(cfg.clause_lo + c);
+    if (drop && drop[c] == 1u) return;  // kernel.cu:555
+    const int k0 = cfg.coalesced ? 0 : (int)(g / (uint32_t)cfg.clauses_per_class);
+    const int nk = cfg.coalesced ? K : 1;
+    int32_t *wk = (int32_t *)smraw;                       // [nk]
+    int32_t *sel_s = wk + nk;                             // [UPD_BC]
+    int32_t *cnt = sel_s + UPD_BC;                        // [UPD_BC + 1]
+    uint32_t *list = (uint32_t *)(cnt + UPD_BC + 1);      // [UPD_BC * nk]
+    uint8_t *evt = (uint8_t *)(list + UPD_BC * nk);       // [UPD_BC * nk]
+    const int tid = threadIdx.x, nt = blockDim.x;
+    const bool ok_inc = ninc[c] <= cfg.max_included_literals;
+    const uint32_t max_s = (uint32_t)(cfg.max_state + cfg.state_offset);
+    const uint32_t zero_s = (uint32_t)cfg.state_offset;
+
+    for (int kk = tid; kk < nk; kk += nt) wk[kk] = weights[(int64_t)c * K + k0 + kk];
+
+    for (int b0 = 0; b0 < B; b0 += UPD_BC) {
+        const int bc = min(UPD_BC, B - b0);
+        if (tid < bc) sel_s[tid] = sel[(int64_t)(b0 + tid) * C + c];
+        __syncthreads();
+        // 1. decisions, class-parallel, sample-sequential (weights evolve)
+        for (int kk = tid; kk < nk; kk += nt) {
+            const int k = k0 + kk;
+            int32_t wv = wk[kk];
+            for (int bl = 0; bl < bc; ++bl) {
+                const int b = b0 + bl;
+                uint64_t th = thr[(int64_t)b * K + k];
+                const int target = (th >> 63) ? -1 : 1;
+                th &= ~(1ull << 63);
+                u32x4 r = draw(cfg.seed, g, t0 + (uint64_t)b, 0, TAG_CLASS, (uint32_t)k);
+                uint8_t ev = EV_NONE;
+                bool pass = !(target == -1 && !((uint64_t)r.x < cfg.q_threshold));  // kernel.cu:573
+                if (pass && (uint64_t)r.y < th) {                                    // kernel.cu:582
+                    const int sign = (wv >= 0) - (wv < 0);
+                    const bool fired = sel_s[bl] > -1;
+                    const int ts = target * sign;
+                    if (ts > 0 && fired && ok_inc) {
+                        ev = EV_T1A;
+                        wv += sign;
+                    } else if (ts > 0) {
+                        ev = EV_T1B;
+                    } else if (ts < 0 && fired) {
+                        ev = EV_T2;
+                        wv -= sign;
+                        if (!cfg.negative_polarity && wv < 1) wv = 1;  // kernel.cu:603-606
+                    }
+                }
+                evt[bl * nk + kk] = ev;
+            }
+            wk[kk] = wv;
+        }
+        __syncthreads();
+        // 2. compaction in (sample, class) order
+        if (tid < 32) {
+            int n = 0;
+            if (tid < bc)
+                for (int kk = 0; kk < nk; ++kk) n += evt[tid * nk + kk] != EV_NONE;
+            int incl = n;
+            for (int o = 1; o < 32; o <<= 1) {
+                int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                if (tid >= o) incl += v;
+            }
+            int pos = incl - n;
+            if (tid < bc)
+                for (int kk = 0; kk < nk; ++kk) {
+                    uint32_t ev = evt[tid * nk + kk];
+                    if (ev != EV_NONE) list[pos++] = ((uint32_t)tid << 24) | (ev << 22) | (uint32_t)kk;
+                }
+            if (tid == 31) cnt[0] = incl;
+        }
+        __syncthreads();
+        const int nev = cnt[0];
+        // 3. stream the literal words
+        if (nev > 0) {
+            for (int w = tid; w < W; w += nt) {
+                Counter<NB> ctr;
+#pragma unroll
+                for (int i = 0; i < NB; ++i) ctr.p[i] = state[((int64_t)i * C + c) * W + w];
+                const uint32_t vm = valid_mask(w, W, cfg.literals);
+                for (int e = 0; e < nev; ++e) {
+                    const uint32_t ent = list[e];
+                    const int bl = (int)(ent >> 24);
+                    const uint32_t ev = (ent >> 22) & 3u;
+                    const int k = k0 + (int)(ent & 0x3FFFFFu);
+                    const int b = b0 + bl;
+                    const uint64_t t = t0 + (uint64_t)b;
+                    if (ev == EV_T2) {  // type2_fb, kernel.cu:481-506
+                        const uint32_t x = lits[((int64_t)b * P + sel_s[bl]) * W + w];
+                        ctr.inc(~x & vm & ctr.below_top());
+                    } else {
+                        uint32_t cand;
+                        if (ev == EV_T1A) {  // type1a_fb, kernel.cu:410-443
+                            const uint32_t x = lits[((int64_t)b * P + sel_s[bl]) * W + w];
+                            ctr.inc(x & vm & ctr.lt(max_s));
+                            cand = ~x & vm & ctr.ne(zero_s);
+                        } else {  // type1b_fb, kernel.cu:453-470
+                            cand = vm & ctr.ne(zero_s);
+                        }
+                        if (cand) ctr.dec(cand & smask_word(cfg.seed, cfg.s_threshold16, g, t, (uint32_t)k, (uint32_t)w));
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < NB; ++i) state[((int64_t)i * C + c) * W + w] = ctr.p[i];
+            }
+        }
+        __syncthreads();
+    }
+    for (int kk = tid; kk < nk; kk += nt) weights[(int64_t)c * K + k0 + kk] = wk[kk];
+}
+
+static size_t update_smem(int nk) {
+    return (size_t)nk * 4 + UPD_BC * 4 + (UPD_BC + 1) * 4 + (size_t)UPD_BC * nk * 4 + (size_t)UPD_BC * nk + 16;
+}
+
+}  // namespace ytm
+
+using namespace ytm;
+
+extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, int32_t *weights, const int32_t *cs,
+                                       const int32_t *Y, const uint32_t *drop, const uint32_t *lits, int32_t B,
+                                       uint64_t t0, const int32_t *sel_override, void *workspace, void *stream) {
+    ytm_status rc = check_cfg(cfg);
+    if (rc) return rc;
+    if (B <= 0) return fail(YTM_ERR_ARG, "batch must be positive");
+    if (!state || !weights || !cs || !Y || !lits || !workspace) return fail(YTM_ERR_ARG, "null pointer");
+    if (cfg->n_classes >= (1 << 22)) return fail(YTM_ERR_UNSUPPORTED, "too many classes");
+    cudaStream_t st = as_stream(stream);
+    TrainWs l = train_ws_layout(cfg, B);
+    char *ws = (char *)workspace;
+    const int32_t *ninc = (const int32_t *)(ws + l.ninc);
+    const int32_t *sel = sel_override ? sel_override : (const int32_t *)(ws + l.sel);
+    uint64_t *thr = (uint64_t *)(ws + l.thr);
+    {
+        int64_t total = (int64_t)B * cfg->n_classes;
+        unsigned blocks = (unsigned)std::min<int64_t>((int64_t)cdiv(total, 256), (int64_t)sm_count() * 8);
+        k_thresholds<<<blocks, 256, 0, st>>>(cs, Y, B, cfg->n_classes, cfg->T, thr);
+        if ((rc = launch_check("update thresholds"))) return rc;
+    }
+    const int nk = cfg->coalesced ? cfg->n_classes : 1;
+    const size_t smem = update_smem(nk);
+    if (smem > 227 * 1024) return fail(YTM_ERR_UNSUPPORTED, "too many classes for the feedback kernel");
+    const int W = cfg->words;
+    const int tpb = W <= 32 ? 32 : (W <= 64 ? 64 : (W <= 128 ? 128 : 256));
+    YTM_DISPATCH_PLANES(cfg->planes, {
+        if (smem > 48 * 1024) {
+            if ((rc = cuda_check(cudaFuncSetAttribute(k_update<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                      (int)smem), "update smem")))
+                return rc;
+        }
+        k_update<NB><<<cfg->clause_count, tpb, smem, st>>>(*cfg, state, weights, thr, drop, lits, B, t0, sel, ninc);
+    });
+    return launch_check("feedback");
+}
