@@ -22,7 +22,9 @@ OUT = os.path.join(HERE, "_ref")
 DEFAULT_REF = "/root/reference"
 KERNEL_REL = os.path.join("src", "cutm", "cuda", "kernel.cu")
 
-# name -> reference constructor kwargs (BaseTM.__init__, base.py:42-74)
+# name -> reference constructor kwargs (BaseTM.__init__, base.py:42-74).
+# Every shape has LITERALS % 4 == 0: the reference's uint4 loads of TA states
+# (kernel.cu:176, 412, 455, 483) are misaligned otherwise and fault.
 SHAPES = {
     # inference shapes (any hyper-parameters)
     "inf_p1": dict(number_of_clauses_per_class=8, T=50, s=10.0, dim=(28, 28, 1), n_classes=10, coalesced=False),
@@ -31,7 +33,7 @@ SHAPES = {
     "inf_rgb": dict(number_of_clauses_per_class=32, T=100, s=10.0, dim=(12, 12, 6), n_classes=4,
                     patch_dim=(5, 5)),
     "inf_nonsq": dict(number_of_clauses_per_class=24, T=10, s=3.0, dim=(9, 7, 2), n_classes=3,
-                      patch_dim=(4, 3)),
+                      patch_dim=(4, 4)),
     "inf_noloc": dict(number_of_clauses_per_class=16, T=10, s=3.0, dim=(8, 8, 1), n_classes=2,
                       patch_dim=(4, 4), encode_loc=False),
     "inf_noneg": dict(number_of_clauses_per_class=16, T=10, s=3.0, dim=(16, 1, 1), n_classes=2,
@@ -43,7 +45,7 @@ SHAPES = {
                        coalesced=False),
     "tr_coal": dict(number_of_clauses_per_class=24, T=1, s=1.0, dim=(40, 1, 1), n_classes=4, q=3.0),
     "tr_conv": dict(number_of_clauses_per_class=16, T=1, s=1.0, dim=(6, 6, 1), n_classes=3, q=2.0,
-                    patch_dim=(3, 3)),
+                    patch_dim=(4, 4)),
     "tr_maxinc": dict(number_of_clauses_per_class=24, T=1, s=1.0, dim=(40, 1, 1), n_classes=4, q=3.0,
                       max_included_literals=3, negative_polarity=False),
 }
