@@ -186,6 +186,20 @@ ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, int32_t *wei
 ytm_status ytm_train_selection(const ytm_config *cfg, int32_t B, const void *workspace,
                                int32_t *sel, void *stream);
 
+/* Inference without a workspace, for callers that cannot allocate device
+ * memory (code inside a stream capture, embedders whose device memory is
+ * handed out by another runtime).  No counterpart in the reference.
+ * Same inputs and output as ytm_infer; scratch comes from a fixed array of
+ * YTM_NOALLOC_SCRATCH_BYTES that every GPU loading the library keeps until
+ * exit.  Calls needing more scratch (include counts + N * ceil(C/32) words of
+ * fired bits) fail with YTM_ERR_ARG: split N.  The first call on a device
+ * looks up the array's device address and should precede any stream capture.
+ * Calls share the array: calls that overlap on the GPU race. */
+#define YTM_NOALLOC_SCRATCH_BYTES (16u << 20)
+ytm_status ytm_infer_noalloc(const ytm_config *cfg, const uint32_t *state, const int32_t *weights,
+                             const int32_t *bias, const uint32_t *lits, int64_t N, int32_t *cs,
+                             void *stream);
+
 /* Message of the last failing call on this thread ("" if none). */
 const char *ytm_last_error(void);
 

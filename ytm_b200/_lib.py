@@ -19,7 +19,7 @@ EXPORTS = (
     "ytm_config_init", "ytm_config_shard", "ytm_workspace_bytes", "ytm_encode", "ytm_state_init",
     "ytm_state_from_u32", "ytm_state_to_u32", "ytm_include_mask", "ytm_weights_init", "ytm_infer",
     "ytm_transform", "ytm_transform_patchwise", "ytm_train_eval", "ytm_train_update",
-    "ytm_train_selection", "ytm_last_error", "ytm_version",
+    "ytm_train_selection", "ytm_last_error", "ytm_version", "ytm_infer_noalloc",
 )
 
 
@@ -67,6 +67,7 @@ _SIGS = {
     "ytm_train_eval": ([_CFG, _P, _P, _P, _P, _P, _I32, _U64, _I32, _P, _P, _P, _P], ct.c_int),
     "ytm_train_update": ([_CFG, _P, _P, _P, _P, _P, _P, _I32, _U64, _P, _P, _P], ct.c_int),
     "ytm_train_selection": ([_CFG, _I32, _P, _P, _P], ct.c_int),
+    "ytm_infer_noalloc": ([_CFG, _P, _P, _P, _P, _I64, _P, _P], ct.c_int),
     "ytm_last_error": ([], ct.c_char_p),
     "ytm_version": ([], ct.c_char_p),
 }

@@ -329,3 +329,80 @@ ytm_status ytm_train_selection(const ytm_config *cfg, int32_t B, const void *wor
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free inference.
+//
+// Some callers cannot allocate device memory: code running inside a CUDA
+// stream capture, embedders whose memory is carved up in advance by another
+// runtime, or hosts that forbid cudaMalloc after start-up.  ytm_infer_noalloc
+// gives them inference without a workspace argument.  Its scratch (include
+// counts and the fired-clause bitmap) lives in the fixed array below, which
+// every GPU that loads this library holds until the process exits.
+//
+// Host code must not pass `g_noalloc_scratch` itself to a kernel: in host code
+// that name is only a host-side stand-in for the symbol.  The device address is
+// looked up once per device with cudaGetSymbolAddress, with that device
+// current, the first time the entry point runs on it; that first call should
+// therefore come before any stream capture.
+//
+// All calls share the array and it keeps the previous call's contents; the
+// bitmap is cleared on every call.  Calls that overlap on the GPU (different
+// streams, or other threads) race on the array and must be serialised by the
+// caller.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace ytm {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[YTM_NOALLOC_SCRATCH_BYTES];
+
+static std::mutex g_noalloc_mu;
+static void *g_noalloc_ptr[64];
+
+static ytm_status noalloc_scratch(void **out) {
+    int dev = 0;
+    ytm_status rc = cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+    if (rc) return rc;
+    if (dev < 0 || dev >= 64) return fail(YTM_ERR_UNSUPPORTED, "device index above 63");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void *p = nullptr;
+        if ((rc = cuda_check(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress"))) return rc;
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return YTM_OK;
+}
+
+}  // namespace ytm
+
+extern "C" ytm_status ytm_infer_noalloc(const ytm_config *cfg, const uint32_t *state, const int32_t *weights,
+                                        const int32_t *bias, const uint32_t *lits, int64_t N, int32_t *cs,
+                                        void *stream) {
+    ytm_status rc = check_cfg(cfg);
+    if (rc) return rc;
+    if (N < 0) return fail(YTM_ERR_ARG, "N < 0");
+    if (N == 0) return YTM_OK;
+    if (!state || !weights || !lits || !cs) return fail(YTM_ERR_ARG, "null pointer");
+    InferWs l = infer_ws_layout(cfg, N);
+    if (l.total > (uint64_t)YTM_NOALLOC_SCRATCH_BYTES)
+        return fail(YTM_ERR_ARG, "ytm_infer_noalloc: " + std::to_string(l.total) +
+                                     " bytes of scratch needed, the fixed scratch holds " +
+                                     std::to_string((uint64_t)YTM_NOALLOC_SCRATCH_BYTES) +
+                                     "; pass fewer samples per call");
+    void *scratch = nullptr;
+    if ((rc = noalloc_scratch(&scratch))) return rc;
+    cudaStream_t st = as_stream(stream);
+    const int C = cfg->clause_count, W = cfg->words, P = cfg->patches;
+    char *ws = (char *)scratch;
+    int32_t *ninc = (int32_t *)(ws + l.ninc);
+    uint32_t *fired = (uint32_t *)(ws + l.fired);
+    const uint32_t *inc = state + (int64_t)(cfg->planes - 1) * C * W;
+    if ((rc = launch_ninc(cfg, state, ninc, st))) return rc;
+    if ((rc = cuda_check(cudaMemsetAsync(fired, 0, (size_t)N * cdiv(C, 32) * 4, st), "memset"))) return rc;
+    if ((rc = launch_match<MODE_ANY>(inc, lits, N * P, C, W, P, fired, st))) return rc;
+    k_cs_init<<<grid1(N * cfg->n_classes), 256, 0, st>>>(cs, bias, N, cfg->n_classes);
+    if ((rc = launch_check("cs init"))) return rc;
+    return launch_class_sums(fired, ninc, weights, cfg, N, 0, cs, st);
+}
