@@ -133,27 +133,31 @@ def run_reference(args):
     O.set_threads(threads)
     o = O.Oracle(seed=42, **kw)
     b = B
-    X, y = workload(args.workload, b * max(2, args.steps + args.warmup))
+    S = B if B > 1 else 256
+    X, y = workload(args.workload, S * max(2, args.steps + args.warmup))
     lits = o.encode(X)
     Y = O.encode_Y_multiclass(y, kw["n_classes"], kw["T"])
     ta, w, pw = o.init_state(), o.init_weights(), np.zeros((o.C, o.P), np.int32)
     t = 0
+    def step():
+        nonlocal t
+        for _ in range(S // b):
+            s = t % len(lits)
+            o.train_batch(ta, w, pw, lits[s:s + b], Y[s:s + b], t)
+            t += b
     for i in range(args.warmup):
-        o.train_batch(ta, w, pw, lits[t:t + b], Y[t:t + b], t)
-        t += b
+        step()
     t_start = time.perf_counter()
     for i in range(args.steps):
-        s = t % len(lits)
-        o.train_batch(ta, w, pw, lits[s:s + b], Y[s:s + b], t)
-        t += b
+        step()
     el = time.perf_counter() - t_start
-    v = args.steps * b / el
+    v = args.steps * S / el
     out = {"metric": METRIC, "impl": "reference", "value": v, "unit": "samples/s", "n_gpus": args.gpus,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * el / args.steps,
            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u32",
            "data": "synthetic", "config": {"workload": args.workload, "global_batch": b, **_cfgjson(kw)},
            "cpu_baseline": {"value": v, "unit": "samples/s", "cores": O.get_threads(), "kind": "port",
-                            "sample": f"{args.steps} batches of {b} samples of {args.workload}, oracle/ytm_oracle.c "
+                            "sample": f"{args.steps} steps of {S} samples (batch {b}) of {args.workload}, oracle/ytm_oracle.c "
                                       f"(restatement of kernel.cu), OpenMP"},
            "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
@@ -195,7 +199,8 @@ def main():
     name = args.workload
     kw = synthetic.MODELS[name]
     B = synthetic.BATCH[name]
-    n_train = B * (args.steps + args.warmup)
+    S = B if B > 1 else 256  # samples per step (batch-1 workloads: 256 single-sample batches)
+    n_train = S * (args.steps + args.warmup)
     X, y = workload(name, n_train)
     tm = MultiClassTM(seed=42, device=dev, **kw)
     eng = tm.engine
@@ -209,16 +214,17 @@ def main():
         torch.cuda.synchronize()
 
     def step(i, ev=None):
-        lb, yb = lits[i * B:(i + 1) * B], Yd[i * B:(i + 1) * B]
-        t = tm.sample_counter
-        cs = eng.train_eval(lb, t, None, add_bias=rank == 0)
-        cs = tm._allreduce(cs)
-        if ev:
-            ev[0].record()
-        eng.train_update(cs, yb, lb, t, None)
-        if ev:
-            ev[1].record()
-        tm.sample_counter += B
+        for j in range(i * S, (i + 1) * S, B):
+            lb, yb = lits[j:j + B], Yd[j:j + B]
+            t = tm.sample_counter
+            cs = eng.train_eval(lb, t, None, add_bias=rank == 0)
+            cs = tm._allreduce(cs)
+            if ev and j == i * S:
+                ev[0].record()
+            eng.train_update(cs, yb, lb, t, None)
+            if ev and j == i * S:
+                ev[1].record()
+            tm.sample_counter += B
 
     for i in range(args.warmup):
         step(i)
@@ -241,7 +247,7 @@ def main():
         t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
-    value = args.steps * B / (total_ms / 1000.0)
+    value = args.steps * S / (total_ms / 1000.0)
 
     # roofline of the dominant kernel (feedback): the state's read-modify-write
     cfg = eng.cfg
@@ -277,13 +283,13 @@ def main():
     Xh = torch.from_numpy(X.view(np.int32)).pin_memory()
     yh = y
     for i in range(2):
-        tm.fit(Xh[i * B:(i + 1) * B], yh[i * B:(i + 1) * B], batch_size=B)
+        tm.fit(Xh[i * S:(i + 1) * S], yh[i * S:(i + 1) * S], batch_size=B)
     barrier()
     a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for j in range(args.steps):
-        i = (args.warmup + j) % (n_train // B)
-        tm.fit(Xh[i * B:(i + 1) * B], yh[i * B:(i + 1) * B], batch_size=B)
+        i = (args.warmup + j) % (n_train // S)
+        tm.fit(Xh[i * S:(i + 1) * S], yh[i * S:(i + 1) * S], batch_size=B)
         tm.last_class_sums.cpu()
     b_.record()
     barrier()
@@ -292,8 +298,8 @@ def main():
         t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    e2e = {"value": args.steps * B / (e2e_ms / 1000.0), "unit": "samples/s",
-           "h2d_bytes_per_step": int(B * X.shape[1] * 4 + B * kw["n_classes"] * 4),
+    e2e = {"value": args.steps * S / (e2e_ms / 1000.0), "unit": "samples/s",
+           "h2d_bytes_per_step": int(S * X.shape[1] * 4 + S * kw["n_classes"] * 4),
            "d2h_bytes_per_step": int(B * kw["n_classes"] * 4)}
 
     if rank == 0:
@@ -301,10 +307,10 @@ def main():
             "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "u32", "data": "synthetic",
-            "config": {"workload": name, "global_batch": B, "parallelism": f"clause-shard{world}",
+            "config": {"workload": name, "global_batch": B, "samples_per_step": S, "parallelism": f"clause-shard{world}",
                        "l2": "flushed between timed steps (2x L2 write)", **_cfgjson(kw)},
             "e2e": e2e,
-            "gpu_launches": 7 * args.steps,
+            "gpu_launches": 7 * args.steps * (S // B),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": None, "kernel": "k_update (feedback)",
                          "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg_bytes,

@@ -76,8 +76,8 @@ typedef struct ytm_config {
     int32_t planes;            /* bits per counter                              */
     int32_t state_offset;      /* stored value = state + state_offset           */
     int32_t state_top;         /* largest representable state                  */
-    /* decision thresholds (fractions of 2^32 or 2^16) */
-    uint32_t s_threshold16;    /* literal mask Bernoulli(1/s) = thr / 65536     */
+    /* decision thresholds (fractions of 2^32 or 2^12) */
+    uint32_t s_threshold12;    /* literal mask Bernoulli(1/s) = thr / 4096      */
     uint64_t q_threshold;      /* negative-class selection, thr / 2^32          */
     /* clause shard held by this process */
     int32_t clause_lo;         /* first global clause index                     */
@@ -105,6 +105,7 @@ ytm_status ytm_config_shard(ytm_config *cfg, int32_t rank, int32_t world);
 #define YTM_OP_INFER 2
 #define YTM_OP_TRANSFORM 3
 #define YTM_OP_TRAIN 4
+#define YTM_OP_TRAIN_B1 5   /* ytm_train_fit_b1 (n ignored) */
 uint64_t ytm_workspace_bytes(const ytm_config *cfg, int32_t op, int64_t n);
 
 /* Encode raw inputs into per-patch literal words.
@@ -180,6 +181,18 @@ ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, int32_t *wei
                             const int32_t *cs, const int32_t *Y, const uint32_t *drop,
                             const uint32_t *lits, int32_t B, uint64_t t0,
                             const int32_t *sel_override, void *workspace, void *stream);
+
+/* Train on samples 0..N-1 one at a time, in order: the reference's
+ * per-sample loop (_fit, base.py:305-357: pack_clauses, fast_eval,
+ * select_active, clause_update per sample).  Same result as ytm_train_eval +
+ * ytm_train_update with B = 1 for each sample, t = t0 + i, but one fused
+ * launch per sample (feedback of sample i and evaluation of sample i+1) queued
+ * from C++.  Single-patch models only (YTM_ERR_UNSUPPORTED otherwise); one
+ * process (the class sums are not all-reduced).  lits u32 [N][1][W], Y i32
+ * [N][K].  workspace: ytm_workspace_bytes(cfg, YTM_OP_TRAIN_B1, 0). */
+ytm_status ytm_train_fit_b1(const ytm_config *cfg, uint32_t *state, int32_t *weights, const int32_t *bias,
+                            const uint32_t *drop, const uint32_t *lits, const int32_t *Y, int64_t N,
+                            uint64_t t0, int32_t *patch_w, void *workspace, void *stream);
 
 /* Read back the patch picks of the last ytm_train_eval on this workspace:
  * sel i32 [B][C] (-1 = not fired).  Device-to-device copy on `stream`. */

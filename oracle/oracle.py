@@ -49,7 +49,7 @@ class OrcCfg(ct.Structure):
         ("seed", ct.c_uint64),
         ("banks", ct.c_int32), ("C", ct.c_int32), ("L", ct.c_int32), ("W", ct.c_int32), ("P", ct.c_int32),
         ("max_state", ct.c_int32), ("half_state", ct.c_int32), ("state_top", ct.c_int32),
-        ("s_thr16", ct.c_uint32), ("q_thr", ct.c_uint64),
+        ("s_thr12", ct.c_uint32), ("q_thr", ct.c_uint64),
     ]
 
 
@@ -66,6 +66,7 @@ def _declare(L):
     L.orc_set_threads.argtypes = [ct.c_int]
     L.orc_get_threads.restype = ct.c_int
     L.orc_philox4x32_10.argtypes = [_P, _P, _P]
+    L.orc_philox4x32.argtypes = [_P, _P, ct.c_int, _P]
     L.orc_smask_word.argtypes = [ct.POINTER(OrcCfg), ct.c_uint32, _U64, ct.c_uint32, ct.c_uint32]
     L.orc_smask_word.restype = ct.c_uint32
     L.orc_update_threshold.argtypes = [_I32, _I32]
@@ -97,6 +98,14 @@ def philox4x32_10(ctr, key):
     k = _c(key, np.uint32)
     out = np.zeros(4, np.uint32)
     lib().orc_philox4x32_10(_ptr(c), _ptr(k), _ptr(out))
+    return out
+
+
+def philox4x32(ctr, key, rounds):
+    c = _c(ctr, np.uint32)
+    k = _c(key, np.uint32)
+    out = np.zeros(4, np.uint32)
+    lib().orc_philox4x32(_ptr(c), _ptr(k), int(rounds), _ptr(out))
     return out
 
 

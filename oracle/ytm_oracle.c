@@ -43,7 +43,7 @@ typedef struct orc_cfg {
     /* derived, base.py:94-121 */
     int32_t banks, C, L, W, P;
     int32_t max_state, half_state, state_top;
-    uint32_t s_thr16;
+    uint32_t s_thr12;
     uint64_t q_thr;
 } orc_cfg;
 
@@ -86,10 +86,10 @@ int orc_cfg_init(orc_cfg *c, int32_t clauses_per_class, int32_t T, double s, int
         c->state_top = p + c->half_state;
     }
     {
-        double t = floor(65536.0 / s + 0.5);
+        double t = floor(4096.0 / s + 0.5);
         if (!(t > 0.0)) t = 0.0;
-        if (t > 65536.0) t = 65536.0;
-        c->s_thr16 = (uint32_t)t;
+        if (t > 4096.0) t = 4096.0;
+        c->s_thr12 = (uint32_t)t;
     }
     {
         double qp = c->q / (double)(K - 1 > 1 ? K - 1 : 1); /* kernel.cu:32 */
@@ -103,7 +103,7 @@ int orc_cfg_init(orc_cfg *c, int32_t clauses_per_class, int32_t T, double s, int
 
 void orc_cfg_sizes(const orc_cfg *c, int32_t *out) {
     out[0] = c->C; out[1] = c->K; out[2] = c->L; out[3] = c->W; out[4] = c->P;
-    out[5] = c->state_top; out[6] = (int32_t)c->s_thr16; out[7] = c->half_state;
+    out[5] = c->state_top; out[6] = (int32_t)c->s_thr12; out[7] = c->half_state;
 }
 
 void orc_set_threads(int n) {
@@ -124,12 +124,12 @@ int orc_get_threads(void) {
 
 /* --------------------------------------------------------------- Philox */
 
-/* Philox4x32-10 (Salmon et al., SC'11): multipliers 0xD2511F53, 0xCD9E8D57,
+/* Philox4x32-R (Salmon et al., SC'11): multipliers 0xD2511F53, 0xCD9E8D57,
  * Weyl key increments 0x9E3779B9, 0xBB67AE85. */
-void orc_philox4x32_10(const uint32_t ctr_in[4], const uint32_t key_in[2], uint32_t out[4]) {
+void orc_philox4x32(const uint32_t ctr_in[4], const uint32_t key_in[2], int rounds, uint32_t out[4]) {
     uint32_t c0 = ctr_in[0], c1 = ctr_in[1], c2 = ctr_in[2], c3 = ctr_in[3];
     uint32_t k0 = key_in[0], k1 = key_in[1];
-    for (int r = 0; r < 10; ++r) {
+    for (int r = 0; r < rounds; ++r) {
         if (r) { k0 += 0x9E3779B9u; k1 += 0xBB67AE85u; }
         uint64_t p0 = (uint64_t)0xD2511F53u * c0;
         uint64_t p1 = (uint64_t)0xCD9E8D57u * c2;
@@ -141,30 +141,41 @@ void orc_philox4x32_10(const uint32_t ctr_in[4], const uint32_t key_in[2], uint3
     out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
 }
 
+void orc_philox4x32_10(const uint32_t ctr_in[4], const uint32_t key_in[2], uint32_t out[4]) {
+    orc_philox4x32(ctr_in, key_in, 10, out);
+}
+
 /* Decision streams.  counter = (global clause, sample counter low 32 bits,
  * sub-index, tag | class << 2); key = (seed low, seed high ^ sample high). */
 enum { TAG_PATCH = 0, TAG_CLASS = 1, TAG_SMASK = 2, TAG_INIT = 3 };
 
-static inline void draw(const orc_cfg *c, uint32_t clause, uint64_t t, uint32_t sub, uint32_t tag,
-                        uint32_t k, uint32_t out[4]) {
+static inline void draw_r(const orc_cfg *c, uint32_t clause, uint64_t t, uint32_t sub, uint32_t tag,
+                          uint32_t k, int rounds, uint32_t out[4]) {
     uint32_t ctr[4] = {clause, (uint32_t)t, sub, tag | (k << 2)};
     uint32_t key[2] = {(uint32_t)c->seed, (uint32_t)(c->seed >> 32) ^ (uint32_t)(t >> 32)};
-    orc_philox4x32_10(ctr, key, out);
+    orc_philox4x32(ctr, key, rounds, out);
 }
 
-/* Bernoulli(s_thr16 / 65536) for the 32 literals of word w: literal j is set
- * iff the 16-bit number whose bit 15-i is bit j of random word i is below the
- * threshold.  Stands in for `curand_uniform(rng) <= S_INV` (kernel.cu:425-428,
- * 439, 457-460, 466). */
+/* Decision draws use Philox4x32-10; the bulk literal-mask draws use the
+ * 7-round variant, which Salmon et al. report as passing BigCrush. */
+static inline void draw(const orc_cfg *c, uint32_t clause, uint64_t t, uint32_t sub, uint32_t tag,
+                        uint32_t k, uint32_t out[4]) {
+    draw_r(c, clause, t, sub, tag, k, 10, out);
+}
+
+/* Bernoulli(s_thr12 / 4096) for the 32 literals of word w: literal j is set
+ * iff the 12-bit number whose bit 11-i is bit j of random word i is below the
+ * threshold (three Philox4x32-7 draws give the 12 random words).  Stands in
+ * for `curand_uniform(rng) <= S_INV` (kernel.cu:425-428, 439, 457-460, 466). */
 uint32_t orc_smask_word(const orc_cfg *c, uint32_t clause, uint64_t t, uint32_t k, uint32_t w) {
-    uint32_t thr = c->s_thr16;
-    if (thr >= 65536u) return 0xFFFFFFFFu;
+    uint32_t thr = c->s_thr12;
+    if (thr >= 4096u) return 0xFFFFFFFFu;
     if (thr == 0u) return 0u;
-    uint32_t R[16];
-    for (uint32_t j = 0; j < 4; ++j) draw(c, clause, t, w * 4u + j, TAG_SMASK, k, &R[4 * j]);
+    uint32_t R[12];
+    for (uint32_t j = 0; j < 3; ++j) draw_r(c, clause, t, w * 4u + j, TAG_SMASK, k, 7, &R[4 * j]);
     uint32_t lt = 0u, eq = 0xFFFFFFFFu;
-    for (int i = 0; i < 16; ++i) {
-        if ((thr >> (15 - i)) & 1u) {
+    for (int i = 0; i < 12; ++i) {
+        if ((thr >> (11 - i)) & 1u) {
             lt |= eq & ~R[i];
             eq &= R[i];
         } else {

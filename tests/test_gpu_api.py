@@ -1,0 +1,127 @@
+"""GPU tests of the reference-facing API (ytm_b200.cutm mirrors
+src/cutm/{multiclass,multioutput,base}.py): fit/predict/score, encode,
+transforms, getters, state dict and pickle, against the oracle."""
+import io
+import lzma
+import pickle
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from ytm_b200 import synthetic
+from ytm_b200.cutm import MultiClassTM, MultiOutputTM
+
+pytestmark = pytest.mark.gpu
+
+KW = dict(number_of_clauses_per_class=40, T=20, s=4.0, dim=(8, 8, 1), n_classes=3, patch_dim=(5, 5), seed=3)
+
+
+def data(n=60, seed=0):
+    rng = np.random.default_rng(seed)
+    return (rng.random((n, 64)) < 0.35).astype(np.uint32), rng.integers(0, 3, n).astype(np.uint32)
+
+
+@pytest.mark.parametrize("bs", [1, 8])
+def test_multiclass_fit_predict_matches_oracle(bs):
+    X, y = data()
+    tm = MultiClassTM(**KW)
+    assert (tm.number_of_clauses, tm.number_of_patches) == (40, 16)
+    enc = tm.encode(X)
+    tm.fit(enc, y, is_X_encoded=True, batch_size=bs, block_size=16)
+    tm.fit(X, y, batch_size=bs)  # raw inputs, encoded on the device
+    o = O.Oracle(**KW)
+    lits = o.encode(X)
+    np.testing.assert_array_equal(enc, lits)
+    Y = O.encode_Y_multiclass(y, 3, KW["T"])
+    ta, w, pw = o.init_state(), o.init_weights(), np.zeros((o.C, o.P), np.int32)
+    t = o.fit(ta, w, pw, lits, Y, 0, batch_size=bs)
+    o.fit(ta, w, pw, lits, Y, t, batch_size=bs)
+    np.testing.assert_array_equal(tm.get_ta_state(), ta)
+    np.testing.assert_array_equal(tm.get_weights(), w.astype(np.float32))
+    np.testing.assert_array_equal(tm.get_patch_weights(), pw)
+    np.testing.assert_array_equal(tm.get_literals(), (ta > 128).astype(np.uint32))
+    preds, cs = tm.predict(X)
+    assert cs.dtype == np.float32 and preds.shape == (60,)
+    np.testing.assert_array_equal(cs, o.infer(ta, w, lits).astype(np.float32))
+    np.testing.assert_array_equal(preds, np.argmax(cs, axis=1))
+    np.testing.assert_array_equal(tm.transform(X), o.transform(ta, lits))
+    np.testing.assert_array_equal(tm.transform_patchwise(enc, is_X_encoded=True), o.transform_patchwise(ta, lits))
+
+
+def test_non_coalesced_getter_shapes():
+    tm = MultiClassTM(number_of_clauses_per_class=10, T=5, s=3.0, dim=(16, 1, 1), n_classes=4, coalesced=False,
+                      seed=1)
+    assert tm.get_ta_state().shape == (4, 10, 32)
+    assert tm.get_weights().shape == (4, 10, 4)
+    assert tm.get_patch_weights().shape == (4, 10, 1)
+    assert tm.get_bias_weights().shape == (4,)
+
+
+def test_multioutput_matches_oracle():
+    rng = np.random.default_rng(2)
+    X = (rng.random((40, 64)) < 0.35).astype(np.uint32)
+    Ym = (rng.random((40, 3)) < 0.4).astype(np.uint32)
+    tm = MultiOutputTM(**KW)
+    tm.fit(X, Ym, batch_size=4)
+    o = O.Oracle(**KW)
+    lits = o.encode(X)
+    ta, w, pw = o.init_state(), o.init_weights(), np.zeros((o.C, o.P), np.int32)
+    o.fit(ta, w, pw, lits, O.encode_Y_multioutput(Ym, KW["T"]), 0, batch_size=4)
+    np.testing.assert_array_equal(tm.get_ta_state(), ta)
+    preds, cs = tm.predict(X)
+    np.testing.assert_array_equal(cs, o.infer(ta, w, lits).astype(np.float32))
+    np.testing.assert_array_equal(preds, (cs >= 0).astype(np.uint32))
+
+
+def test_pickle_lzma_roundtrip_and_continue():
+    """Scripts save models with pickle + LZMAFile (pneumonia_mnist.py:119-120)."""
+    X, y = data()
+    tm = MultiClassTM(**KW)
+    tm.fit(X[:30], y[:30], batch_size=2)
+    buf = io.BytesIO()
+    with lzma.LZMAFile(buf, "wb") as f:
+        pickle.dump(tm, f)
+    buf.seek(0)
+    with lzma.LZMAFile(buf, "rb") as f:
+        tm2 = pickle.load(f)
+    np.testing.assert_array_equal(tm2.get_ta_state(), tm.get_ta_state())
+    np.testing.assert_array_equal(tm2.predict(X)[1], tm.predict(X)[1])
+    tm.fit(X[30:], y[30:], batch_size=2)
+    tm2.fit(X[30:], y[30:], batch_size=2)  # the sample counter travels: same decisions
+    np.testing.assert_array_equal(tm2.get_ta_state(), tm.get_ta_state())
+
+
+def test_state_dict_in_reference_layout():
+    tm = MultiClassTM(**KW)
+    sd = tm.get_state_dict()
+    assert sd["ta_state"].dtype == np.uint32 and sd["ta_state"].shape == (40 * tm.number_of_literals,)
+    assert sd["clause_weights"].dtype == np.float32 and sd["patch_weights"].dtype == np.int32
+    rng = np.random.default_rng(0)
+    sd["ta_state"] = rng.integers(0, 257, sd["ta_state"].shape).astype(np.uint32)
+    tm.load_state_dict({"state": sd})
+    np.testing.assert_array_equal(tm.get_state_dict()["ta_state"], sd["ta_state"])
+    sd["ta_state"][0] = 10_000
+    with pytest.raises(ValueError):
+        tm.load_state_dict({"state": sd})
+
+
+def test_learns_config1_like_data():
+    """Vanilla TM on prototype data (config 1 distribution, fewer clauses):
+    one epoch at batch 1 gives high test accuracy."""
+    X, y = synthetic.prototypes(3000, seed=11)
+    tm = MultiClassTM(number_of_clauses_per_class=100, T=50, s=10.0, dim=(28, 28, 1), n_classes=10,
+                      coalesced=False, seed=5)
+    tm.fit(X[:2000], y[:2000])
+    acc = (tm.predict(X[2000:])[0] == y[2000:]).mean()
+    assert acc > 0.9, acc
+
+
+def test_bad_inputs_raise():
+    tm = MultiClassTM(**KW)
+    with pytest.raises(AssertionError):
+        tm.encode(np.zeros((3, 64), np.int64))
+    with pytest.raises(AssertionError):
+        tm.fit(np.zeros((3, 64), np.uint32), np.zeros((3, 2), np.uint32))
+    with pytest.raises(NotImplementedError):
+        MultiClassTM(bias=True, **KW)

@@ -205,3 +205,31 @@ def test_infer_equals_transform_times_weights_config1_size():
     W = host(e.weights).astype(np.int64)
     np.testing.assert_array_equal(cs, (out * nonempty[None, :]) @ W)
     assert 0 < out.mean() < 1
+
+
+@pytest.mark.parametrize("case", ["vanilla", "coalesced_b1", "states4096", "states16", "maxinc_nopol",
+                                  "many_classes", "drop"])
+def test_fused_batch1_matches_oracle(case):
+    """ytm_train_fit_b1 (one fused launch per sample) == the oracle's
+    per-sample loop."""
+    kw, _ = TRAIN_CASES["coalesced_b1" if case == "drop" else case]
+    seed = 4321
+    o = O.Oracle(**oracle_kwargs(kw, seed))
+    e = engine_for(kw, seed)
+    rng = np.random.default_rng(8)
+    N = 40
+    D = kw["dim"][0] * kw["dim"][1] * kw["dim"][2]
+    X = (rng.random((N, D)) < 0.35).astype(np.uint32)
+    Y = O.encode_Y_multiclass(rng.integers(0, kw["n_classes"], N), kw["n_classes"], kw["T"])
+    lits_h = o.encode(X)
+    lits = dev(lits_h)
+    drop_h = (rng.random(o.C) < 0.15).astype(np.uint32) if case == "drop" else None
+    ta, w, pw = o.init_state(), o.init_weights(), np.zeros((o.C, o.P), np.int32)
+    t = 0
+    for ep in range(3):
+        t = o.fit(ta, w, pw, lits_h, Y, t, batch_size=1, drop=drop_h)
+        e.train_fit_b1(lits, dev(Y, np.int32), ep * N, None if drop_h is None else dev(drop_h))
+        np.testing.assert_array_equal(e.get_ta_state(), ta, err_msg=f"epoch {ep}")
+        np.testing.assert_array_equal(host(e.weights), w)
+        np.testing.assert_array_equal(host(e.patch_w), pw)
+    assert not np.array_equal(ta, o.init_state())

@@ -92,11 +92,11 @@ def test_batch_of_one_equals_per_sample_loop():
 
 
 def test_smask_rate():
-    """The literal mask is Bernoulli(round(65536/s)/65536)."""
+    """The literal mask is Bernoulli(round(4096/s)/4096)."""
     o = O.Oracle(number_of_clauses_per_class=4, T=10, s=10.0, dim=(4, 1, 1), n_classes=2, seed=9)
     ones = sum(bin(o.smask_word(c, t, 0, 0)).count("1") for c in range(4) for t in range(500))
     rate = ones / (4 * 500 * 32)
-    assert abs(rate - 6554 / 65536) < 0.01
+    assert abs(rate - 410 / 4096) < 0.01
 
 
 def test_oracle_threads():

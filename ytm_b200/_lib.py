@@ -12,7 +12,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libytm.so")
 
 YTM_OK = 0
-YTM_OP_ENCODE, YTM_OP_INFER, YTM_OP_TRANSFORM, YTM_OP_TRAIN = 1, 2, 3, 4
+YTM_OP_ENCODE, YTM_OP_INFER, YTM_OP_TRANSFORM, YTM_OP_TRAIN, YTM_OP_TRAIN_B1 = 1, 2, 3, 4, 5
 
 # Every function include/ytm.h declares; tests check the library exports them.
 EXPORTS = (
@@ -20,6 +20,7 @@ EXPORTS = (
     "ytm_state_from_u32", "ytm_state_to_u32", "ytm_include_mask", "ytm_weights_init", "ytm_infer",
     "ytm_transform", "ytm_transform_patchwise", "ytm_train_eval", "ytm_train_update",
     "ytm_train_selection", "ytm_last_error", "ytm_version", "ytm_infer_noalloc",
+    "ytm_train_fit_b1",
 )
 
 
@@ -41,7 +42,7 @@ class Config(ct.Structure):
         ("loc_literals", ct.c_int32),
         ("max_state", ct.c_int32), ("half_state", ct.c_int32), ("planes", ct.c_int32),
         ("state_offset", ct.c_int32), ("state_top", ct.c_int32),
-        ("s_threshold16", ct.c_uint32), ("q_threshold", ct.c_uint64),
+        ("s_threshold12", ct.c_uint32), ("q_threshold", ct.c_uint64),
         ("clause_lo", ct.c_int32), ("clause_count", ct.c_int32),
     ]
 
@@ -67,6 +68,7 @@ _SIGS = {
     "ytm_train_eval": ([_CFG, _P, _P, _P, _P, _P, _I32, _U64, _I32, _P, _P, _P, _P], ct.c_int),
     "ytm_train_update": ([_CFG, _P, _P, _P, _P, _P, _P, _I32, _U64, _P, _P, _P], ct.c_int),
     "ytm_train_selection": ([_CFG, _I32, _P, _P, _P], ct.c_int),
+    "ytm_train_fit_b1": ([_CFG, _P, _P, _P, _P, _P, _P, _I64, _U64, _P, _P, _P], ct.c_int),
     "ytm_infer_noalloc": ([_CFG, _P, _P, _P, _P, _I64, _P, _P], ct.c_int),
     "ytm_last_error": ([], ct.c_char_p),
     "ytm_version": ([], ct.c_char_p),

@@ -133,10 +133,10 @@ ytm_status ytm_config_init(ytm_config *cfg, int32_t clauses_per_class, int32_t T
         if (nb > 16) return fail(YTM_ERR_UNSUPPORTED, "number_of_ta_states needs more than 16 bit planes");
     }
     {
-        double t = floor(65536.0 / s + 0.5);
+        double t = floor(4096.0 / s + 0.5);
         if (!(t > 0.0)) t = 0.0;
-        if (t > 65536.0) t = 65536.0;
-        cfg->s_threshold16 = (uint32_t)t;
+        if (t > 4096.0) t = 4096.0;
+        cfg->s_threshold12 = (uint32_t)t;
     }
     {
         double qp = cfg->q / (double)(n_classes - 1 > 1 ? n_classes - 1 : 1);  // kernel.cu:32
@@ -171,6 +171,8 @@ uint64_t ytm_workspace_bytes(const ytm_config *cfg, int32_t op, int64_t n) {
             return infer_ws_layout(cfg, n).total;
         case YTM_OP_TRAIN:
             return train_ws_layout(cfg, n).total;
+        case YTM_OP_TRAIN_B1:
+            return b1_ws_layout(cfg).total;
         default:
             return 0;
     }

@@ -35,10 +35,11 @@ struct u32x4 {
     uint32_t x, y, z, w;
 };
 
-__device__ __forceinline__ u32x4 philox10(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t k0,
-                                          uint32_t k1) {
+template <int R>
+__device__ __forceinline__ u32x4 philox(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t k0,
+                                        uint32_t k1) {
 #pragma unroll
-    for (int r = 0; r < 10; ++r) {
+    for (int r = 0; r < R; ++r) {
         if (r) {
             k0 += 0x9E3779B9u;
             k1 += 0xBB67AE85u;
@@ -59,28 +60,32 @@ __device__ __forceinline__ u32x4 philox10(uint32_t c0, uint32_t c1, uint32_t c2,
 // sub-index, tag | class << 2); key = (seed low, seed high ^ sample high).
 enum : uint32_t { TAG_PATCH = 0, TAG_CLASS = 1, TAG_SMASK = 2, TAG_INIT = 3 };
 
+// Decision draws use Philox4x32-10; the bulk literal-mask draws use the
+// 7-round variant, which Salmon et al. report as passing BigCrush.
+template <int R = 10>
 __device__ __forceinline__ u32x4 draw(uint64_t seed, uint32_t clause, uint64_t t, uint32_t sub, uint32_t tag,
                                       uint32_t k) {
-    return philox10(clause, (uint32_t)t, sub, tag | (k << 2), (uint32_t)seed,
-                    (uint32_t)(seed >> 32) ^ (uint32_t)(t >> 32));
+    return philox<R>(clause, (uint32_t)t, sub, tag | (k << 2), (uint32_t)seed,
+                     (uint32_t)(seed >> 32) ^ (uint32_t)(t >> 32));
 }
 
-// Bernoulli(thr/65536) bits for the 32 literals of word w of clause g in the
-// feedback for class k of sample t: literal j is set iff the 16-bit number
-// whose bit 15-i is bit j of random word i is below thr.  (Stands in for the
-// reference's per-literal `curand_uniform(rng) <= S_INV`.)
+// Bernoulli(thr/4096) bits for the 32 literals of word w of clause g in the
+// feedback for class k of sample t: literal j is set iff the 12-bit number
+// whose bit 11-i is bit j of random word i is below thr; three Philox4x32-7
+// draws give the 12 words.  (Stands in for the reference's per-literal
+// `curand_uniform(rng) <= S_INV`.)
 __device__ __forceinline__ uint32_t smask_word(uint64_t seed, uint32_t thr, uint32_t g, uint64_t t, uint32_t k,
                                                uint32_t w) {
-    if (thr >= 65536u) return 0xFFFFFFFFu;
+    if (thr >= 4096u) return 0xFFFFFFFFu;
     if (thr == 0u) return 0u;
     uint32_t lt = 0u, eq = 0xFFFFFFFFu;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        u32x4 r = draw(seed, g, t, w * 4u + (uint32_t)j, TAG_SMASK, k);
+    for (int j = 0; j < 3; ++j) {
+        u32x4 r = draw<7>(seed, g, t, w * 4u + (uint32_t)j, TAG_SMASK, k);
         uint32_t R[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            int bit = 15 - (4 * j + i);
+            int bit = 11 - (4 * j + i);
             if ((thr >> bit) & 1u) {
                 lt |= eq & ~R[i];
                 eq &= R[i];
@@ -196,6 +201,10 @@ struct InferWs {
     uint64_t ninc, fired, total;
 };
 InferWs infer_ws_layout(const ytm_config *cfg, int64_t N);
+struct B1Ws {
+    uint64_t cs, fired, ninc, total;
+};
+B1Ws b1_ws_layout(const ytm_config *cfg);
 
 // Shared launchers (eval.cu) used by several entry points.
 ytm_status launch_ninc(const ytm_config *cfg, const uint32_t *state, int32_t *ninc, cudaStream_t st);

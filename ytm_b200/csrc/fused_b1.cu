@@ -1,0 +1,275 @@
+// fused_b1.cu — the reference's per-sample training loop (base.py:305-357),
+// one kernel launch per sample, issued from C++ (no host round trip).
+//
+// The reference runs 4 kernels and 4 host syncs per sample.  Here launch i
+// does, for every clause (one warp each):
+//   1. the feedback of sample i (clause_update, kernel.cu:531-613) with the
+//      class sums and picks that launch i-1 produced, and
+//   2. the evaluation of sample i+1 on the just-updated state (fast_eval +
+//      select_active, kernel.cu:255-316): include count, fired bit, patch
+//      weight, and the clause's weight row added to the class sums of i+1,
+// so the bit planes are read and written once per sample.  Launch boundaries
+// are the grid-wide barrier between "all class sums of i+1 are complete" and
+// "feedback of i+1 starts".  A prologue launch evaluates the first sample.
+//
+// Class sums live in a ring of three [K] slots: launch i reads slot i%3,
+// accumulates slot (i+1)%3 and clears slot (i+2)%3, which launch i-1 finished
+// reading and launch i+1 will fill.  Results are bit-identical to
+// ytm_train_eval + ytm_train_update with B = 1 (single patch models).
+#include "common.cuh"
+
+namespace ytm {
+
+#ifndef YTM_FB_CPB
+#define YTM_FB_CPB 64
+#endif
+constexpr int FB_WARPS = 8, FB_CPB = YTM_FB_CPB;  // warps and clauses per block
+
+
+B1Ws b1_ws_layout(const ytm_config *cfg) {
+    B1Ws l;
+    const uint64_t C = cfg->clause_count, K = cfg->n_classes;
+    uint64_t o = 0;
+    l.cs = o;    o = align_up(o + 3 * K * 4, 256);
+    l.fired = o; o = align_up(o + 2 * C, 256);
+    l.ninc = o;  o = align_up(o + C * 4, 256);
+    l.total = o;
+    return l;
+}
+
+// Block = 8 warps owning FB_CPB consecutive clauses.  Thresholds of sample i
+// are computed once per block; decisions run one clause per thread (the
+// Philox class draws of 32 clauses share each warp instruction); then each
+// warp streams the words of its clauses (8 per warp), applying the events and
+// evaluating sample i+1.
+template <int NB>
+__global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
+    ytm_config cfg, uint32_t *__restrict__ state, int32_t *__restrict__ weights, const int32_t *__restrict__ bias,
+    const uint32_t *__restrict__ drop, const uint32_t *__restrict__ lits, const int32_t *__restrict__ Y, int64_t i,
+    int64_t N, uint64_t t0, int do_update, int32_t *__restrict__ cs_ring, uint8_t *__restrict__ fired_pp,
+    int32_t *__restrict__ ninc_ws, int32_t *__restrict__ patch_w) {
+    extern __shared__ __align__(16) unsigned char smraw[];
+    const int C = cfg.clause_count, W = cfg.words, K = cfg.n_classes, L = cfg.literals;
+    const int nk = cfg.coalesced ? K : 1;
+    const int KB = (nk + 31) >> 5;                       // 32-class chunks per clause
+    uint64_t *thr_s = (uint64_t *)smraw;                 // [K]  threshold | target bit
+    int32_t *cs_blk = (int32_t *)(thr_s + K);            // [K]
+    uint32_t *ev_s = (uint32_t *)(cs_blk + K);           // [FB_CPB][KB][3]: any, type Ia, type II
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int do_eval = (i + 1 < N) || !do_update;       // the prologue evaluates sample 0
+    const int64_t e_next = do_update ? i + 1 : 0;        // sample evaluated by this launch
+    const int32_t *cs_cur = cs_ring + (i % 3) * K;
+    int32_t *cs_next = cs_ring + (e_next % 3) * K;
+    const uint8_t *fired_cur = fired_pp + (i & 1) * (int64_t)C;
+    uint8_t *fired_next = fired_pp + (e_next & 1) * (int64_t)C;
+    const uint64_t t = t0 + (uint64_t)i;
+    const int cbase = blockIdx.x * FB_CPB;
+
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        cs_blk[k] = 0;
+        if (do_update) {
+            int32_t v = cs_cur[k] + (bias ? bias[k] : 0);
+            v = v > cfg.T ? cfg.T : (v < -cfg.T ? -cfg.T : v);  // clip_cs, kernel.cu:397
+            const int32_t y = Y[i * K + k];
+            uint64_t th = update_threshold(y, v);
+            if (v > y) th |= 1ull << 63;                          // target -1, kernel.cu:571
+            thr_s[k] = th;
+        }
+    }
+    if (blockIdx.x == 0 && do_update)
+        for (int k = threadIdx.x; k < K; k += blockDim.x) cs_ring[((i + 2) % 3) * K + k] = 0;
+    __syncthreads();
+
+    // ---- 1. decisions of sample i: one clause per thread
+    if (do_update && threadIdx.x < FB_CPB) {
+        const int c = cbase + threadIdx.x;
+        uint32_t *ev = ev_s + threadIdx.x * KB * 3;
+        for (int q = 0; q < KB * 3; ++q) ev[q] = 0u;
+        if (c < C && !(drop && drop[c] == 1u)) {  // kernel.cu:555
+            const uint32_t g = (uint32_t)(cfg.clause_lo + c);
+            const int k0 = cfg.coalesced ? 0 : (int)(g / (uint32_t)cfg.clauses_per_class);
+            const bool fired = fired_cur[c] != 0;
+            const bool ok_inc = ninc_ws[c] <= cfg.max_included_literals;
+            for (int kk = 0; kk < nk; ++kk) {
+                const int k = k0 + kk;
+                uint64_t th = thr_s[k];
+                const int target = (th >> 63) ? -1 : 1;
+                th &= ~(1ull << 63);
+                u32x4 r = draw(cfg.seed, g, t, 0, TAG_CLASS, (uint32_t)k);
+                if (target == -1 && !((uint64_t)r.x < cfg.q_threshold)) continue;  // kernel.cu:573
+                if (!((uint64_t)r.y < th)) continue;                                // kernel.cu:582
+                int32_t *lw = &weights[(int64_t)c * K + k];
+                int32_t wv = *lw;
+                const int sign = (wv >= 0) - (wv < 0);
+                const int ts = target * sign;
+                const uint32_t bit = 1u << (kk & 31);
+                uint32_t *e3 = ev + (kk >> 5) * 3;
+                if (ts > 0 && fired && ok_inc) {
+                    e3[0] |= bit;
+                    e3[1] |= bit;
+                    *lw = wv + sign;
+                } else if (ts > 0) {
+                    e3[0] |= bit;
+                } else if (ts < 0 && fired) {
+                    e3[0] |= bit;
+                    e3[2] |= bit;
+                    wv -= sign;
+                    if (!cfg.negative_polarity && wv < 1) wv = 1;  // kernel.cu:603-606
+                    *lw = wv;
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- 2. per clause: feedback over the words, then evaluation of sample i+1
+    const uint32_t max_s = (uint32_t)(cfg.max_state + cfg.state_offset);
+    const uint32_t zero_s = (uint32_t)cfg.state_offset;
+    const uint32_t *x_cur = lits + i * W;
+    const uint32_t *x_next = lits + e_next * W;
+    constexpr int CPW = FB_CPB / FB_WARPS;  // clauses per warp
+    bool has_ev[CPW];
+#pragma unroll
+    for (int q = 0; q < CPW; ++q) {
+        const int j = wib + q * FB_WARPS;
+        bool a = false;
+        if (do_update)
+            for (int kb = 0; kb < KB; ++kb) a |= ev_s[(j * KB + kb) * 3] != 0u;
+        has_ev[q] = a;
+    }
+    // 2a. clauses without events: only the evaluation of sample i+1, with the
+    //     loads of all of this warp's clauses in flight together
+    uint32_t viol[CPW];
+    int cnt[CPW];
+#pragma unroll
+    for (int q = 0; q < CPW; ++q) { viol[q] = 0u; cnt[q] = 0; }
+    if (do_eval) {
+        for (int w = lane; w < W; w += 32) {
+            const uint32_t xn = x_next[w];
+#pragma unroll
+            for (int q = 0; q < CPW; ++q) {
+                const int c = cbase + wib + q * FB_WARPS;
+                if (!has_ev[q] && c < C) {
+                    const uint32_t top = state[((int64_t)(NB - 1) * C + c) * W + w];
+                    viol[q] |= top & ~xn;
+                    cnt[q] += __popc(top);
+                }
+            }
+        }
+    }
+    // 2b. clauses with events: feedback of sample i, then the evaluation
+#pragma unroll 1
+    for (int q = 0; q < CPW; ++q) {
+        if (!has_ev[q]) continue;
+        const int j = wib + q * FB_WARPS;
+        const int c = cbase + j;
+        const uint32_t g = (uint32_t)(cfg.clause_lo + c);
+        const int k0 = cfg.coalesced ? 0 : (int)(g / (uint32_t)cfg.clauses_per_class);
+        const uint32_t *ev = ev_s + j * KB * 3;
+        const bool fired_cur_b = fired_cur[c] != 0;
+        uint32_t vq = 0u;
+        int cq = 0;
+        for (int w = lane; w < W; w += 32) {
+            const uint32_t vm = valid_mask(w, W, L);
+            Counter<NB> ctr;
+#pragma unroll
+            for (int b = 0; b < NB; ++b) ctr.p[b] = state[((int64_t)b * C + c) * W + w];
+            const uint32_t x = fired_cur_b ? x_cur[w] : 0u;
+            for (int kb = 0; kb < KB; ++kb) {
+                uint32_t m = ev[kb * 3];
+                const uint32_t m1a = ev[kb * 3 + 1], m2 = ev[kb * 3 + 2];
+                while (m) {
+                    const int b = __ffs(m) - 1;
+                    m &= m - 1u;
+                    if ((m2 >> b) & 1u) {  // type2_fb, kernel.cu:481-506
+                        ctr.inc(~x & vm & ctr.below_top());
+                    } else {
+                        uint32_t cand;
+                        if ((m1a >> b) & 1u) {  // type1a_fb, kernel.cu:410-443
+                            ctr.inc(x & vm & ctr.lt(max_s));
+                            cand = ~x & vm & ctr.ne(zero_s);
+                        } else {  // type1b_fb, kernel.cu:453-470
+                            cand = vm & ctr.ne(zero_s);
+                        }
+                        if (cand)
+                            ctr.dec(cand & smask_word(cfg.seed, cfg.s_threshold12, g, t,
+                                                      (uint32_t)(k0 + kb * 32 + b), (uint32_t)w));
+                    }
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < NB; ++b) state[((int64_t)b * C + c) * W + w] = ctr.p[b];
+            if (do_eval) {
+                vq |= ctr.p[NB - 1] & ~x_next[w];
+                cq += __popc(ctr.p[NB - 1]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < CPW; ++r)
+            if (r == q) { viol[r] = vq; cnt[r] = cq; }
+    }
+    // 2c. fired bits, include counts, patch weights and class sums of i+1
+    if (do_eval) {
+#pragma unroll
+        for (int q = 0; q < CPW; ++q) {
+            const int c = cbase + wib + q * FB_WARPS;
+            if (c >= C) break;
+            const uint32_t vr = __reduce_or_sync(0xFFFFFFFFu, viol[q]);
+            const int cr = __reduce_add_sync(0xFFFFFFFFu, cnt[q]);
+            const uint32_t g = (uint32_t)(cfg.clause_lo + c);
+            const int k0 = cfg.coalesced ? 0 : (int)(g / (uint32_t)cfg.clauses_per_class);
+            // an empty clause matches (kernel.cu:273-276); a dropped one never fires
+            const bool f = !(drop && drop[c] == 1u) && vr == 0u;
+            if (lane == 0) {
+                ninc_ws[c] = cr;
+                fired_next[c] = f ? 1 : 0;
+                if (f) patch_w[(int64_t)c * cfg.patches] += 1;  // kernel.cu:305
+            }
+            if (f)
+                for (int kk = lane; kk < nk; kk += 32)
+                    atomicAdd(&cs_blk[k0 + kk], weights[(int64_t)c * K + k0 + kk]);
+        }
+    }
+    __syncthreads();
+    if (do_eval)
+        for (int k = threadIdx.x; k < K; k += blockDim.x)
+            if (cs_blk[k]) atomicAdd(&cs_next[k], cs_blk[k]);
+}
+
+}  // namespace ytm
+
+using namespace ytm;
+
+extern "C" ytm_status ytm_train_fit_b1(const ytm_config *cfg, uint32_t *state, int32_t *weights, const int32_t *bias,
+                                       const uint32_t *drop, const uint32_t *lits, const int32_t *Y, int64_t N,
+                                       uint64_t t0, int32_t *patch_w, void *workspace, void *stream) {
+    ytm_status rc = check_cfg(cfg);
+    if (rc) return rc;
+    if (cfg->patches != 1) return fail(YTM_ERR_UNSUPPORTED, "ytm_train_fit_b1 handles single-patch models");
+    if (N < 0) return fail(YTM_ERR_ARG, "N < 0");
+    if (N == 0) return YTM_OK;
+    if (!state || !weights || !lits || !Y || !patch_w || !workspace) return fail(YTM_ERR_ARG, "null pointer");
+    if (cfg->coalesced && cfg->n_classes > 256)
+        return fail(YTM_ERR_UNSUPPORTED, "ytm_train_fit_b1 handles at most 256 classes");
+    cudaStream_t st = as_stream(stream);
+    B1Ws l = b1_ws_layout(cfg);
+    char *ws = (char *)workspace;
+    int32_t *cs_ring = (int32_t *)(ws + l.cs);
+    uint8_t *fired = (uint8_t *)(ws + l.fired);
+    int32_t *ninc = (int32_t *)(ws + l.ninc);
+    if ((rc = cuda_check(cudaMemsetAsync(cs_ring, 0, 3 * (size_t)cfg->n_classes * 4, st), "memset"))) return rc;
+    const int C = cfg->clause_count;
+    const int blocks = (int)cdiv(C, FB_CPB);
+    const int nk = cfg->coalesced ? cfg->n_classes : 1;
+    const size_t smem = (size_t)cfg->n_classes * 12 + (size_t)FB_CPB * ((nk + 31) / 32) * 12 + 16;
+    YTM_DISPATCH_PLANES(cfg->planes, {
+        k_fused_b1<NB><<<blocks, FB_WARPS * 32, smem, st>>>(*cfg, state, weights, bias, drop, lits, Y, 0, N, t0, 0,
+                                                           cs_ring, fired, ninc, patch_w);
+        if ((rc = launch_check("fused b1 prologue"))) return rc;
+        for (int64_t i = 0; i < N; ++i) {
+            k_fused_b1<NB><<<blocks, FB_WARPS * 32, smem, st>>>(*cfg, state, weights, bias, drop, lits, Y, i, N, t0,
+                                                               1, cs_ring, fired, ninc, patch_w);
+        }
+    });
+    return launch_check("fused b1");
+}

@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(256) k_update(ytm_config cfg, uint32_t *__rest
                         } else {  // type1b_fb, kernel.cu:453-470
                             cand = vm & ctr.ne(zero_s);
                         }
-                        if (cand) ctr.dec(cand & smask_word(cfg.seed, cfg.s_threshold16, g, t, (uint32_t)k, (uint32_t)w));
+                        if (cand) ctr.dec(cand & smask_word(cfg.seed, cfg.s_threshold12, g, t, (uint32_t)k, (uint32_t)w));
                     }
                 }
 #pragma unroll

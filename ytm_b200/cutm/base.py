@@ -238,6 +238,13 @@ class BaseTM:
             mask = None
         drop = None if mask is None else self._to_device(mask[self.clause_lo:self.clause_lo + self.clause_count])
         t = self.sample_counter
+        if batch_size == 1 and self.world == 1 and self.number_of_patches == 1 and N > 0 \
+                and hasattr(self.engine, "train_fit_b1"):
+            # the reference's per-sample loop, one fused launch per sample
+            self.engine.train_fit_b1(lits, Y, t, drop)
+            self.sample_counter = t + N
+            self.last_class_sums = self.engine.b1_class_sums(N)
+            return
         for i in range(0, N, batch_size):
             B = min(batch_size, N - i)
             lb, yb = lits[i:i + B], Y[i:i + B]
@@ -317,6 +324,7 @@ class BaseTM:
             "min_y": self.min_y,
             "max_y": self.max_y,
             "sample_counter": self.sample_counter,
+            "decision_key": self._key,
         }
 
     def load_state_dict(self, state):
@@ -333,3 +341,9 @@ class BaseTM:
         self.engine.weights.copy_(torch.from_numpy(np.ascontiguousarray(w.astype(np.int32))))
         self.engine.patch_w.copy_(torch.from_numpy(np.ascontiguousarray(pw)))
         self.sample_counter = int(sd.get("sample_counter", 0))
+        if sd.get("decision_key") is not None and int(sd["decision_key"]) != self._key:
+            # a model saved with seed=None keeps drawing from its own stream
+            self._key = int(sd["decision_key"])
+            self.cfg_full.seed = self._key
+            self.cfg.seed = self._key
+            self.engine.cfg.seed = self._key

@@ -159,6 +159,25 @@ class CudaEngine:
                                             _p(lits_b), B, int(t0), _p(sel_override), _p(ws), self._stream()),
                   "ytm_train_update")
 
+    def train_fit_b1(self, lits: torch.Tensor, Y: torch.Tensor, t0: int, drop: torch.Tensor | None) -> None:
+        """Batch-1 training over all samples of lits in order (single patch,
+        single process): one fused launch per sample."""
+        N = lits.shape[0]
+        if N == 0:
+            return
+        ws = self.workspace(_lib.YTM_OP_TRAIN_B1, 0)
+        with torch.cuda.device(self.device):
+            check(self.lib.ytm_train_fit_b1(self._cfg, _p(self.state), _p(self.weights), _p(self.bias), _p(drop),
+                                            _p(lits), _p(Y), N, int(t0), _p(self.patch_w), _p(ws), self._stream()),
+                  "ytm_train_fit_b1")
+
+    def b1_class_sums(self, N: int) -> torch.Tensor:
+        """Class sums [1, K] the last train_fit_b1 call used for its last
+        sample (slot (N-1) % 3 of the class-sum ring at the workspace start)."""
+        ws = self._ws[_lib.YTM_OP_TRAIN_B1]
+        ring = ws[:3 * self.K * 4].view(torch.int32).view(3, self.K)
+        return ring[(N - 1) % 3].reshape(1, self.K)
+
     def selection(self, B: int) -> torch.Tensor:
         sel = torch.empty((B, self.C), dtype=torch.int32, device=self.device)
         ws = self.workspace(_lib.YTM_OP_TRAIN, B)
