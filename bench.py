@@ -251,7 +251,7 @@ def main():
 
     # roofline of the dominant kernel (feedback): the state's read-modify-write
     cfg = eng.cfg
-    chunks = (B + 31) // 32
+    chunks = (B + 63) // 64  # k_update chunk of 64 samples
     alg_bytes = cfg.clause_count * chunks * cfg.planes * cfg.words * 4 * 2 + B * cfg.words * 4 * cfg.patches
     upd_s = statistics.mean(upd_ms) / 1000.0
     peak, peak_kind = load_peaks()

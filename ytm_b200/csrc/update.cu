@@ -4,10 +4,10 @@
 // (kernel.cu:397-613): one thread per clause walks classes and then all L
 // literals as u32 states, drawing one curand uniform per eligible literal.
 //
-// Here a CTA owns one clause.  Per chunk of 32 samples:
-//  1. threads over classes decide, for each (sample, class), whether and which
-//     feedback fires (Q-selection and update draws from Philox, target, weight
-//     sign), updating the clause's weights in shared memory as they go;
+// Here a CTA owns one clause.  Per chunk of 64 samples:
+//  1. all (sample, class) Q-selection and update draws run in parallel; then
+//     threads over classes walk the samples in order to fix each feedback type
+//     (it depends on the weight sign), updating weights in shared memory;
 //  2. the decided events are compacted into a list in (sample, class) order;
 //  3. threads over literal words load the word's bit planes once, apply every
 //     event of the chunk in order with bit-parallel ripple adders (32 literals
@@ -18,7 +18,7 @@
 
 namespace ytm {
 
-constexpr int UPD_BC = 32;  // samples per chunk
+constexpr int UPD_BC = 64;  // samples per chunk
 
 // thr[b][k] = floor(p * 2^32) of the update probability, bit 63 set when the
 // target is -1 (kernel.cu:544-551, 569-571).
@@ -65,21 +65,29 @@ __global__ void __launch_bounds__(256) k_update(ytm_config cfg, uint32_t *__rest
 
     for (int b0 = 0; b0 < B; b0 += UPD_BC) {
         const int bc = min(UPD_BC, B - b0);
-        if (tid < bc) sel_s[tid] = sel[(int64_t)(b0 + tid) * C + c];
+        for (int q = tid; q < bc; q += nt) sel_s[q] = sel[(int64_t)(b0 + q) * C + c];
         __syncthreads();
-        // 1. decisions, class-parallel, sample-sequential (weights evolve)
+        // 1a. the chunk's Q-selection and update draws, all (sample, class)
+        //     pairs in parallel: 1 = update with target +1, 2 = with target -1
+        for (int idx = tid; idx < bc * nk; idx += nt) {
+            const int bl = idx / nk, kk = idx - bl * nk;
+            const int b = b0 + bl, k = k0 + kk;
+            uint64_t th = thr[(int64_t)b * K + k];
+            const bool neg = (th >> 63) != 0;
+            th &= ~(1ull << 63);
+            u32x4 r = draw(cfg.seed, g, t0 + (uint64_t)b, 0, TAG_CLASS, (uint32_t)k);
+            const bool pass = !(neg && !((uint64_t)r.x < cfg.q_threshold));  // kernel.cu:573
+            evt[idx] = (pass && (uint64_t)r.y < th) ? (neg ? 2 : 1) : 0;      // kernel.cu:582
+        }
+        __syncthreads();
+        // 1b. feedback types, class-parallel and sample-sequential (weights evolve)
         for (int kk = tid; kk < nk; kk += nt) {
-            const int k = k0 + kk;
             int32_t wv = wk[kk];
             for (int bl = 0; bl < bc; ++bl) {
-                const int b = b0 + bl;
-                uint64_t th = thr[(int64_t)b * K + k];
-                const int target = (th >> 63) ? -1 : 1;
-                th &= ~(1ull << 63);
-                u32x4 r = draw(cfg.seed, g, t0 + (uint64_t)b, 0, TAG_CLASS, (uint32_t)k);
+                const uint8_t a = evt[bl * nk + kk];
                 uint8_t ev = EV_NONE;
-                bool pass = !(target == -1 && !((uint64_t)r.x < cfg.q_threshold));  // kernel.cu:573
-                if (pass && (uint64_t)r.y < th) {                                    // kernel.cu:582
+                if (a) {
+                    const int target = a == 1 ? 1 : -1;
                     const int sign = (wv >= 0) - (wv < 0);
                     const bool fired = sel_s[bl] > -1;
                     const int ts = target * sign;
@@ -101,21 +109,26 @@ __global__ void __launch_bounds__(256) k_update(ytm_config cfg, uint32_t *__rest
         __syncthreads();
         // 2. compaction in (sample, class) order
         if (tid < 32) {
-            int n = 0;
-            if (tid < bc)
-                for (int kk = 0; kk < nk; ++kk) n += evt[tid * nk + kk] != EV_NONE;
-            int incl = n;
-            for (int o = 1; o < 32; o <<= 1) {
-                int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-                if (tid >= o) incl += v;
-            }
-            int pos = incl - n;
-            if (tid < bc)
-                for (int kk = 0; kk < nk; ++kk) {
-                    uint32_t ev = evt[tid * nk + kk];
-                    if (ev != EV_NONE) list[pos++] = ((uint32_t)tid << 24) | (ev << 22) | (uint32_t)kk;
+            int base = 0;
+            for (int r0 = 0; r0 < bc; r0 += 32) {
+                const int row = r0 + tid;
+                int n = 0;
+                if (row < bc)
+                    for (int kk = 0; kk < nk; ++kk) n += evt[row * nk + kk] != EV_NONE;
+                int incl = n;
+                for (int o = 1; o < 32; o <<= 1) {
+                    int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                    if (tid >= o) incl += v;
                 }
-            if (tid == 31) cnt[0] = incl;
+                int pos = base + incl - n;
+                if (row < bc)
+                    for (int kk = 0; kk < nk; ++kk) {
+                        uint32_t ev = evt[row * nk + kk];
+                        if (ev != EV_NONE) list[pos++] = ((uint32_t)row << 24) | (ev << 22) | (uint32_t)kk;
+                    }
+                base += __shfl_sync(0xFFFFFFFFu, incl, 31);
+            }
+            if (tid == 0) cnt[0] = base;
         }
         __syncthreads();
         const int nev = cnt[0];
