@@ -86,6 +86,28 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
+def lop3_peak(dev):
+    """Measured LOP3 throughput (ops/s) of this GPU: the ceiling of the
+    word-test (one LOP3 each) clause evaluation."""
+    import ctypes as ct
+    import torch
+    from ytm_b200 import _lib
+    lib = _lib.load()
+    out = torch.zeros(1, dtype=torch.int32, device=dev)
+    ops = ct.c_uint64(0)
+    stream = ct.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    blocks = torch.cuda.get_device_properties(dev).multi_processor_count * 8
+    best = 0.0
+    for it in (64, 4096, 4096, 4096):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        _lib.check(lib.ytm_probe_lop3(blocks, it, ct.c_void_p(out.data_ptr()), ct.byref(ops), stream))
+        b.record()
+        torch.cuda.synchronize(dev)
+        best = max(best, ops.value / (a.elapsed_time(b) / 1000.0))
+    return best
+
+
 def workload(name, n):
     from ytm_b200 import synthetic
     X, y = synthetic.make(name, n)
@@ -231,7 +253,17 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
+    fused = B == 1 and world == 1 and tm._fused_b1_ok()
+
     def step(i, ev=None):
+        if fused:  # the path MultiClassTM.fit takes at batch 1: one fused launch per sample
+            if ev:
+                ev[0].record()
+            eng.train_fit_b1(lits[i * S:(i + 1) * S], Yd[i * S:(i + 1) * S], tm.sample_counter, None)
+            if ev:
+                ev[1].record()
+            tm.sample_counter += S
+            return
         for j in range(i * S, (i + 1) * S, B):
             lb, yb = lits[j:j + B], Yd[j:j + B]
             t = tm.sample_counter
@@ -269,8 +301,15 @@ def main():
 
     # roofline of the dominant kernel (feedback): the state's read-modify-write
     cfg = eng.cfg
-    chunks = (B + 63) // 64  # k_update chunk of 64 samples
-    alg_bytes = cfg.clause_count * chunks * cfg.planes * cfg.words * 4 * 2 + B * cfg.words * 4 * cfg.patches
+    if fused:  # per sample: every clause's planes read + written once, literals read once
+        alg_bytes = S * (cfg.clause_count * cfg.planes * cfg.words * 4 * 2 + cfg.words * 4 * cfg.patches)
+        kernel = "k_fused_b1 (feedback of sample i + evaluation of sample i+1), per 256 launches"
+        launches = S + 1
+    else:
+        chunks = (B + 63) // 64  # k_update chunk of 64 samples
+        alg_bytes = cfg.clause_count * chunks * cfg.planes * cfg.words * 4 * 2 + B * cfg.words * 4 * cfg.patches
+        kernel = "k_update (feedback)"
+        launches = 7 * (S // B)
     upd_s = statistics.mean(upd_ms) / 1000.0
     peak, peak_kind = load_peaks()
     achieved = alg_bytes / upd_s / 1e9
@@ -295,6 +334,8 @@ def main():
         infer_ms = float(t.item())
     infer_value = ni / (infer_ms / 1000.0)
     word_tests = ni * cfg.clauses * cfg.patches * cfg.words
+
+    lop3 = lop3_peak(dev)
 
     # end to end through the public API: pinned host inputs, H2D, encode, train,
     # D2H of the batch's class sums
@@ -328,13 +369,15 @@ def main():
             "config": {"workload": name, "global_batch": B, "samples_per_step": S, "parallelism": f"clause-shard{world}",
                        "l2": "flushed between timed steps (2x L2 write)", **_cfgjson(kw)},
             "e2e": e2e,
-            "gpu_launches": 7 * args.steps * (S // B),
+            "gpu_launches": launches * args.steps,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "kernel": "k_update (feedback)",
+                         "frac": achieved / peak, "traffic": None, "kernel": kernel,
                          "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg_bytes,
                          "launch_ms": statistics.mean(upd_ms)},
             "infer": {"value": infer_value, "unit": "samples/s", "samples": ni,
-                      "dense_word_tests_per_s": word_tests / (infer_ms / 1000.0)},
+                      "dense_word_tests_per_s": word_tests / (infer_ms / 1000.0),
+                      "lop3_peak_per_s": lop3, "int_pipe_frac": word_tests / (infer_ms / 1000.0) / lop3,
+                      "kernel": "k_match<0> (one LOP3 per word test)"},
             "clocks": clk.summary(),
         }
         if not args.no_cpu:

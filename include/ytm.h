@@ -187,8 +187,8 @@ ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, int32_t *wei
  * select_active, clause_update per sample).  Same result as ytm_train_eval +
  * ytm_train_update with B = 1 for each sample, t = t0 + i, but one fused
  * launch per sample (feedback of sample i and evaluation of sample i+1) queued
- * from C++.  Single-patch models only (YTM_ERR_UNSUPPORTED otherwise); one
- * process (the class sums are not all-reduced).  lits u32 [N][1][W], Y i32
+ * from C++.  Up to 2048 patches; one process (the class sums are not
+ * all-reduced).  lits u32 [N][P][W], Y i32
  * [N][K].  workspace: ytm_workspace_bytes(cfg, YTM_OP_TRAIN_B1, 0). */
 ytm_status ytm_train_fit_b1(const ytm_config *cfg, uint32_t *state, int32_t *weights, const int32_t *bias,
                             const uint32_t *drop, const uint32_t *lits, const int32_t *Y, int64_t N,
@@ -212,6 +212,12 @@ ytm_status ytm_train_selection(const ytm_config *cfg, int32_t B, const void *wor
 ytm_status ytm_infer_noalloc(const ytm_config *cfg, const uint32_t *state, const int32_t *weights,
                              const int32_t *bias, const uint32_t *lits, int64_t N, int32_t *cs,
                              void *stream);
+
+/* Measurement helper (no reference counterpart): launch `blocks` x 256
+ * threads that each run `iters` x 8 dependent-free LOP3 operations (the
+ * word-test operation a |= b & ~c); *ops receives the operation count.  Time
+ * it with events on `stream` to get the logic-pipe ceiling. */
+ytm_status ytm_probe_lop3(int32_t blocks, int32_t iters, uint32_t *out, uint64_t *ops, void *stream);
 
 /* Message of the last failing call on this thread ("" if none). */
 const char *ytm_last_error(void);

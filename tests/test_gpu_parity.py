@@ -208,7 +208,7 @@ def test_infer_equals_transform_times_weights_config1_size():
 
 
 @pytest.mark.parametrize("case", ["vanilla", "coalesced_b1", "states4096", "states16", "maxinc_nopol",
-                                  "many_classes", "drop"])
+                                  "many_classes", "drop", "conv", "conv_rgb_b3", "noneg_noloc"])
 def test_fused_batch1_matches_oracle(case):
     """ytm_train_fit_b1 (one fused launch per sample) == the oracle's
     per-sample loop."""

@@ -15,7 +15,8 @@
 // Class sums live in a ring of three [K] slots: launch i reads slot i%3,
 // accumulates slot (i+1)%3 and clears slot (i+2)%3, which launch i-1 finished
 // reading and launch i+1 will fill.  Results are bit-identical to
-// ytm_train_eval + ytm_train_update with B = 1 (single patch models).
+// ytm_train_eval + ytm_train_update with B = 1.  Convolutional models test,
+// per clause, only its non-zero include words against each patch.
 #include "common.cuh"
 
 namespace ytm {
@@ -31,7 +32,7 @@ B1Ws b1_ws_layout(const ytm_config *cfg) {
     const uint64_t C = cfg->clause_count, K = cfg->n_classes;
     uint64_t o = 0;
     l.cs = o;    o = align_up(o + 3 * K * 4, 256);
-    l.fired = o; o = align_up(o + 2 * C, 256);
+    l.fired = o; o = align_up(o + 2 * C * 4, 256);
     l.ninc = o;  o = align_up(o + C * 4, 256);
     l.total = o;
     return l;
@@ -46,7 +47,7 @@ template <int NB>
 __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     ytm_config cfg, uint32_t *__restrict__ state, int32_t *__restrict__ weights, const int32_t *__restrict__ bias,
     const uint32_t *__restrict__ drop, const uint32_t *__restrict__ lits, const int32_t *__restrict__ Y, int64_t i,
-    int64_t N, uint64_t t0, int do_update, int32_t *__restrict__ cs_ring, uint8_t *__restrict__ fired_pp,
+    int64_t N, uint64_t t0, int do_update, int32_t *__restrict__ cs_ring, int32_t *__restrict__ sel_pp,
     int32_t *__restrict__ ninc_ws, int32_t *__restrict__ patch_w) {
     extern __shared__ __align__(16) unsigned char smraw[];
     const int C = cfg.clause_count, W = cfg.words, K = cfg.n_classes, L = cfg.literals;
@@ -55,13 +56,17 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     uint64_t *thr_s = (uint64_t *)smraw;                 // [K]  threshold | target bit
     int32_t *cs_blk = (int32_t *)(thr_s + K);            // [K]
     uint32_t *ev_s = (uint32_t *)(cs_blk + K);           // [FB_CPB][KB][3]: any, type Ia, type II
+    uint32_t *lw_s = ev_s + FB_CPB * KB * 3;              // [FB_WARPS][W] non-zero include words (P > 1)
+    uint32_t *li_s = lw_s + FB_WARPS * W;                 // [FB_WARPS][W] their include masks
+    uint32_t *mb_s = li_s + FB_WARPS * W;                 // [FB_WARPS][PW] patch match bits
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int do_eval = (i + 1 < N) || !do_update;       // the prologue evaluates sample 0
     const int64_t e_next = do_update ? i + 1 : 0;        // sample evaluated by this launch
     const int32_t *cs_cur = cs_ring + (i % 3) * K;
     int32_t *cs_next = cs_ring + (e_next % 3) * K;
-    const uint8_t *fired_cur = fired_pp + (i & 1) * (int64_t)C;
-    uint8_t *fired_next = fired_pp + (e_next & 1) * (int64_t)C;
+    const int32_t *sel_cur = sel_pp + (i & 1) * (int64_t)C;     // picks of sample i (-1: not fired)
+    int32_t *sel_next = sel_pp + (e_next & 1) * (int64_t)C;     // picks of sample i+1
+    const int P = cfg.patches, PW = (P + 31) >> 5;
     const uint64_t t = t0 + (uint64_t)i;
     const int cbase = blockIdx.x * FB_CPB;
 
@@ -88,7 +93,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
         if (c < C && !(drop && drop[c] == 1u)) {  // kernel.cu:555
             const uint32_t g = (uint32_t)(cfg.clause_lo + c);
             const int k0 = cfg.coalesced ? 0 : (int)(g / (uint32_t)cfg.clauses_per_class);
-            const bool fired = fired_cur[c] != 0;
+            const bool fired = sel_cur[c] >= 0;
             const bool ok_inc = ninc_ws[c] <= cfg.max_included_literals;
             for (int kk = 0; kk < nk; ++kk) {
                 const int k = k0 + kk;
@@ -125,8 +130,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     // ---- 2. per clause: feedback over the words, then evaluation of sample i+1
     const uint32_t max_s = (uint32_t)(cfg.max_state + cfg.state_offset);
     const uint32_t zero_s = (uint32_t)cfg.state_offset;
-    const uint32_t *x_cur = lits + i * W;
-    const uint32_t *x_next = lits + e_next * W;
+    const uint32_t *x_next = lits + e_next * P * W;  // patch 0 of sample i+1 (single-patch eval)
     constexpr int CPW = FB_CPB / FB_WARPS;  // clauses per warp
     bool has_ev[CPW];
 #pragma unroll
@@ -143,7 +147,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     int cnt[CPW];
 #pragma unroll
     for (int q = 0; q < CPW; ++q) { viol[q] = 0u; cnt[q] = 0; }
-    if (do_eval) {
+    if (do_eval && P == 1) {
         for (int w = lane; w < W; w += 32) {
             const uint32_t xn = x_next[w];
 #pragma unroll
@@ -166,7 +170,8 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
         const uint32_t g = (uint32_t)(cfg.clause_lo + c);
         const int k0 = cfg.coalesced ? 0 : (int)(g / (uint32_t)cfg.clauses_per_class);
         const uint32_t *ev = ev_s + j * KB * 3;
-        const bool fired_cur_b = fired_cur[c] != 0;
+        const int32_t sc = sel_cur[c];
+        const uint32_t *x_cur = lits + (i * P + (sc > 0 ? sc : 0)) * W;  // the picked patch of sample i
         uint32_t vq = 0u;
         int cq = 0;
         for (int w = lane; w < W; w += 32) {
@@ -174,7 +179,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
             Counter<NB> ctr;
 #pragma unroll
             for (int b = 0; b < NB; ++b) ctr.p[b] = state[((int64_t)b * C + c) * W + w];
-            const uint32_t x = fired_cur_b ? x_cur[w] : 0u;
+            const uint32_t x = sc >= 0 ? x_cur[w] : 0u;
             for (int kb = 0; kb < KB; ++kb) {
                 uint32_t m = ev[kb * 3];
                 const uint32_t m1a = ev[kb * 3 + 1], m2 = ev[kb * 3 + 2];
@@ -199,7 +204,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
             }
 #pragma unroll
             for (int b = 0; b < NB; ++b) state[((int64_t)b * C + c) * W + w] = ctr.p[b];
-            if (do_eval) {
+            if (do_eval && P == 1) {
                 vq |= ctr.p[NB - 1] & ~x_next[w];
                 cq += __popc(ctr.p[NB - 1]);
             }
@@ -208,8 +213,8 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
         for (int r = 0; r < CPW; ++r)
             if (r == q) { viol[r] = vq; cnt[r] = cq; }
     }
-    // 2c. fired bits, include counts, patch weights and class sums of i+1
-    if (do_eval) {
+    // 2c. single patch: fired bits, include counts, patch weights, class sums of i+1
+    if (do_eval && P == 1) {
 #pragma unroll
         for (int q = 0; q < CPW; ++q) {
             const int c = cbase + wib + q * FB_WARPS;
@@ -222,12 +227,83 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
             const bool f = !(drop && drop[c] == 1u) && vr == 0u;
             if (lane == 0) {
                 ninc_ws[c] = cr;
-                fired_next[c] = f ? 1 : 0;
-                if (f) patch_w[(int64_t)c * cfg.patches] += 1;  // kernel.cu:305
+                sel_next[c] = f ? 0 : -1;
+                if (f) patch_w[c] += 1;  // kernel.cu:305
             }
             if (f)
                 for (int kk = lane; kk < nk; kk += 32)
                     atomicAdd(&cs_blk[k0 + kk], weights[(int64_t)c * K + k0 + kk]);
+        }
+    }
+    // 2d. several patches: match every patch of sample i+1 testing only the
+    //     clause's non-zero include words (fast_eval, kernel.cu:255-282), then
+    //     pick one matching patch uniformly (select_active, kernel.cu:285-316)
+    if (do_eval && P > 1) {
+        uint32_t *lw = lw_s + wib * W, *li = li_s + wib * W, *mb = mb_s + wib * PW;
+        const uint32_t *xs = lits + e_next * P * W;
+        const uint64_t t_next = t0 + (uint64_t)e_next;
+#pragma unroll 1
+        for (int q = 0; q < CPW; ++q) {
+            const int c = cbase + wib + q * FB_WARPS;
+            if (c >= C) break;
+            const uint32_t g = (uint32_t)(cfg.clause_lo + c);
+            const int k0 = cfg.coalesced ? 0 : (int)(g / (uint32_t)cfg.clauses_per_class);
+            int n = 0, cr = 0;
+            for (int w0 = 0; w0 < W; w0 += 32) {
+                const int w = w0 + lane;
+                const uint32_t top = w < W ? state[((int64_t)(NB - 1) * C + c) * W + w] : 0u;
+                cr += __popc(top);
+                const uint32_t m = __ballot_sync(0xFFFFFFFFu, top != 0u);
+                if (top) {
+                    const int pos = n + __popc(m & ((1u << lane) - 1u));
+                    lw[pos] = (uint32_t)w;
+                    li[pos] = top;
+                }
+                n += __popc(m);
+            }
+            cr = __reduce_add_sync(0xFFFFFFFFu, cr);
+            __syncwarp();
+            const bool dropped = drop && drop[c] == 1u;
+            int count = 0;
+            if (!dropped) {
+                for (int p0 = 0; p0 < P; p0 += 32) {
+                    const int p = p0 + lane;
+                    bool ok = p < P;
+                    if (ok) {
+                        const uint32_t *xp = xs + (int64_t)p * W;
+                        for (int j = 0; j < n; ++j)
+                            if (li[j] & ~xp[lw[j]]) { ok = false; break; }
+                    }
+                    const uint32_t m = __ballot_sync(0xFFFFFFFFu, ok);
+                    if (lane == 0) mb[p0 >> 5] = m;
+                    count += __popc(m);
+                }
+            }
+            __syncwarp();
+            int32_t sp = -1;
+            if (count > 0) {
+                const uint32_t r = draw(cfg.seed, g, t_next, 0, TAG_PATCH, 0).x;
+                uint32_t idx = (uint32_t)(((uint64_t)r * (uint64_t)count) >> 32);
+                for (int jw = 0; jw < PW; ++jw) {
+                    uint32_t word = mb[jw];
+                    const uint32_t pc = (uint32_t)__popc(word);
+                    if (idx < pc) {
+                        for (uint32_t z = 0; z < idx; ++z) word &= word - 1u;
+                        sp = jw * 32 + __ffs(word) - 1;
+                        break;
+                    }
+                    idx -= pc;
+                }
+            }
+            if (lane == 0) {
+                ninc_ws[c] = cr;
+                sel_next[c] = sp;
+                if (sp >= 0) patch_w[(int64_t)c * P + sp] += 1;  // kernel.cu:305
+            }
+            if (sp >= 0)
+                for (int kk = lane; kk < nk; kk += 32)
+                    atomicAdd(&cs_blk[k0 + kk], weights[(int64_t)c * K + k0 + kk]);
+            __syncwarp();
         }
     }
     __syncthreads();
@@ -245,7 +321,7 @@ extern "C" ytm_status ytm_train_fit_b1(const ytm_config *cfg, uint32_t *state, i
                                        uint64_t t0, int32_t *patch_w, void *workspace, void *stream) {
     ytm_status rc = check_cfg(cfg);
     if (rc) return rc;
-    if (cfg->patches != 1) return fail(YTM_ERR_UNSUPPORTED, "ytm_train_fit_b1 handles single-patch models");
+    if (cfg->patches > 32 * 64) return fail(YTM_ERR_UNSUPPORTED, "ytm_train_fit_b1 handles at most 2048 patches");
     if (N < 0) return fail(YTM_ERR_ARG, "N < 0");
     if (N == 0) return YTM_OK;
     if (!state || !weights || !lits || !Y || !patch_w || !workspace) return fail(YTM_ERR_ARG, "null pointer");
@@ -255,20 +331,27 @@ extern "C" ytm_status ytm_train_fit_b1(const ytm_config *cfg, uint32_t *state, i
     B1Ws l = b1_ws_layout(cfg);
     char *ws = (char *)workspace;
     int32_t *cs_ring = (int32_t *)(ws + l.cs);
-    uint8_t *fired = (uint8_t *)(ws + l.fired);
+    int32_t *sel = (int32_t *)(ws + l.fired);
     int32_t *ninc = (int32_t *)(ws + l.ninc);
     if ((rc = cuda_check(cudaMemsetAsync(cs_ring, 0, 3 * (size_t)cfg->n_classes * 4, st), "memset"))) return rc;
     const int C = cfg->clause_count;
     const int blocks = (int)cdiv(C, FB_CPB);
     const int nk = cfg->coalesced ? cfg->n_classes : 1;
-    const size_t smem = (size_t)cfg->n_classes * 12 + (size_t)FB_CPB * ((nk + 31) / 32) * 12 + 16;
+    size_t smem = (size_t)cfg->n_classes * 12 + (size_t)FB_CPB * ((nk + 31) / 32) * 12 + 16;
+    if (cfg->patches > 1) smem += (size_t)FB_WARPS * (2 * cfg->words + (cfg->patches + 31) / 32) * 4;
+    if (smem > 200 * 1024) return fail(YTM_ERR_UNSUPPORTED, "ytm_train_fit_b1: literal vector too long");
     YTM_DISPATCH_PLANES(cfg->planes, {
+        if (smem > 48 * 1024) {
+            if ((rc = cuda_check(cudaFuncSetAttribute(k_fused_b1<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                      (int)smem), "fused b1 smem")))
+                return rc;
+        }
         k_fused_b1<NB><<<blocks, FB_WARPS * 32, smem, st>>>(*cfg, state, weights, bias, drop, lits, Y, 0, N, t0, 0,
-                                                           cs_ring, fired, ninc, patch_w);
+                                                           cs_ring, sel, ninc, patch_w);
         if ((rc = launch_check("fused b1 prologue"))) return rc;
         for (int64_t i = 0; i < N; ++i) {
             k_fused_b1<NB><<<blocks, FB_WARPS * 32, smem, st>>>(*cfg, state, weights, bias, drop, lits, Y, i, N, t0,
-                                                               1, cs_ring, fired, ninc, patch_w);
+                                                               1, cs_ring, sel, ninc, patch_w);
         }
     });
     return launch_check("fused b1");

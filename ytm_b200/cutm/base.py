@@ -238,7 +238,7 @@ class BaseTM:
             mask = None
         drop = None if mask is None else self._to_device(mask[self.clause_lo:self.clause_lo + self.clause_count])
         t = self.sample_counter
-        if batch_size == 1 and self.world == 1 and self.number_of_patches == 1 and N > 0 \
+        if batch_size == 1 and self.world == 1 and N > 0 and self._fused_b1_ok() \
                 and hasattr(self.engine, "train_fit_b1"):
             # the reference's per-sample loop, one fused launch per sample
             self.engine.train_fit_b1(lits, Y, t, drop)
@@ -254,6 +254,12 @@ class BaseTM:
             t += B
             self.last_class_sums = cs
         self.sample_counter = t
+
+    def _fused_b1_ok(self) -> bool:
+        """Batch-1 training runs as one fused launch per sample unless the
+        per-clause patch scan would be long (P * W above 16k words): then the
+        tiled evaluation kernel of the general path is faster."""
+        return self.number_of_patches * self.number_of_literal_chunks <= 16384
 
     # -- inference (base.py:375-420) --------------------------------------------------
     def _score_device(self, lits: torch.Tensor, chunk: int | None = None) -> torch.Tensor:

@@ -160,8 +160,8 @@ class CudaEngine:
                   "ytm_train_update")
 
     def train_fit_b1(self, lits: torch.Tensor, Y: torch.Tensor, t0: int, drop: torch.Tensor | None) -> None:
-        """Batch-1 training over all samples of lits in order (single patch,
-        single process): one fused launch per sample."""
+        """Batch-1 training over all samples of lits in order (single
+        process): one fused launch per sample."""
         N = lits.shape[0]
         if N == 0:
             return
