@@ -38,7 +38,7 @@ B1Ws b1_ws_layout(const ytm_config *cfg) {
     return l;
 }
 
-// Block = 8 warps owning FB_CPB consecutive clauses.  Thresholds of sample i
+// Block = 8 warps owning FB_CPB clauses.  Thresholds of sample i
 // are computed once per block; decisions run one clause per thread (the
 // Philox class draws of 32 clauses share each warp instruction); then each
 // warp streams the words of its clauses (8 per warp), applying the events and
@@ -50,6 +50,11 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     int64_t N, uint64_t t0, int do_update, int32_t *__restrict__ cs_ring, int32_t *__restrict__ sel_pp,
     int32_t *__restrict__ ninc_ws, int32_t *__restrict__ patch_w) {
     extern __shared__ __align__(16) unsigned char smraw[];
+    // Programmatic dependent launch: let launch i+1 be scheduled now, and
+    // wait here until launch i-1 has completed and its writes are visible.
+    // Everything below reads what the previous launch wrote.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int C = cfg.clause_count, W = cfg.words, K = cfg.n_classes, L = cfg.literals;
     const int nk = cfg.coalesced ? K : 1;
     const int KB = (nk + 31) >> 5;                       // 32-class chunks per clause
@@ -68,7 +73,10 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     int32_t *sel_next = sel_pp + (e_next & 1) * (int64_t)C;     // picks of sample i+1
     const int P = cfg.patches, PW = (P + 31) >> 5;
     const uint64_t t = t0 + (uint64_t)i;
-    const int cbase = blockIdx.x * FB_CPB;
+    // Block b owns clauses b, b + G, b + 2G, ... (G = grid size): every block
+    // gets an even share of every clause bank, so the bank of the true class,
+    // where most feedback lands, does not pile up on a few blocks.
+    const int G = gridDim.x;
 
     for (int k = threadIdx.x; k < K; k += blockDim.x) {
         cs_blk[k] = 0;
@@ -87,7 +95,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
 
     // ---- 1. decisions of sample i: one clause per thread
     if (do_update && threadIdx.x < FB_CPB) {
-        const int c = cbase + threadIdx.x;
+        const int c = (int)threadIdx.x * G + blockIdx.x;
         uint32_t *ev = ev_s + threadIdx.x * KB * 3;
         for (int q = 0; q < KB * 3; ++q) ev[q] = 0u;
         if (c < C && !(drop && drop[c] == 1u)) {  // kernel.cu:555
@@ -152,7 +160,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
             const uint32_t xn = x_next[w];
 #pragma unroll
             for (int q = 0; q < CPW; ++q) {
-                const int c = cbase + wib + q * FB_WARPS;
+                const int c = (wib + q * FB_WARPS) * G + blockIdx.x;
                 if (!has_ev[q] && c < C) {
                     const uint32_t top = state[((int64_t)(NB - 1) * C + c) * W + w];
                     viol[q] |= top & ~xn;
@@ -166,7 +174,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     for (int q = 0; q < CPW; ++q) {
         if (!has_ev[q]) continue;
         const int j = wib + q * FB_WARPS;
-        const int c = cbase + j;
+        const int c = j * G + blockIdx.x;
         const uint32_t g = (uint32_t)(cfg.clause_lo + c);
         const int k0 = cfg.coalesced ? 0 : (int)(g / (uint32_t)cfg.clauses_per_class);
         const uint32_t *ev = ev_s + j * KB * 3;
@@ -217,7 +225,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     if (do_eval && P == 1) {
 #pragma unroll
         for (int q = 0; q < CPW; ++q) {
-            const int c = cbase + wib + q * FB_WARPS;
+            const int c = (wib + q * FB_WARPS) * G + blockIdx.x;
             if (c >= C) break;
             const uint32_t vr = __reduce_or_sync(0xFFFFFFFFu, viol[q]);
             const int cr = __reduce_add_sync(0xFFFFFFFFu, cnt[q]);
@@ -244,7 +252,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
         const uint64_t t_next = t0 + (uint64_t)e_next;
 #pragma unroll 1
         for (int q = 0; q < CPW; ++q) {
-            const int c = cbase + wib + q * FB_WARPS;
+            const int c = (wib + q * FB_WARPS) * G + blockIdx.x;
             if (c >= C) break;
             const uint32_t g = (uint32_t)(cfg.clause_lo + c);
             const int k0 = cfg.coalesced ? 0 : (int)(g / (uint32_t)cfg.clauses_per_class);
@@ -346,12 +354,24 @@ extern "C" ytm_status ytm_train_fit_b1(const ytm_config *cfg, uint32_t *state, i
                                                       (int)smem), "fused b1 smem")))
                 return rc;
         }
-        k_fused_b1<NB><<<blocks, FB_WARPS * 32, smem, st>>>(*cfg, state, weights, bias, drop, lits, Y, 0, N, t0, 0,
-                                                           cs_ring, sel, ninc, patch_w);
-        if ((rc = launch_check("fused b1 prologue"))) return rc;
-        for (int64_t i = 0; i < N; ++i) {
-            k_fused_b1<NB><<<blocks, FB_WARPS * 32, smem, st>>>(*cfg, state, weights, bias, drop, lits, Y, i, N, t0,
-                                                               1, cs_ring, sel, ninc, patch_w);
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3((unsigned)blocks);
+        lc.blockDim = dim3(FB_WARPS * 32);
+        lc.dynamicSmemBytes = smem;
+        lc.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        lc.attrs = attr;
+        lc.numAttrs = 1;
+        const ytm_config c = *cfg;
+        for (int64_t i = -1; i < N; ++i) {  // i = -1: the prologue evaluating sample 0
+            const int64_t ii = i < 0 ? 0 : i;
+            const int upd = i < 0 ? 0 : 1;
+            if ((rc = cuda_check(cudaLaunchKernelEx(&lc, k_fused_b1<NB>, c, state, weights, bias, drop, lits, Y, ii, N,
+                                                    t0, upd, cs_ring, sel, ninc, patch_w),
+                                 "fused b1 launch")))
+                return rc;
         }
     });
     return launch_check("fused b1");
