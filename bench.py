@@ -29,6 +29,9 @@ sys.path.insert(0, ROOT)
 
 METRIC = "train & infer samples/s (1/2/4/8 B200) + % of HBM/INT-pipe roofline vs CPU"
 L2_BYTES = 126 * 1024 * 1024
+# DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
+# capture each (profiles/k_update_c2.md); None where no capture was made.
+TRAFFIC = {"c2": 28.37e6 + 0.056e6}
 
 
 def load_peaks():
@@ -41,49 +44,62 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled every 10 ms through
+    NVML while the timed region runs (nvidia-smi -lms 200 as a fallback)."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, index):
-        self.index = index
-        self.rows = []
-        self.proc = None
+    def __init__(self, dev):
+        self.dev = dev
+        self.rows = []  # (sm_mhz, max_mhz, reasons bitmask)
+        self._stop = threading.Event()
+        self._nvml = None
+
+    def _handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            import torch
+            bus = torch.cuda.get_device_properties(self.dev).pci_bus_id
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode() if isinstance(bus, str) else bus)
+        except Exception:
+            idx = self.dev.index if hasattr(self.dev, "index") else int(self.dev)
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(idx)
+
+    def _poll(self):
+        nv, h = self._nvml
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h) if hasattr(
+                    nv, "nvmlDeviceGetCurrentClocksEventReasons") else nv.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                self.rows.append((sm, mx, rs))
+            except Exception:
+                pass
+            self._stop.wait(0.01)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            self._nvml = self._handle()
+            self.t = threading.Thread(target=self._poll, daemon=True)
             self.t.start()
         except Exception:
-            self.proc = None
+            self._nvml = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
-
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self._stop.set()
+        if self._nvml:
+            self.t.join(timeout=2)
 
     def summary(self):
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in self.rows if len(r) > 8 for n, v in zip(names, r[5:9]) if v == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        reasons = sorted({name for _, _, r in self.rows for bit, name in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": max(r[1] for r in self.rows),
+                "reasons": reasons, "samples": len(self.rows), "source": "nvml, 10 ms"}
 
 
 def lop3_peak(dev):
@@ -210,7 +226,7 @@ def _cfgjson(kw):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
@@ -282,7 +298,7 @@ def main():
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     upd = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    with ClockSampler(local) as clk:
+    with ClockSampler(dev) as clk:
         barrier()
         for j in range(args.steps):
             flush.zero_()  # L2 flush between timed steps (outside the step events)
@@ -306,7 +322,11 @@ def main():
         kernel = "k_fused_b1 (feedback of sample i + evaluation of sample i+1), per 256 launches"
         launches = S + 1
     else:
-        chunks = (B + 63) // 64  # k_update chunk of 64 samples
+        nk = cfg.n_classes if cfg.coalesced else 1
+        bc = min(256, (B + 31) // 32 * 32)  # k_update's chunk: event list within 32 KB of shared memory
+        while bc > 32 and nk * 4 + bc * 4 + 4 + bc * nk * 5 + 16 > 32 * 1024:
+            bc -= 32
+        chunks = (B + bc - 1) // bc
         alg_bytes = cfg.clause_count * chunks * cfg.planes * cfg.words * 4 * 2 + B * cfg.words * 4 * cfg.patches
         kernel = "k_update (feedback)"
         launches = 7 * (S // B)
@@ -371,7 +391,7 @@ def main():
             "e2e": e2e,
             "gpu_launches": launches * args.steps,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "kernel": kernel,
+                         "frac": achieved / peak, "traffic": TRAFFIC.get(name) if world == 1 else None, "kernel": kernel,
                          "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg_bytes,
                          "launch_ms": statistics.mean(upd_ms)},
             "infer": {"value": infer_value, "unit": "samples/s", "samples": ni,

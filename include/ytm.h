@@ -145,6 +145,15 @@ ytm_status ytm_infer(const ytm_config *cfg, const uint32_t *state, const int32_t
                      const int32_t *bias, const uint32_t *lits, int64_t N, int32_t *cs,
                      void *workspace, void *stream);
 
+/* Same as ytm_infer, but from include masks u32 [C][W] (the layout of
+ * ytm_include_mask / the reference's packed clauses, kernel.cu:155-204)
+ * instead of the bit-sliced state: used by sample-sharded inference, where
+ * every rank holds a replica of all clauses' include masks.
+ * workspace: ytm_workspace_bytes(cfg, YTM_OP_INFER, N). */
+ytm_status ytm_infer_include(const ytm_config *cfg, const uint32_t *inc, const int32_t *weights,
+                             const int32_t *bias, const uint32_t *lits, int64_t N, int32_t *cs,
+                             void *workspace, void *stream);
+
 /* Clause outputs u32 [N][C] (1 if any patch matches; empty clauses give 1).
  * Replaces transform (kernel.cu:346-368, base.py:465-502).
  * workspace: ytm_workspace_bytes(cfg, YTM_OP_TRANSFORM, N). */

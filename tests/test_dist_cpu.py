@@ -53,6 +53,16 @@ class OracleShardEngine:
         full[self.lo:self.lo + self.C] = self._ta
         return full
 
+    def include_mask(self):
+        packed, ninc = self.o.pack(self._ta)
+        return torch.from_numpy(packed.view(np.int32)), torch.from_numpy(ninc)
+
+    def infer_include(self, cfg_full, inc, weights, lits, bias):
+        # states with exactly these include bits: half+1 where included, 0 elsewhere
+        bits = np.unpackbits(inc.numpy().view(np.uint32).view(np.uint8), axis=1, bitorder="little")[:, :self.L]
+        ta = np.where(bits == 1, self.o.half_state + 1, 0).astype(np.uint32)
+        return torch.from_numpy(self.o.infer(ta, weights.numpy(), self._lits(lits)))
+
     def encode(self, X):
         return torch.from_numpy(self.o.encode(X.numpy().view(np.uint32)).view(np.int32))
 
@@ -119,6 +129,9 @@ def _worker(rank, world, port, out_dir):
         tm.fit(X, y, batch_size=4)
         ta, w, pw = tm.get_ta_state(), tm.get_weights(), tm.get_patch_weights()
         pred, cs = tm.predict(X)
+        tm.inference_sharding = "clauses"
+        pred2, cs2 = tm.predict(X)
+        assert np.array_equal(cs, cs2)
         tr = tm.transform(X)
         if rank == 0:
             np.savez(os.path.join(out_dir, "dist.npz"), ta=ta, w=w, pw=pw, cs=cs, tr=tr, t=tm.sample_counter)

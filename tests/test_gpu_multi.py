@@ -27,9 +27,11 @@ tm = MultiClassTM(number_of_clauses_per_class=300, T=100, s=8.0, dim=(28, 28, 1)
 tm.fit(X[:512], y[:512], batch_size=64)
 tm.fit(X[:512], y[:512], batch_size=64)
 ta, w = tm.get_ta_state(), tm.get_weights()
-pred, cs = tm.predict(X[512:])
+pred, cs = tm.predict(X[512:])          # sample-sharded inference (default)
+tm.inference_sharding = "clauses"
+pred2, cs2 = tm.predict(X[512:])        # clause-sharded inference
 if rank == 0:
-    np.savez(sys.argv[2], ta=ta, w=w, cs=cs)
+    np.savez(sys.argv[2], ta=ta, w=w, cs=cs, cs2=cs2)
 if world > 1:
     dist.destroy_process_group()
 """
@@ -61,5 +63,5 @@ def test_two_gpu_sharding_equals_one_gpu(tmp_path):
     _run(1, tmp_path / "one.npz", tmp_path)
     _run(2, tmp_path / "two.npz", tmp_path)
     a, b = np.load(tmp_path / "one.npz"), np.load(tmp_path / "two.npz")
-    for k in ("ta", "w", "cs"):
+    for k in ("ta", "w", "cs", "cs2"):
         np.testing.assert_array_equal(a[k], b[k])

@@ -16,6 +16,9 @@
 
 namespace ytm {
 
+__global__ void k_ninc(int C, int W, const uint32_t *__restrict__ inc, int32_t *__restrict__ ninc,
+                       uint32_t *__restrict__ inc_out);
+
 enum { MODE_ANY = 0, MODE_PBITS = 1, MODE_PATCHWISE = 2 };
 
 constexpr int RT = 64, CT = 64, KW = 16, XS = RT + 4;
@@ -250,6 +253,29 @@ ytm_status ytm_infer(const ytm_config *cfg, const uint32_t *state, const int32_t
     uint32_t *fired = (uint32_t *)(ws + l.fired);
     const uint32_t *inc = state + (int64_t)(cfg->planes - 1) * C * W;
     if ((rc = launch_ninc(cfg, state, ninc, st))) return rc;
+    if ((rc = cuda_check(cudaMemsetAsync(fired, 0, (size_t)N * cdiv(C, 32) * 4, st), "memset"))) return rc;
+    if ((rc = launch_match<MODE_ANY>(inc, lits, N * P, C, W, P, fired, st))) return rc;
+    k_cs_init<<<grid1(N * cfg->n_classes), 256, 0, st>>>(cs, bias, N, cfg->n_classes);
+    if ((rc = launch_check("cs init"))) return rc;
+    return launch_class_sums(fired, ninc, weights, cfg, N, 0, cs, st);
+}
+
+ytm_status ytm_infer_include(const ytm_config *cfg, const uint32_t *inc, const int32_t *weights,
+                             const int32_t *bias, const uint32_t *lits, int64_t N, int32_t *cs, void *workspace,
+                             void *stream) {
+    ytm_status rc = check_cfg(cfg);
+    if (rc) return rc;
+    if (N < 0) return fail(YTM_ERR_ARG, "N < 0");
+    if (N == 0) return YTM_OK;
+    if (!inc || !weights || !lits || !cs || !workspace) return fail(YTM_ERR_ARG, "null pointer");
+    cudaStream_t st = as_stream(stream);
+    const int C = cfg->clause_count, W = cfg->words, P = cfg->patches;
+    InferWs l = infer_ws_layout(cfg, N);
+    char *ws = (char *)workspace;
+    int32_t *ninc = (int32_t *)(ws + l.ninc);
+    uint32_t *fired = (uint32_t *)(ws + l.fired);
+    k_ninc<<<grid1((int64_t)C * 32), 256, 0, st>>>(C, W, inc, ninc, nullptr);
+    if ((rc = launch_check("include counts"))) return rc;
     if ((rc = cuda_check(cudaMemsetAsync(fired, 0, (size_t)N * cdiv(C, 32) * 4, st), "memset"))) return rc;
     if ((rc = launch_match<MODE_ANY>(inc, lits, N * P, C, W, P, fired, st))) return rc;
     k_cs_init<<<grid1(N * cfg->n_classes), 256, 0, st>>>(cs, bias, N, cfg->n_classes);

@@ -4,7 +4,7 @@
 // (kernel.cu:397-613): one thread per clause walks classes and then all L
 // literals as u32 states, drawing one curand uniform per eligible literal.
 //
-// Here a CTA owns one clause.  Per chunk of 64 samples:
+// Here a CTA owns one clause.  Per chunk of up to 256 samples:
 //  1. all (sample, class) Q-selection and update draws run in parallel; then
 //     threads over classes walk the samples in order to fix each feedback type
 //     (it depends on the weight sign), updating weights in shared memory;
@@ -18,7 +18,7 @@
 
 namespace ytm {
 
-constexpr int UPD_BC = 64;  // samples per chunk
+constexpr int UPD_BC_MAX = 256;  // samples per chunk at most (list entries hold 8-bit rows)
 
 // thr[b][k] = floor(p * 2^32) of the update probability, bit 63 set when the
 // target is -1 (kernel.cu:544-551, 569-571).
@@ -43,7 +43,8 @@ __global__ void __launch_bounds__(256) k_update(ytm_config cfg, uint32_t *__rest
                                                 int32_t *__restrict__ weights, const uint64_t *__restrict__ thr,
                                                 const uint32_t *__restrict__ drop,
                                                 const uint32_t *__restrict__ lits, int B, uint64_t t0,
-                                                const int32_t *__restrict__ sel, const int32_t *__restrict__ ninc) {
+                                                const int32_t *__restrict__ sel, const int32_t *__restrict__ ninc,
+                                                int BC) {
     extern __shared__ __align__(16) unsigned char smraw[];
     const int C = cfg.clause_count, W = cfg.words, K = cfg.n_classes, P = cfg.patches;
     const int c = blockIdx.x;
@@ -52,10 +53,10 @@ __global__ void __launch_bounds__(256) k_update(ytm_config cfg, uint32_t *__rest
     const int k0 = cfg.coalesced ? 0 : (int)(g / (uint32_t)cfg.clauses_per_class);
     const int nk = cfg.coalesced ? K : 1;
     int32_t *wk = (int32_t *)smraw;                       // [nk]
-    int32_t *sel_s = wk + nk;                             // [UPD_BC]
-    int32_t *cnt = sel_s + UPD_BC;                        // [UPD_BC + 1]
-    uint32_t *list = (uint32_t *)(cnt + UPD_BC + 1);      // [UPD_BC * nk]
-    uint8_t *evt = (uint8_t *)(list + UPD_BC * nk);       // [UPD_BC * nk]
+    int32_t *sel_s = wk + nk;                             // [BC]
+    int32_t *cnt = sel_s + BC;                            // [1]
+    uint32_t *list = (uint32_t *)(cnt + 1);               // [BC * nk]
+    uint8_t *evt = (uint8_t *)(list + BC * nk);           // [BC * nk]
     const int tid = threadIdx.x, nt = blockDim.x;
     const bool ok_inc = ninc[c] <= cfg.max_included_literals;
     const uint32_t max_s = (uint32_t)(cfg.max_state + cfg.state_offset);
@@ -63,8 +64,8 @@ __global__ void __launch_bounds__(256) k_update(ytm_config cfg, uint32_t *__rest
 
     for (int kk = tid; kk < nk; kk += nt) wk[kk] = weights[(int64_t)c * K + k0 + kk];
 
-    for (int b0 = 0; b0 < B; b0 += UPD_BC) {
-        const int bc = min(UPD_BC, B - b0);
+    for (int b0 = 0; b0 < B; b0 += BC) {
+        const int bc = min(BC, B - b0);
         for (int q = tid; q < bc; q += nt) sel_s[q] = sel[(int64_t)(b0 + q) * C + c];
         __syncthreads();
         // 1a. the chunk's Q-selection and update draws, all (sample, class)
@@ -170,8 +171,8 @@ __global__ void __launch_bounds__(256) k_update(ytm_config cfg, uint32_t *__rest
     for (int kk = tid; kk < nk; kk += nt) weights[(int64_t)c * K + k0 + kk] = wk[kk];
 }
 
-static size_t update_smem(int nk) {
-    return (size_t)nk * 4 + UPD_BC * 4 + (UPD_BC + 1) * 4 + (size_t)UPD_BC * nk * 4 + (size_t)UPD_BC * nk + 16;
+static size_t update_smem(int nk, int bc) {
+    return (size_t)nk * 4 + (size_t)bc * 4 + 4 + (size_t)bc * nk * 4 + (size_t)bc * nk + 16;
 }
 
 }  // namespace ytm
@@ -199,7 +200,11 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
         if ((rc = launch_check("update thresholds"))) return rc;
     }
     const int nk = cfg->coalesced ? cfg->n_classes : 1;
-    const size_t smem = update_smem(nk);
+    // the largest chunk (multiple of 32, at most 256 and the batch) whose
+    // event list fits 32 KB of shared memory (keeps several CTAs per SM)
+    int BC = std::min(UPD_BC_MAX, ((B + 31) / 32) * 32);
+    while (BC > 32 && update_smem(nk, BC) > 32 * 1024) BC -= 32;
+    const size_t smem = update_smem(nk, BC);
     if (smem > 227 * 1024) return fail(YTM_ERR_UNSUPPORTED, "too many classes for the feedback kernel");
     const int W = cfg->words;
     const int tpb = W <= 32 ? 32 : (W <= 64 ? 64 : (W <= 128 ? 128 : 256));
@@ -209,7 +214,8 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
                                                       (int)smem), "update smem")))
                 return rc;
         }
-        k_update<NB><<<cfg->clause_count, tpb, smem, st>>>(*cfg, state, weights, thr, drop, lits, B, t0, sel, ninc);
+        k_update<NB><<<cfg->clause_count, tpb, smem, st>>>(*cfg, state, weights, thr, drop, lits, B, t0, sel, ninc,
+                                                           BC);
     });
     return launch_check("feedback");
 }

@@ -56,13 +56,18 @@ class BaseTM:
     """Tsetlin Machine on B200 GPUs (one clause shard per process).
 
     Extra keyword arguments beyond the reference's: ``device`` (CUDA device of
-    this process, default the current one) and ``process_group`` (a
+    this process, default the current one), ``process_group`` (a
     torch.distributed group to shard clauses over; default the world group when
-    torch.distributed is initialised, else none).
+    torch.distributed is initialised, else none) and ``inference_sharding``
+    ("samples": every rank holds a replica of all include masks and weights,
+    gathered once after each change, and scores its slice of the samples;
+    "clauses": every rank scores all samples on its clauses and the class sums
+    are all-reduced).
     """
 
     def __init__(self, number_of_clauses_per_class: int, T: int, s: float, dim: tuple[int, int, int],
-                 n_classes: int, device=None, process_group=None, _engine_factory=None, **opt_args):
+                 n_classes: int, device=None, process_group=None, inference_sharding: str = "samples",
+                 _engine_factory=None, **opt_args):
         self.init_args = {"number_of_clauses_per_class": number_of_clauses_per_class, "T": T, "s": s,
                           "dim": tuple(dim), "n_classes": n_classes}
         self.opt_args: BaseTMOptArgs = {  # base.py:60-74
@@ -149,6 +154,11 @@ class BaseTM:
         self.engine = factory(self.cfg, device)
         self.device = self.engine.device
         self.sample_counter = 0  # global sample counter t of the decision stream
+        if inference_sharding not in ("samples", "clauses"):
+            raise ValueError("inference_sharding must be 'samples' or 'clauses'")
+        self.inference_sharding = inference_sharding
+        self._model_version = 0  # bumped by every change of states or weights
+        self._replica = None     # (version, include masks, weights) for sample-sharded inference
         self.last_class_sums = None  # class sums (int32, device) of the last trained batch
 
     # -- process group helpers -------------------------------------------------
@@ -192,9 +202,11 @@ class BaseTM:
 
     # -- resets (base.py:208-222) ----------------------------------------------------
     def _reset_clauses(self):
+        self._model_version += 1
         self.engine.reset_state()
 
     def _reset_weights(self, reset_bias: bool = True):
+        self._model_version += 1
         self.engine.reset_weights()
 
     # -- encoding (base.py:224-263) ----------------------------------------------------
@@ -238,6 +250,7 @@ class BaseTM:
             mask = None
         drop = None if mask is None else self._to_device(mask[self.clause_lo:self.clause_lo + self.clause_count])
         t = self.sample_counter
+        self._model_version += 1
         if batch_size == 1 and self.world == 1 and N > 0 and self._fused_b1_ok() \
                 and hasattr(self.engine, "train_fit_b1"):
             # the reference's per-sample loop, one fused launch per sample
@@ -262,8 +275,38 @@ class BaseTM:
         return self.number_of_patches * self.number_of_literal_chunks <= 16384
 
     # -- inference (base.py:375-420) --------------------------------------------------
+    def _gather_rows(self, t: torch.Tensor) -> torch.Tensor:
+        """Concatenate every rank's shard-local rows of t (clause axis 0)."""
+        counts = [_lib.shard_config(self.cfg_full, r, self.world).clause_count for r in range(self.world)]
+        m = max(counts)
+        pad = torch.zeros((m,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        pad[:t.shape[0]] = t
+        parts = [torch.empty_like(pad) for _ in range(self.world)]
+        dist.all_gather(parts, pad, group=self._pg)
+        return torch.cat([p[:n] for p, n in zip(parts, counts)]).contiguous()
+
+    def _replicated_model(self):
+        if self._replica is None or self._replica[0] != self._model_version:
+            inc, _ = self.engine.include_mask()
+            self._replica = (self._model_version, self._gather_rows(inc), self._gather_rows(self.engine.weights))
+        return self._replica[1], self._replica[2]
+
+    def _score_samples_sharded(self, lits: torch.Tensor) -> torch.Tensor:
+        N = lits.shape[0]
+        inc, w = self._replicated_model()
+        per = -(-N // self.world)
+        lo, hi = min(N, per * self.rank), min(N, per * (self.rank + 1))
+        cs = torch.zeros((per, self.number_of_outputs), dtype=torch.int32, device=self.device)
+        if hi > lo:
+            cs[:hi - lo] = self.engine.infer_include(self.cfg_full, inc, w, lits[lo:hi], self.engine.bias)
+        parts = [torch.empty_like(cs) for _ in range(self.world)]
+        dist.all_gather(parts, cs, group=self._pg)
+        return torch.cat(parts)[:N]
+
     def _score_device(self, lits: torch.Tensor, chunk: int | None = None) -> torch.Tensor:
         N = lits.shape[0]
+        if self.world > 1 and self.inference_sharding == "samples":
+            return self._score_samples_sharded(lits)
         if chunk is None:
             per = max(1, self.number_of_patches * self.number_of_literal_chunks * 4
                       + ((self.clause_count + 31) // 32) * 4)
@@ -343,6 +386,7 @@ class BaseTM:
             raise ValueError("clause weights must be whole numbers")
         pw = np.asarray(sd["patch_weights"], dtype=np.int32).reshape(C, P)[lo:lo + n]
         self.min_y, self.max_y = sd["min_y"], sd["max_y"]
+        self._model_version += 1
         self.engine.set_ta_state(ta)
         self.engine.weights.copy_(torch.from_numpy(np.ascontiguousarray(w.astype(np.int32))))
         self.engine.patch_w.copy_(torch.from_numpy(np.ascontiguousarray(pw)))

@@ -119,6 +119,21 @@ class CudaEngine:
                                      _p(lits), N, _p(cs), _p(ws), self._stream()), "ytm_infer")
         return cs
 
+    def infer_include(self, cfg_full: _lib.Config, inc: torch.Tensor, weights: torch.Tensor, lits: torch.Tensor,
+                      bias: torch.Tensor | None) -> torch.Tensor:
+        """Class sums from replicated include masks [C][W] and weights [C][K]
+        of the whole model (cfg_full), for the given samples."""
+        N = lits.shape[0]
+        cs = torch.empty((N, self.K), dtype=torch.int32, device=self.device)
+        if N == 0:
+            return cs
+        need = int(self.lib.ytm_workspace_bytes(ct.byref(cfg_full), _lib.YTM_OP_INFER, N))
+        ws = torch.empty(max(need, 256), dtype=torch.uint8, device=self.device)
+        with torch.cuda.device(self.device):
+            check(self.lib.ytm_infer_include(ct.byref(cfg_full), _p(inc), _p(weights), _p(bias), _p(lits), N, _p(cs),
+                                             _p(ws), self._stream()), "ytm_infer_include")
+        return cs
+
     def transform(self, lits: torch.Tensor) -> torch.Tensor:
         N = lits.shape[0]
         out = torch.empty((N, self.C), dtype=torch.int32, device=self.device)
