@@ -106,6 +106,7 @@ ytm_status ytm_config_shard(ytm_config *cfg, int32_t rank, int32_t world);
 #define YTM_OP_TRANSFORM 3
 #define YTM_OP_TRAIN 4
 #define YTM_OP_TRAIN_B1 5   /* ytm_train_fit_b1 (n ignored) */
+#define YTM_OP_ENCODE_THERMO 6
 uint64_t ytm_workspace_bytes(const ytm_config *cfg, int32_t op, int64_t n);
 
 /* Encode raw inputs into per-patch literal words.
@@ -114,6 +115,15 @@ uint64_t ytm_workspace_bytes(const ytm_config *cfg, int32_t op, int64_t n);
  * lits: u32 [N][P][W].  workspace: ytm_workspace_bytes(cfg, YTM_OP_ENCODE, N). */
 ytm_status ytm_encode(const ytm_config *cfg, const uint32_t *X, int64_t N, uint32_t *lits,
                       void *workspace, void *stream);
+
+/* Encode raw 8-bit images without the host u32-per-bit expansion: img u8
+ * [N][dim0*dim1][ch] with ch = dim2 / levels is thermometer-binarised as
+ * ThermometerBinarizer(levels).binarize_rgb / binarize_gray would
+ * (tm_utils/binarizer.py:5-21: bit c*levels+j of a pixel is
+ * img[c] >= (j+1)*255/(levels+1)) and encoded as ytm_encode would encode the
+ * binarised array.  workspace: ytm_workspace_bytes(cfg, YTM_OP_ENCODE_THERMO, N). */
+ytm_status ytm_encode_thermometer(const ytm_config *cfg, const uint8_t *img, int64_t N, int32_t levels,
+                                  uint32_t *lits, void *workspace, void *stream);
 
 /* Set every TA state of the shard to number_of_ta_states/2.
  * Replaces _reset_clauses (base.py:208-209). */

@@ -125,3 +125,27 @@ def test_bad_inputs_raise():
         tm.fit(np.zeros((3, 64), np.uint32), np.zeros((3, 2), np.uint32))
     with pytest.raises(NotImplementedError):
         MultiClassTM(bias=True, **KW)
+
+
+def _binarize_rgb(X, levels):
+    """ThermometerBinarizer(levels).binarize_rgb, tm_utils/binarizer.py:17-21."""
+    thr = (np.arange(1, levels + 1) * 255 / (levels + 1)).reshape(1, 1, 1, 1, levels)
+    out = (X[:, :, :, :, None] >= thr).reshape(X.shape[0], X.shape[1], X.shape[2], X.shape[3] * levels)
+    return np.asarray(out, dtype=np.uint32)
+
+
+@pytest.mark.parametrize("levels,ch,patch", [(8, 3, (5, 5)), (4, 1, (9, 9)), (3, 2, (4, 6))])
+def test_thermometer_encoding_on_device(levels, ch, patch):
+    rng = np.random.default_rng(levels)
+    imgs = rng.integers(0, 256, size=(7, 9, 9, ch), dtype=np.uint8)
+    imgs[0, 0, 0, :] = 255
+    imgs[0, 0, 1, :] = 0
+    tm = MultiClassTM(number_of_clauses_per_class=8, T=10, s=3.0, dim=(9, 9, ch * levels), n_classes=2,
+                      patch_dim=patch, seed=1)
+    want = tm.encode(_binarize_rgb(imgs, levels).reshape(7, -1))
+    np.testing.assert_array_equal(tm.encode_thermometer(imgs, levels), want)
+    o = O.Oracle(number_of_clauses_per_class=8, T=10, s=3.0, dim=(9, 9, ch * levels), n_classes=2, patch_dim=patch)
+    np.testing.assert_array_equal(want, o.encode(_binarize_rgb(imgs, levels).reshape(7, -1)))
+    lits = tm.encode_thermometer(imgs, levels, on_device=True)
+    tm.fit(lits, np.array([0, 1, 0, 1, 1, 0, 1]), is_X_encoded=True)
+    assert tm.predict(lits, is_X_encoded=True)[1].shape == (7, 2)

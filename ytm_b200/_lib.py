@@ -12,7 +12,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libytm.so")
 
 YTM_OK = 0
-YTM_OP_ENCODE, YTM_OP_INFER, YTM_OP_TRANSFORM, YTM_OP_TRAIN, YTM_OP_TRAIN_B1 = 1, 2, 3, 4, 5
+YTM_OP_ENCODE, YTM_OP_INFER, YTM_OP_TRANSFORM, YTM_OP_TRAIN, YTM_OP_TRAIN_B1, YTM_OP_ENCODE_THERMO = 1, 2, 3, 4, 5, 6
 
 # Every function include/ytm.h declares; tests check the library exports them.
 EXPORTS = (
@@ -21,6 +21,7 @@ EXPORTS = (
     "ytm_transform", "ytm_transform_patchwise", "ytm_train_eval", "ytm_train_update",
     "ytm_train_selection", "ytm_last_error", "ytm_version", "ytm_infer_noalloc",
     "ytm_train_fit_b1", "ytm_probe_lop3", "ytm_infer_include",
+    "ytm_encode_thermometer",
 )
 
 
@@ -72,6 +73,7 @@ _SIGS = {
     "ytm_infer_noalloc": ([_CFG, _P, _P, _P, _P, _I64, _P, _P], ct.c_int),
     "ytm_probe_lop3": ([_I32, _I32, _P, ct.POINTER(ct.c_uint64), _P], ct.c_int),
     "ytm_infer_include": ([_CFG, _P, _P, _P, _P, _I64, _P, _P, _P], ct.c_int),
+    "ytm_encode_thermometer": ([_CFG, _P, _I64, _I32, _P, _P, _P], ct.c_int),
     "ytm_last_error": ([], ct.c_char_p),
     "ytm_version": ([], ct.c_char_p),
 }

@@ -166,6 +166,10 @@ uint64_t ytm_workspace_bytes(const ytm_config *cfg, int32_t op, int64_t n) {
             uint64_t D = (uint64_t)cfg->dim0 * cfg->dim1 * cfg->dim2;
             return align_up((uint64_t)n * (cdiv(D, 32) + 1) * 4, 256);
         }
+        case YTM_OP_ENCODE_THERMO: {
+            uint64_t D = (uint64_t)cfg->dim0 * cfg->dim1 * cfg->dim2;
+            return align_up((uint64_t)n * (cdiv(D, 32) + 1) * 4 + 256 * 4, 256);
+        }
         case YTM_OP_INFER:
         case YTM_OP_TRANSFORM:
             return infer_ws_layout(cfg, n).total;

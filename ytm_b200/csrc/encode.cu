@@ -111,9 +111,68 @@ __global__ void k_literals(ytm_config cfg, const uint32_t *__restrict__ img, int
     }
 }
 
+// Thermometer binarisation fused into the bit packing: img u8 [N][pixels][ch]
+// -> bit image [N][IWS] with bit (pixel * ch + c) * levels + j set iff
+// img >= thr[j] (thr[j] = ceil((j+1) * 255 / (levels+1)), the integer form of
+// ThermometerBinarizer's float thresholds, tm_utils/binarizer.py:11-21).
+__global__ void k_thermo_bitpack(const uint8_t *__restrict__ img, int64_t N, int64_t pixels, int ch, int levels,
+                                 const uint32_t *__restrict__ thr, int64_t IWS, uint32_t *__restrict__ out) {
+    const int64_t D = pixels * ch * levels;
+    const int64_t total = N * IWS * 32;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t n = i / (IWS * 32), q = i % (IWS * 32);
+        bool v = false;
+        if (q < D) {
+            const int64_t pc = q / levels;  // pixel * ch + c
+            const int j = (int)(q % levels);
+            v = img[n * pixels * ch + pc] >= thr[j];
+        }
+        const uint32_t b = __ballot_sync(0xFFFFFFFFu, v);
+        if ((threadIdx.x & 31) == 0) out[n * IWS + q / 32] = b;
+    }
+}
+
 }  // namespace ytm
 
 using namespace ytm;
+
+extern "C" ytm_status ytm_encode_thermometer(const ytm_config *cfg, const uint8_t *img, int64_t N, int32_t levels,
+                                             uint32_t *lits, void *workspace, void *stream) {
+    ytm_status rc = check_cfg(cfg);
+    if (rc) return rc;
+    if (N < 0 || levels <= 0 || levels > 255) return fail(YTM_ERR_ARG, "bad N or levels");
+    if (cfg->dim2 % levels) return fail(YTM_ERR_ARG, "dim2 must be channels * levels");
+    if (N == 0) return YTM_OK;
+    if (!img || !lits || !workspace) return fail(YTM_ERR_ARG, "null pointer");
+    cudaStream_t st = as_stream(stream);
+    const int ch = cfg->dim2 / levels;
+    const int64_t pixels = (int64_t)cfg->dim0 * cfg->dim1;
+    const int64_t D = pixels * cfg->dim2;
+    const int64_t IWS = (int64_t)cdiv(D, 32) + 1;
+    uint32_t *bits = (uint32_t *)workspace;
+    uint32_t *thr = bits + N * IWS;  // levels thresholds after the bit images
+    uint32_t h[256];
+    for (int j = 0; j < levels; ++j) h[j] = (uint32_t)ceil((double)(j + 1) * 255.0 / (double)(levels + 1));
+    if ((rc = cuda_check(cudaMemcpyAsync(thr, h, levels * 4, cudaMemcpyHostToDevice, st), "thresholds"))) return rc;
+    const int sms = sm_count();
+    {
+        int64_t blocks = std::min<int64_t>(cdiv(N * IWS * 32, 256), (int64_t)sms * 16);
+        k_thermo_bitpack<<<(unsigned)blocks, 256, 0, st>>>(img, N, pixels, ch, levels, thr, IWS, bits);
+        if ((rc = launch_check("thermometer bitpack"))) return rc;
+    }
+    const int PWn = (cfg->half_literals + 31) / 32;
+    int wpb = 8;
+    size_t smem = (size_t)wpb * PWn * 4;
+    while (smem > 48 * 1024 && wpb > 1) { wpb >>= 1; smem = (size_t)wpb * PWn * 4; }
+    if (smem > 48 * 1024 &&
+        (rc = cuda_check(cudaFuncSetAttribute(k_literals, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                         "encode smem")))
+        return rc;
+    int64_t blocks = std::min<int64_t>(cdiv(N * cfg->patches, wpb), (int64_t)sms * 32);
+    k_literals<<<(unsigned)blocks, wpb * 32, smem, st>>>(*cfg, bits, IWS, N, lits);
+    return launch_check("encode literals");
+}
 
 extern "C" ytm_status ytm_encode(const ytm_config *cfg, const uint32_t *X, int64_t N, uint32_t *lits,
                                  void *workspace, void *stream) {

@@ -225,6 +225,24 @@ class BaseTM:
         """Raw u32 inputs [N, D0*D1*D2] -> encoded literals u32 [N, P, W] (host)."""
         return self._encode_device(X).cpu().numpy().view(np.uint32)
 
+    def encode_thermometer(self, images, levels: int = 8, on_device: bool = False):
+        """Thermometer-binarise and encode raw 8-bit images on the GPU.
+
+        images: uint8 [N, H, W, C] or [N, H, W] (numpy or torch), with
+        dim = (W, H, C * levels).  Same result as
+        ``tm.encode(ThermometerBinarizer(levels).binarize_rgb(images).reshape(N, -1))``
+        (tm_utils/binarizer.py:17-21) without the host's u32-per-bit array.
+        Returns u32 [N, P, W] on the host, or the int32 device tensor with
+        on_device=True (pass it to fit/predict with is_X_encoded=True)."""
+        t = images if isinstance(images, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(images))
+        if t.dtype != torch.uint8:
+            raise TypeError("images must be uint8")
+        t = t.reshape(t.shape[0], -1).to(self.device)
+        if t.shape[1] * levels != self.dim[0] * self.dim[1] * self.dim[2]:
+            raise ValueError("images do not match dim = (width, height, channels * levels)")
+        lits = self.engine.encode_thermometer(t, levels)
+        return lits if on_device else lits.cpu().numpy().view(np.uint32)
+
     def _literals_device(self, X, is_X_encoded: bool) -> torch.Tensor:
         if not is_X_encoded:
             return self._encode_device(X)

@@ -108,6 +108,20 @@ class CudaEngine:
             check(self.lib.ytm_encode(self._cfg, _p(X), N, _p(lits), _p(ws), self._stream()), "ytm_encode")
         return lits
 
+    def encode_thermometer(self, img: torch.Tensor, levels: int) -> torch.Tensor:
+        """Raw uint8 images [N, dim0*dim1*channels] on this device ->
+        literals int32 [N, P, W] (thermometer binarisation on the device)."""
+        img = img.contiguous()
+        N = img.shape[0]
+        lits = torch.empty((N, self.P, self.W), dtype=torch.int32, device=self.device)
+        if N == 0:
+            return lits
+        ws = self.workspace(_lib.YTM_OP_ENCODE_THERMO, N)
+        with torch.cuda.device(self.device):
+            check(self.lib.ytm_encode_thermometer(self._cfg, _p(img), N, int(levels), _p(lits), _p(ws),
+                                                  self._stream()), "ytm_encode_thermometer")
+        return lits
+
     def infer(self, lits: torch.Tensor, add_bias: bool = True) -> torch.Tensor:
         N = lits.shape[0]
         cs = torch.empty((N, self.K), dtype=torch.int32, device=self.device)
