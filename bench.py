@@ -44,62 +44,76 @@ def load_peaks():
 
 
 class ClockSampler:
-    """SM clock and clock-event (throttle) reasons sampled every 10 ms through
-    NVML while the timed region runs (nvidia-smi -lms 200 as a fallback)."""
+    """nvidia-smi samples of SM clock and clock-event (throttle) reasons,
+    every 20 ms, from before the timed region until after it."""
 
-    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
-               0x80: "hw_power_brake_slowdown"}
+    Q = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, dev):
-        self.dev = dev
-        self.rows = []  # (sm_mhz, max_mhz, reasons bitmask)
-        self._stop = threading.Event()
-        self._nvml = None
-
-    def _handle(self):
-        import pynvml
-        pynvml.nvmlInit()
+        import torch
+        self.bus = None
         try:
-            import torch
-            bus = torch.cuda.get_device_properties(self.dev).pci_bus_id
-            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode() if isinstance(bus, str) else bus)
+            self.bus = torch.cuda.get_device_properties(dev).pci_bus_id
         except Exception:
-            idx = self.dev.index if hasattr(self.dev, "index") else int(self.dev)
-            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(idx)
-
-    def _poll(self):
-        nv, h = self._nvml
-        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
-        while not self._stop.is_set():
-            try:
-                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h) if hasattr(
-                    nv, "nvmlDeviceGetCurrentClocksEventReasons") else nv.nvmlDeviceGetCurrentClocksThrottleReasons(h)
-                self.rows.append((sm, mx, rs))
-            except Exception:
-                pass
-            self._stop.wait(0.01)
+            pass
+        self.index = dev.index if hasattr(dev, "index") else int(dev)
+        self.rows = []
+        self.proc = None
 
     def __enter__(self):
         try:
-            self._nvml = self._handle()
-            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            time.sleep(0.5)  # let the sampler start before the timed region
         except Exception:
-            self._nvml = None
+            self.proc = None
         return self
 
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
     def __exit__(self, *a):
-        self._stop.set()
-        if self._nvml:
-            self.t.join(timeout=2)
+        if self.proc:
+            time.sleep(0.05)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def _mine(self, rows):
+        """Rows of this process's GPU: matched on the PCI bus id, else the
+        device index among the GPUs nvidia-smi lists."""
+        if self.bus is not None:
+            def bus_of(x):  # nvidia-smi "00000000:1B:00.0" -> 0x1B
+                try:
+                    return int(x.split(":")[1], 16)
+                except (IndexError, ValueError):
+                    return None
+            want = self.bus if isinstance(self.bus, int) else bus_of(str(self.bus))
+            m = [r[1:] for r in rows if bus_of(r[0]) == want]
+            if m:
+                return m
+        ids = sorted({r[0] for r in rows})
+        if self.index < len(ids):
+            return [r[1:] for r in rows if r[0] == ids[self.index]]
+        return []
 
     def summary(self):
-        if not self.rows:
+        rows = self._mine([r for r in self.rows if len(r) >= 9])
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        reasons = sorted({name for _, _, r in self.rows for bit, name in self.REASONS.items() if r & bit})
-        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": max(r[1] for r in self.rows),
-                "reasons": reasons, "samples": len(self.rows), "source": "nvml, 10 ms"}
+        reasons = sorted({n for r in rows for n, v in zip(self.NAMES, r[4:8]) if v == "Active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(sm), "source": "nvidia-smi -lms 20"}
 
 
 def lop3_peak(dev):

@@ -172,9 +172,9 @@ uint64_t ytm_workspace_bytes(const ytm_config *cfg, int32_t op, int64_t n) {
         }
         case YTM_OP_INFER:
         case YTM_OP_TRANSFORM:
-            return infer_ws_layout(cfg, n).total;
+            return infer_ws_layout(cfg, n).total + cs_planes_bytes(cfg);
         case YTM_OP_TRAIN:
-            return train_ws_layout(cfg, n).total;
+            return train_ws_layout(cfg, n).total + cs_planes_bytes(cfg);
         case YTM_OP_TRAIN_B1:
             return b1_ws_layout(cfg).total;
         default:

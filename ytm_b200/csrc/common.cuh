@@ -205,6 +205,7 @@ struct B1Ws {
     uint64_t cs, fired, ninc, total;
 };
 B1Ws b1_ws_layout(const ytm_config *cfg);
+uint64_t cs_planes_bytes(const ytm_config *cfg);  // class-sum weight planes scratch (eval.cu)
 
 // Shared launchers (eval.cu) used by several entry points.
 ytm_status launch_ninc(const ytm_config *cfg, const uint32_t *state, int32_t *ninc, cudaStream_t st);

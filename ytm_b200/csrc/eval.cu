@@ -176,6 +176,157 @@ static ytm_status launch_class_sums(const uint32_t *fired, const int32_t *ninc, 
     return launch_check("class sums");
 }
 
+static unsigned grid1(int64_t threads) {
+    int64_t b = (int64_t)cdiv(threads, 256);
+    int64_t cap = (int64_t)sm_count() * 32;
+    if (b > cap) b = cap;
+    return (unsigned)(b < 1 ? 1 : b);
+}
+
+// ---- class sums from weight bit planes ------------------------------------
+// For every 32-clause word w and class k, the weights u = w[c][k] + OFF
+// (offset binary, OFF = 2^(npl-1), npl bits) are stored as npl bit planes;
+// then sum_c fired_c * w[c][k] = sum_b 2^b popc(f & plane_b) - OFF * popc(f)
+// for f = the word's fired bits, evaluated modulo 2^32 (exact: the true sum
+// fits int32).  Words where nothing fired are skipped; every class sum has
+// one writer.
+
+constexpr int CSP_KCH = 16;
+
+__global__ void k_wmax(const int32_t *__restrict__ w, int C, int K, int own_class, int clause_lo, int cpc,
+                       int32_t *__restrict__ wmax) {
+    int m = 0;
+    const int64_t total = (int64_t)C * K;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(i / K), k = (int)(i % K);
+        if (own_class && k != (clause_lo + c) / cpc) continue;
+        const int v = w[i];
+        m = max(m, v < 0 ? -v : v);
+    }
+    for (int o = 16; o; o >>= 1) m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    if ((threadIdx.x & 31) == 0 && m) atomicMax(wmax, m);
+}
+
+__device__ __forceinline__ int planes_for(int wmax) { return 33 - __clz(wmax | 1) > 32 ? 32 : 33 - __clz(wmax | 1); }
+
+// One warp per (clause word, class): lane = clause.  planes [CW][K][32];
+// keep [CW] = clauses that count (non-empty when ninc is given).
+__global__ void k_wplanes(const int32_t *__restrict__ w, const int32_t *__restrict__ ninc, int C, int K,
+                          int own_class, int clause_lo, int cpc, const int32_t *__restrict__ wmax,
+                          uint32_t *__restrict__ planes, uint32_t *__restrict__ keep) {
+    const int lane = threadIdx.x & 31;
+    const int CWn = (C + 31) / 32;
+    const int npl = planes_for(*wmax);
+    const uint32_t off = 1u << (npl - 1);
+    const int64_t units = (int64_t)CWn * K;
+    for (int64_t u = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; u < units;
+         u += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+        const int wd = (int)(u / K), k = (int)(u % K);
+        const int c = wd * 32 + lane;
+        int32_t v = 0;
+        if (c < C && !(own_class && k != (clause_lo + c) / cpc)) v = w[(int64_t)c * K + k];
+        const uint32_t x = (uint32_t)v + off;
+        uint32_t *pl = planes + ((int64_t)wd * K + k) * 32;
+        for (int b = 0; b < npl; ++b) {
+            const uint32_t m = __ballot_sync(0xFFFFFFFFu, (x >> b) & 1u);
+            if (lane == 0) pl[b] = m;
+        }
+        if (k == 0) {
+            const uint32_t m = __ballot_sync(0xFFFFFFFFu, c < C && (!ninc || ninc[c] > 0));
+            if (lane == 0) keep[wd] = m;
+        }
+    }
+}
+
+// WARP: one warp per (sample, 16 classes), lanes striding over the clause
+// words (few samples: training batches); else one thread per (sample, 16
+// classes) walking all words (many samples: inference).
+template <bool WARP>
+__global__ void __launch_bounds__(256) k_cs_planes(const uint32_t *__restrict__ fired,
+                                                   const uint32_t *__restrict__ keep,
+                                                   const uint32_t *__restrict__ planes,
+                                                   const int32_t *__restrict__ wmax, const int32_t *__restrict__ bias,
+                                                   int C, int K, int64_t N, int32_t *__restrict__ cs) {
+    const int lane = WARP ? (threadIdx.x & 31) : 0;
+    const int step = WARP ? 32 : 1;
+    const int CWn = (C + 31) / 32;
+    const int KC = (K + CSP_KCH - 1) / CSP_KCH;
+    const int npl = planes_for(*wmax);
+    const uint32_t off = 1u << (npl - 1);
+    const int64_t units = N * KC;
+    const int64_t u0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / step;
+    const int64_t us = ((int64_t)gridDim.x * blockDim.x) / step;
+    for (int64_t u = u0; u < units; u += us) {
+        // consecutive units: consecutive samples of the same classes
+        const int64_t n = u % N;
+        const int k0 = (int)(u / N) * CSP_KCH;
+        const int kn = min(CSP_KCH, K - k0);
+        uint32_t acc[CSP_KCH];
+#pragma unroll
+        for (int j = 0; j < CSP_KCH; ++j) acc[j] = 0u;
+        uint32_t nf = 0u;
+        const uint32_t *fr = fired + n * CWn;
+        for (int wd = lane; wd < CWn; wd += step) {
+            const uint32_t f = fr[wd] & keep[wd];
+            if (!f) continue;
+            nf += (uint32_t)__popc(f);
+            const uint32_t *pl = planes + ((int64_t)wd * K + k0) * 32;
+#pragma unroll
+            for (int j = 0; j < CSP_KCH; ++j) {
+                if (j < kn) {
+                    uint32_t a = 0u;
+                    for (int b = 0; b < npl; ++b) a += (uint32_t)__popc(f & pl[j * 32 + b]) << b;
+                    acc[j] += a;
+                }
+            }
+        }
+        if (WARP) nf = __reduce_add_sync(0xFFFFFFFFu, nf);
+#pragma unroll
+        for (int j = 0; j < CSP_KCH; ++j) {
+            if (j < kn) {
+                const uint32_t t = WARP ? __reduce_add_sync(0xFFFFFFFFu, acc[j]) : acc[j];
+                if (lane == 0) cs[n * K + k0 + j] = (int32_t)(t - off * nf) + (bias ? bias[k0 + j] : 0);
+            }
+        }
+    }
+}
+
+uint64_t cs_planes_bytes(const ytm_config *cfg) {
+    const uint64_t CW = cdiv(cfg->clause_count, 32);
+    return 256 + align_up(CW * cfg->n_classes * 32 * 4, 256) + align_up(CW * 4, 256);
+}
+
+// cs [N][K] = bias + class sums of the fired bits (all classes, or only each
+// clause's own class when own_class); scratch: cs_planes_bytes(cfg).
+static ytm_status launch_cs_planes(const uint32_t *fired, const int32_t *ninc, const int32_t *w, const int32_t *bias,
+                                   const ytm_config *cfg, int64_t N, int own_class, int32_t *cs, void *scratch,
+                                   cudaStream_t st) {
+    const int C = cfg->clause_count, K = cfg->n_classes;
+    const int64_t CW = (int64_t)cdiv(C, 32);
+    char *p = (char *)scratch;
+    int32_t *wmax = (int32_t *)p;
+    uint32_t *planes = (uint32_t *)(p + 256);
+    uint32_t *keep = (uint32_t *)(p + 256 + align_up(CW * K * 32 * 4, 256));
+    ytm_status rc;
+    if ((rc = cuda_check(cudaMemsetAsync(wmax, 0, 4, st), "memset"))) return rc;
+    k_wmax<<<grid1((int64_t)C * K), 256, 0, st>>>(w, C, K, own_class, cfg->clause_lo, cfg->clauses_per_class, wmax);
+    if ((rc = launch_check("weight range"))) return rc;
+    k_wplanes<<<grid1(CW * K * 32), 256, 0, st>>>(w, ninc, C, K, own_class, cfg->clause_lo, cfg->clauses_per_class,
+                                                   wmax, planes, keep);
+    if ((rc = launch_check("weight planes"))) return rc;
+    const int64_t units = N * (int64_t)cdiv(K, CSP_KCH);
+    const int sms = sm_count();
+    if (units < (int64_t)sms * 32) {
+        k_cs_planes<true><<<(unsigned)std::min<int64_t>(cdiv(units * 32, 256), (int64_t)sms * 64), 256, 0, st>>>(
+            fired, keep, planes, wmax, bias, C, K, N, cs);
+    } else {
+        k_cs_planes<false><<<(unsigned)std::min<int64_t>(cdiv(units, 256), (int64_t)sms * 64), 256, 0, st>>>(
+            fired, keep, planes, wmax, bias, C, K, N, cs);
+    }
+    return launch_check("class sums");
+}
+
 __global__ void k_expand(const uint32_t *__restrict__ fired, int64_t N, int C, uint32_t *__restrict__ out) {
     const int CWn = (C + 31) / 32;
     int64_t total = N * C;
@@ -225,12 +376,6 @@ __global__ void k_pick(ytm_config cfg, const uint32_t *__restrict__ mbits, const
     }
 }
 
-static unsigned grid1(int64_t threads) {
-    int64_t b = (int64_t)cdiv(threads, 256);
-    int64_t cap = (int64_t)sm_count() * 32;
-    if (b > cap) b = cap;
-    return (unsigned)(b < 1 ? 1 : b);
-}
 
 }  // namespace ytm
 
@@ -255,9 +400,7 @@ ytm_status ytm_infer(const ytm_config *cfg, const uint32_t *state, const int32_t
     if ((rc = launch_ninc(cfg, state, ninc, st))) return rc;
     if ((rc = cuda_check(cudaMemsetAsync(fired, 0, (size_t)N * cdiv(C, 32) * 4, st), "memset"))) return rc;
     if ((rc = launch_match<MODE_ANY>(inc, lits, N * P, C, W, P, fired, st))) return rc;
-    k_cs_init<<<grid1(N * cfg->n_classes), 256, 0, st>>>(cs, bias, N, cfg->n_classes);
-    if ((rc = launch_check("cs init"))) return rc;
-    return launch_class_sums(fired, ninc, weights, cfg, N, 0, cs, st);
+    return launch_cs_planes(fired, ninc, weights, bias, cfg, N, 0, cs, ws + l.total, st);
 }
 
 ytm_status ytm_infer_include(const ytm_config *cfg, const uint32_t *inc, const int32_t *weights,
@@ -278,9 +421,7 @@ ytm_status ytm_infer_include(const ytm_config *cfg, const uint32_t *inc, const i
     if ((rc = launch_check("include counts"))) return rc;
     if ((rc = cuda_check(cudaMemsetAsync(fired, 0, (size_t)N * cdiv(C, 32) * 4, st), "memset"))) return rc;
     if ((rc = launch_match<MODE_ANY>(inc, lits, N * P, C, W, P, fired, st))) return rc;
-    k_cs_init<<<grid1(N * cfg->n_classes), 256, 0, st>>>(cs, bias, N, cfg->n_classes);
-    if ((rc = launch_check("cs init"))) return rc;
-    return launch_class_sums(fired, ninc, weights, cfg, N, 0, cs, st);
+    return launch_cs_planes(fired, ninc, weights, bias, cfg, N, 0, cs, ws + l.total, st);
 }
 
 ytm_status ytm_transform(const ytm_config *cfg, const uint32_t *state, const uint32_t *lits, int64_t N,
@@ -337,10 +478,8 @@ ytm_status ytm_train_eval(const ytm_config *cfg, const uint32_t *state, const in
     if ((rc = launch_match<MODE_PBITS>(inc, lits, (int64_t)B * P, C, W, P, mbits, st))) return rc;
     k_pick<<<grid1((int64_t)B * C), 256, 0, st>>>(*cfg, mbits, drop, B, t0, sel, fired, patch_w);
     if ((rc = launch_check("patch pick"))) return rc;
-    k_cs_init<<<grid1((int64_t)B * cfg->n_classes), 256, 0, st>>>(cs, add_bias ? bias : nullptr, B,
-                                                                    cfg->n_classes);
-    if ((rc = launch_check("cs init"))) return rc;
-    return launch_class_sums(fired, nullptr, weights, cfg, B, cfg->coalesced ? 0 : 1, cs, st);
+    return launch_cs_planes(fired, nullptr, weights, add_bias ? bias : nullptr, cfg, B, cfg->coalesced ? 0 : 1, cs,
+                            ws + l.total, st);
 }
 
 ytm_status ytm_train_selection(const ytm_config *cfg, int32_t B, const void *workspace, int32_t *sel,
