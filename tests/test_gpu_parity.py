@@ -233,3 +233,29 @@ def test_fused_batch1_matches_oracle(case):
         np.testing.assert_array_equal(host(e.weights), w)
         np.testing.assert_array_equal(host(e.patch_w), pw)
     assert not np.array_equal(ta, o.init_state())
+
+
+@pytest.mark.parametrize("path", ["batch", "fused"])
+def test_sample_counter_crossing_2_32(path):
+    """Decisions key on the sample counter's high word: batches whose samples
+    straddle t = 2^32 must match the oracle too."""
+    kw = dict(number_of_clauses_per_class=30, T=20, s=4.0, dim=(40, 1, 1), n_classes=4)
+    seed = 77
+    o = O.Oracle(**oracle_kwargs(kw, seed))
+    e = engine_for(kw, seed)
+    rng = np.random.default_rng(3)
+    X = (rng.random((12, 40)) < 0.4).astype(np.uint32)
+    Y = O.encode_Y_multiclass(rng.integers(0, 4, 12), 4, 20)
+    lits_h = o.encode(X)
+    lits, Yd = dev(lits_h), dev(Y, np.int32)
+    ta, w, pw = o.init_state(), o.init_weights(), np.zeros((o.C, o.P), np.int32)
+    t0 = 2 ** 32 - 5
+    if path == "batch":
+        o.train_batch(ta, w, pw, lits_h, Y, t0)
+        cs = e.train_eval(lits, t0, None, add_bias=True)
+        e.train_update(cs, Yd, lits, t0, None)
+    else:
+        o.fit(ta, w, pw, lits_h, Y, t0, batch_size=1)
+        e.train_fit_b1(lits, Yd, t0, None)
+    np.testing.assert_array_equal(e.get_ta_state(), ta)
+    np.testing.assert_array_equal(host(e.weights), w)

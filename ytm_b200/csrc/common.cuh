@@ -69,6 +69,50 @@ __device__ __forceinline__ u32x4 draw(uint64_t seed, uint32_t clause, uint64_t t
                      (uint32_t)(seed >> 32) ^ (uint32_t)(t >> 32));
 }
 
+// Round keys of one (seed, sample-counter high word): the Weyl schedule
+// k_r = k_0 + r * constant, computed once on the host and passed as a kernel
+// parameter, so the rounds read their keys from the constant bank.
+struct RoundKeys {
+    uint32_t a[10], b[10];
+};
+
+inline RoundKeys round_keys(uint64_t seed, uint32_t t_hi) {
+    RoundKeys k;
+    uint32_t a = (uint32_t)seed, b = (uint32_t)(seed >> 32) ^ t_hi;
+    for (int r = 0; r < 10; ++r) {
+        k.a[r] = a;
+        k.b[r] = b;
+        a += 0x9E3779B9u;
+        b += 0xBB67AE85u;
+    }
+    return k;
+}
+
+template <int R>
+__device__ __forceinline__ u32x4 philox_rk(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3,
+                                           const RoundKeys &rk) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        uint32_t lo0 = 0xD2511F53u * c0, hi0 = __umulhi(0xD2511F53u, c0);
+        uint32_t lo1 = 0xCD9E8D57u * c2, hi1 = __umulhi(0xCD9E8D57u, c2);
+        uint32_t n0 = hi1 ^ c1 ^ rk.a[r];
+        uint32_t n2 = hi0 ^ c3 ^ rk.b[r];
+        c0 = n0;
+        c1 = lo1;
+        c2 = n2;
+        c3 = lo0;
+    }
+    return {c0, c1, c2, c3};
+}
+
+// draw() with precomputed round keys (valid for samples t whose high word is
+// the one the keys were made for).
+template <int R = 10>
+__device__ __forceinline__ u32x4 draw_rk(const RoundKeys &rk, uint32_t clause, uint64_t t, uint32_t sub,
+                                         uint32_t tag, uint32_t k) {
+    return philox_rk<R>(clause, (uint32_t)t, sub, tag | (k << 2), rk);
+}
+
 // Bernoulli(thr/4096) bits for the 32 literals of word w of clause g in the
 // feedback for class k of sample t: literal j is set iff the 12-bit number
 // whose bit 11-i is bit j of random word i is below thr; three Philox4x32-7
@@ -82,6 +126,30 @@ __device__ __forceinline__ uint32_t smask_word(uint64_t seed, uint32_t thr, uint
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
         u32x4 r = draw<7>(seed, g, t, w * 4u + (uint32_t)j, TAG_SMASK, k);
+        uint32_t R[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            int bit = 11 - (4 * j + i);
+            if ((thr >> bit) & 1u) {
+                lt |= eq & ~R[i];
+                eq &= R[i];
+            } else {
+                eq &= ~R[i];
+            }
+        }
+    }
+    return lt;
+}
+
+// smask_word with precomputed round keys.
+__device__ __forceinline__ uint32_t smask_word_rk(const RoundKeys &rk, uint32_t thr, uint32_t g, uint64_t t,
+                                                  uint32_t k, uint32_t w) {
+    if (thr >= 4096u) return 0xFFFFFFFFu;
+    if (thr == 0u) return 0u;
+    uint32_t lt = 0u, eq = 0xFFFFFFFFu;
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+        u32x4 r = draw_rk<7>(rk, g, t, w * 4u + (uint32_t)j, TAG_SMASK, k);
         uint32_t R[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {

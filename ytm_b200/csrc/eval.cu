@@ -7,7 +7,7 @@
 // the last word is implied because include bits beyond L are never set.
 //
 // The match kernel treats (sample, patch) rows x clauses like a GEMM tile:
-// 64 rows x 64 clauses per CTA, 16-word K-chunks staged in shared memory, 4x4
+// 64 rows x 64 clauses per CTA, 32-word K-chunks staged in shared memory, 4x4
 // (row, clause) pairs per thread held in registers.  Its epilogue writes one of
 // three outputs: any-patch fired bits, per-patch match bits, or u32 per
 // (sample, clause, patch).  Class sums are then a sparse sum of weight rows
@@ -21,7 +21,7 @@ __global__ void k_ninc(int C, int W, const uint32_t *__restrict__ inc, int32_t *
 
 enum { MODE_ANY = 0, MODE_PBITS = 1, MODE_PATCHWISE = 2 };
 
-constexpr int RT = 64, CT = 64, KW = 16, XS = RT + 4;
+constexpr int RT = 64, CT = 64, KW = 32, XS = RT + 4;
 
 template <int MODE>
 __global__ void __launch_bounds__(256) k_match(const uint32_t *__restrict__ inc, const uint32_t *__restrict__ lits,
@@ -38,8 +38,9 @@ __global__ void __launch_bounds__(256) k_match(const uint32_t *__restrict__ inc,
         for (int j = 0; j < 4; ++j) v[i][j] = 0u;
 
     for (int w0 = 0; w0 < W; w0 += KW) {
+        const int kwn = min(KW, W - w0);  // no work on words past W
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < (RT * KW) / 256; ++q) {
             int idx = tid + q * 256;
             int r = idx / KW, kw = idx % KW;
             int w = w0 + kw;
@@ -49,8 +50,8 @@ __global__ void __launch_bounds__(256) k_match(const uint32_t *__restrict__ inc,
             is[kw][r] = (c < C && w < W) ? __ldg(&inc[(int64_t)c * W + w]) : 0u;
         }
         __syncthreads();
-#pragma unroll
-        for (int kw = 0; kw < KW; ++kw) {
+#pragma unroll 8
+        for (int kw = 0; kw < kwn; ++kw) {
             uint4 xv = *reinterpret_cast<const uint4 *>(&xs[kw][ty * 4]);
             uint4 iv = *reinterpret_cast<const uint4 *>(&is[kw][tx * 4]);
             uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w};

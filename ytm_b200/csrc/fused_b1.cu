@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     ytm_config cfg, uint32_t *__restrict__ state, int32_t *__restrict__ weights, const int32_t *__restrict__ bias,
     const uint32_t *__restrict__ drop, const uint32_t *__restrict__ lits, const int32_t *__restrict__ Y, int64_t i,
     int64_t N, uint64_t t0, int do_update, int32_t *__restrict__ cs_ring, int32_t *__restrict__ sel_pp,
-    int32_t *__restrict__ ninc_ws, int32_t *__restrict__ patch_w) {
+    int32_t *__restrict__ ninc_ws, int32_t *__restrict__ patch_w, const RoundKeys rk) {
     extern __shared__ __align__(16) unsigned char smraw[];
     // Programmatic dependent launch: let launch i+1 be scheduled now, and
     // wait here until launch i-1 has completed and its writes are visible.
@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
                 uint64_t th = thr_s[k];
                 const int target = (th >> 63) ? -1 : 1;
                 th &= ~(1ull << 63);
-                u32x4 r = draw(cfg.seed, g, t, 0, TAG_CLASS, (uint32_t)k);
+                u32x4 r = draw_rk(rk, g, t, 0, TAG_CLASS, (uint32_t)k);
                 if (target == -1 && !((uint64_t)r.x < cfg.q_threshold)) continue;  // kernel.cu:573
                 if (!((uint64_t)r.y < th)) continue;                                // kernel.cu:582
                 int32_t *lw = &weights[(int64_t)c * K + k];
@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
                             cand = vm & ctr.ne(zero_s);
                         }
                         if (cand)
-                            ctr.dec(cand & smask_word(cfg.seed, cfg.s_threshold12, g, t,
+                            ctr.dec(cand & smask_word_rk(rk, cfg.s_threshold12, g, t,
                                                       (uint32_t)(k0 + kb * 32 + b), (uint32_t)w));
                     }
                 }
@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
             __syncwarp();
             int32_t sp = -1;
             if (count > 0) {
-                const uint32_t r = draw(cfg.seed, g, t_next, 0, TAG_PATCH, 0).x;
+                const uint32_t r = draw(cfg.seed, g, t_next, 0, TAG_PATCH, 0).x;  // t_next may change the high word
                 uint32_t idx = (uint32_t)(((uint64_t)r * (uint64_t)count) >> 32);
                 for (int jw = 0; jw < PW; ++jw) {
                     uint32_t word = mb[jw];
@@ -368,8 +368,9 @@ extern "C" ytm_status ytm_train_fit_b1(const ytm_config *cfg, uint32_t *state, i
         for (int64_t i = -1; i < N; ++i) {  // i = -1: the prologue evaluating sample 0
             const int64_t ii = i < 0 ? 0 : i;
             const int upd = i < 0 ? 0 : 1;
+            const RoundKeys rk = round_keys(c.seed, (uint32_t)((t0 + (uint64_t)ii) >> 32));  // keys of sample ii
             if ((rc = cuda_check(cudaLaunchKernelEx(&lc, k_fused_b1<NB>, c, state, weights, bias, drop, lits, Y, ii, N,
-                                                    t0, upd, cs_ring, sel, ninc, patch_w),
+                                                    t0, upd, cs_ring, sel, ninc, patch_w, rk),
                                  "fused b1 launch")))
                 return rc;
         }

@@ -39,12 +39,15 @@ __global__ void k_thresholds(const int32_t *__restrict__ cs, const int32_t *__re
 enum : uint32_t { EV_NONE = 0, EV_T1A = 1, EV_T1B = 2, EV_T2 = 3 };
 
 template <int NB>
-__global__ void __launch_bounds__(256) k_update(ytm_config cfg, uint32_t *__restrict__ state,
+#ifndef YTM_UPD_MINB
+#define YTM_UPD_MINB 4  // 64 registers: measured fastest (no spills)
+#endif
+__global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, uint32_t *__restrict__ state,
                                                 int32_t *__restrict__ weights, const uint64_t *__restrict__ thr,
                                                 const uint32_t *__restrict__ drop,
                                                 const uint32_t *__restrict__ lits, int B, uint64_t t0,
                                                 const int32_t *__restrict__ sel, const int32_t *__restrict__ ninc,
-                                                int BC) {
+                                                int BC, const RoundKeys rk, int rk_ok) {
     extern __shared__ __align__(16) unsigned char smraw[];
     const int C = cfg.clause_count, W = cfg.words, K = cfg.n_classes, P = cfg.patches;
     const int c = blockIdx.x;
@@ -76,7 +79,8 @@ __global__ void __launch_bounds__(256) k_update(ytm_config cfg, uint32_t *__rest
             uint64_t th = thr[(int64_t)b * K + k];
             const bool neg = (th >> 63) != 0;
             th &= ~(1ull << 63);
-            u32x4 r = draw(cfg.seed, g, t0 + (uint64_t)b, 0, TAG_CLASS, (uint32_t)k);
+            const uint64_t tb = t0 + (uint64_t)b;
+            u32x4 r = rk_ok ? draw_rk(rk, g, tb, 0, TAG_CLASS, (uint32_t)k) : draw(cfg.seed, g, tb, 0, TAG_CLASS, (uint32_t)k);
             const bool pass = !(neg && !((uint64_t)r.x < cfg.q_threshold));  // kernel.cu:573
             evt[idx] = (pass && (uint64_t)r.y < th) ? (neg ? 2 : 1) : 0;      // kernel.cu:582
         }
@@ -159,7 +163,9 @@ __global__ void __launch_bounds__(256) k_update(ytm_config cfg, uint32_t *__rest
                         } else {  // type1b_fb, kernel.cu:453-470
                             cand = vm & ctr.ne(zero_s);
                         }
-                        if (cand) ctr.dec(cand & smask_word(cfg.seed, cfg.s_threshold12, g, t, (uint32_t)k, (uint32_t)w));
+                        if (cand)
+                            ctr.dec(cand & (rk_ok ? smask_word_rk(rk, cfg.s_threshold12, g, t, (uint32_t)k, (uint32_t)w)
+                                                  : smask_word(cfg.seed, cfg.s_threshold12, g, t, (uint32_t)k, (uint32_t)w)));
                     }
                 }
 #pragma unroll
@@ -206,6 +212,9 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
     while (BC > 32 && update_smem(nk, BC) > 32 * 1024) BC -= 32;
     const size_t smem = update_smem(nk, BC);
     if (smem > 227 * 1024) return fail(YTM_ERR_UNSUPPORTED, "too many classes for the feedback kernel");
+    // round keys for the batch's samples when they share the counter's high word
+    const RoundKeys rk = round_keys(cfg->seed, (uint32_t)(t0 >> 32));
+    const int rk_ok = (t0 >> 32) == ((t0 + (uint64_t)B - 1) >> 32);
     const int W = cfg->words;
     const int tpb = W <= 32 ? 32 : (W <= 64 ? 64 : (W <= 128 ? 128 : 256));
     YTM_DISPATCH_PLANES(cfg->planes, {
@@ -215,7 +224,7 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
                 return rc;
         }
         k_update<NB><<<cfg->clause_count, tpb, smem, st>>>(*cfg, state, weights, thr, drop, lits, B, t0, sel, ninc,
-                                                           BC);
+                                                           BC, rk, rk_ok);
     });
     return launch_check("feedback");
 }
