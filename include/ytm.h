@@ -82,6 +82,13 @@ typedef struct ytm_config {
     /* clause shard held by this process */
     int32_t clause_lo;         /* first global clause index                     */
     int32_t clause_count;      /* clauses held (C above)                        */
+    /* rule variants of the reference's CPU TM, pytm/base.py (0 = cutm rules;
+     * set after ytm_config_init) */
+    int32_t one_negative;      /* per sample: feedback for the true class, then
+                                  for ONE uniformly drawn other class, no
+                                  Q-selection (pytm/base.py:139-143)           */
+    int32_t count_empty;       /* inference counts clauses without includes
+                                  (pytm/base.py:59-67)                         */
 } ytm_config;
 
 /* Fill *cfg.  Arguments mirror BaseTM.__init__ (base.py:42-92) and its defaults

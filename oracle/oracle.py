@@ -50,6 +50,7 @@ class OrcCfg(ct.Structure):
         ("banks", ct.c_int32), ("C", ct.c_int32), ("L", ct.c_int32), ("W", ct.c_int32), ("P", ct.c_int32),
         ("max_state", ct.c_int32), ("half_state", ct.c_int32), ("state_top", ct.c_int32),
         ("s_thr12", ct.c_uint32), ("q_thr", ct.c_uint64),
+        ("one_negative", ct.c_int32), ("count_empty", ct.c_int32),
     ]
 
 
@@ -64,6 +65,7 @@ def _declare(L):
                                ct.c_double, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _U64]
     L.orc_cfg_init.restype = ct.c_int
     L.orc_set_threads.argtypes = [ct.c_int]
+    L.orc_cfg_set_modes.argtypes = [ct.POINTER(OrcCfg), ct.c_int32, ct.c_int32]
     L.orc_get_threads.restype = ct.c_int
     L.orc_philox4x32_10.argtypes = [_P, _P, _P]
     L.orc_philox4x32.argtypes = [_P, _P, ct.c_int, _P]
@@ -124,7 +126,7 @@ class Oracle:
     def __init__(self, number_of_clauses_per_class, T, s, dim, n_classes, q=1.0, patch_dim=None,
                  number_of_ta_states=256, max_included_literals=None, append_negated=True,
                  init_neg_weights=True, negative_polarity=True, encode_loc=True, coalesced=True,
-                 seed=0):
+                 seed=0, one_negative=False, count_empty=False):
         if patch_dim is None:
             patch_dim = (dim[0], dim[1])
         self.cfg = OrcCfg()
@@ -136,6 +138,7 @@ class Oracle:
                                 int(encode_loc), int(coalesced), int(seed) & (2**64 - 1))
         if rc != 0:
             raise ValueError("invalid oracle configuration")
+        lib().orc_cfg_set_modes(ct.byref(self.cfg), int(bool(one_negative)), int(bool(count_empty)))
         c = self.cfg
         self.C, self.K, self.L, self.W, self.P = c.C, c.K, c.L, c.W, c.P
         self.half_state, self.state_top = c.half_state, c.state_top

@@ -33,6 +33,7 @@ class RefKernels:
         L.ref_transform.argtypes = [_P, _P, ct.c_int, ct.c_int, _P]
         L.ref_init_weights.argtypes = [ct.c_ulonglong, _P]
         L.ref_train_step.argtypes = [_P, _P, _P, _P, _P, ct.c_int, ct.c_int, _P, ct.c_ulonglong, _P, _P]
+        L.ref_fit.argtypes = [_P, _P, _P, _P, _P, ct.c_int, ct.c_ulonglong]
         self.L = L
         s = np.zeros(5, np.int32)
         L.ref_sizes(_ptr(s))
@@ -93,3 +94,12 @@ class RefKernels:
         self._ok(self.L.ref_train_step(_ptr(ta), _ptr(w), _ptr(patch_w), _ptr(lits), _ptr(Y), lits.shape[0], int(e),
                                        _ptr(d), seed, _ptr(sel), _ptr(cs)), "train_step")
         return sel, cs
+
+    def fit(self, ta, w, patch_w, lits, Y, seed=0):
+        """One epoch of the reference's _fit loop on the device; ta, w, patch_w
+        updated in place."""
+        for a, dt in ((ta, np.uint32), (w, np.float32), (patch_w, np.int32)):
+            assert a.flags.c_contiguous and a.dtype == dt
+        lits = np.ascontiguousarray(lits, np.uint32)
+        Y = np.ascontiguousarray(Y, np.int32)
+        self._ok(self.L.ref_fit(_ptr(ta), _ptr(w), _ptr(patch_w), _ptr(lits), _ptr(Y), lits.shape[0], seed), "fit")

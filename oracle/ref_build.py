@@ -46,6 +46,9 @@ SHAPES = {
     "tr_coal": dict(number_of_clauses_per_class=24, T=1, s=1.0, dim=(40, 1, 1), n_classes=4, q=3.0),
     "tr_conv": dict(number_of_clauses_per_class=16, T=1, s=1.0, dim=(6, 6, 1), n_classes=3, q=2.0,
                     patch_dim=(4, 4)),
+    # accuracy-parity shapes (configuration 1 / 2 rules, fewer clauses)
+    "acc_vanilla": dict(number_of_clauses_per_class=50, T=15, s=3.9, dim=(28, 28, 1), n_classes=10, coalesced=False),
+    "acc_coal": dict(number_of_clauses_per_class=400, T=100, s=5.0, dim=(28, 28, 1), n_classes=10),
     "tr_maxinc": dict(number_of_clauses_per_class=24, T=1, s=1.0, dim=(40, 1, 1), n_classes=4, q=3.0,
                       max_included_literals=3, negative_polarity=False),
 }

@@ -193,4 +193,49 @@ int ref_train_step(uint32_t *ta, float *w, int32_t *patch_w, const uint32_t *lit
     return rc;
 }
 
+// One epoch of _fit (base.py:266-359) over samples 0..N-1 in order, all on the
+// device: per sample pack_clauses, fast_eval, class_sum <- bias,
+// select_active, clause_update, with one curand state per thread seeded once.
+int ref_fit(uint32_t *ta, float *w, int32_t *patch_w, const uint32_t *lits, const int32_t *Y, int N,
+            unsigned long long seed) {
+    const int bs = 16;
+    dim3 gc, bc, gp, bp;
+    geometry(CLAUSES, bs, &gc, &bc);
+    geometry((long long)CLAUSES * PATCHES, bs, &gp, &bp);
+    int n = gc.x * bc.x;
+    curandState *rng = nullptr;
+    cudaMalloc(&rng, sizeof(curandState) * n);
+    seed_rng<<<(n + 127) / 128, 128>>>(rng, seed, n);
+    uint32_t *dT = dev(ta, (size_t)CLAUSES * LITERALS);
+    float *dW = dev(w, (size_t)CLAUSES * CLASSES);
+    int *dPW = dev(patch_w, (size_t)CLAUSES * PATCHES);
+    float *dBias = dev<float>(nullptr, CLASSES);
+    uint32_t *dX = dev(lits, (size_t)N * PATCHES * NUM_LITERAL_CHUNKS);
+    int *dY = dev(Y, (size_t)N * CLASSES);
+    double ones[CLASSES];
+    for (int k = 0; k < CLASSES; ++k) ones[k] = 1.0;
+    double *dTrue = dev(ones, CLASSES), *dFalse = dev(ones, CLASSES);
+    uint32_t *dDrop = dev<uint32_t>(nullptr, CLAUSES);
+    uint32_t *dPk = dev<uint32_t>(nullptr, (size_t)CLAUSES * NUM_LITERAL_CHUNKS);
+    float *dCS = dev<float>(nullptr, CLASSES);
+    uint32_t *dCO = dev<uint32_t>(nullptr, (size_t)CLAUSES * PATCHES);
+    int *dSel = dev<int>(nullptr, CLAUSES);
+    int *dN = dev<int>(nullptr, CLAUSES);
+    for (int e = 0; e < N; ++e) {
+        pack_clauses<<<gc, bc>>>(dT, dPk, dN);
+        fast_eval<<<gp, bp>>>(dPk, dN, dDrop, dX, dCO, e);
+        cudaMemcpyAsync(dCS, dBias, CLASSES * sizeof(float), cudaMemcpyDeviceToDevice);
+        select_active<<<gc, bc>>>(rng, dW, dCO, dPW, dSel, dCS);
+        clause_update<<<gc, bc>>>(rng, dT, dW, dBias, dCS, dSel, dN, dTrue, dFalse, dDrop, dX, dY, e, 0, 0);
+    }
+    int rc = status();
+    back(ta, dT, (size_t)CLAUSES * LITERALS);
+    back(w, dW, (size_t)CLAUSES * CLASSES);
+    back(patch_w, dPW, (size_t)CLAUSES * PATCHES);
+    cudaFree(rng); cudaFree(dT); cudaFree(dW); cudaFree(dPW); cudaFree(dBias); cudaFree(dX); cudaFree(dY);
+    cudaFree(dTrue); cudaFree(dFalse); cudaFree(dDrop); cudaFree(dPk); cudaFree(dCS); cudaFree(dCO);
+    cudaFree(dSel); cudaFree(dN);
+    return rc;
+}
+
 }  // extern "C"

@@ -45,7 +45,15 @@ typedef struct orc_cfg {
     int32_t max_state, half_state, state_top;
     uint32_t s_thr12;
     uint64_t q_thr;
+    /* rule variants of the reference's CPU TM, pytm/base.py (0 = cutm rules) */
+    int32_t one_negative; /* one uniformly chosen negative class per sample, true class first (base.py:139-143) */
+    int32_t count_empty;  /* inference counts clauses without includes (base.py:59-67) */
 } orc_cfg;
+
+void orc_cfg_set_modes(orc_cfg *c, int32_t one_negative, int32_t count_empty) {
+    c->one_negative = one_negative;
+    c->count_empty = count_empty;
+}
 
 /* ---------------------------------------------------------------- sizes */
 
@@ -286,7 +294,7 @@ void orc_infer(const orc_cfg *c, const uint32_t *ta, const int32_t *weights, con
         int64_t *a = K <= 1024 ? acc : (int64_t *)malloc((size_t)K * 8);
         for (int k = 0; k < K; ++k) a[k] = bias ? bias[k] : 0;
         for (int cl = 0; cl < C; ++cl) {
-            if (ninc[cl] == 0) continue; /* kernel.cu:328 */
+            if (ninc[cl] == 0 && !c->count_empty) continue; /* kernel.cu:328 */
             int out = 0;
             for (int p = 0; p < P && !out; ++p)
                 out = match(c, packed + (int64_t)cl * W, lits + (e * P + p) * W);
@@ -462,6 +470,25 @@ static void type2(const orc_cfg *c, uint32_t *st, const uint32_t *x) {
     }
 }
 
+/* pytm's sample-level pick (pytm/base.py:139-141): the true class is the one
+ * whose target is positive; the other class is drawn uniformly among the rest
+ * from the counter (clause 0xFFFFFFFF, t, 1, CLASS). */
+static void orc_pair(const orc_cfg *c, const int32_t *Yrow, uint64_t t, int *kt, int *ko) {
+    const int K = c->K;
+    int y = -1;
+    for (int k = 0; k < K; ++k)
+        if (Yrow[k] > 0) { y = k; break; }
+    uint32_t r[4];
+    draw(c, 0xFFFFFFFFu, t, 1, TAG_CLASS, 0, r);
+    if (y < 0) {
+        *ko = (int)(((uint64_t)r[0] * (uint64_t)K) >> 32);
+    } else {
+        int idx = K > 1 ? (int)(((uint64_t)r[0] * (uint64_t)(K - 1)) >> 32) : 0;
+        *ko = K > 1 ? (idx < y ? idx : idx + 1) : -1;
+    }
+    *kt = y;
+}
+
 /* Part 2 of a batch: clause_update, kernel.cu:531-613, for every clause of the
  * shard and every sample of the batch in order.  cs [B][K] are the summed class
  * sums, Y [B][K] the +-T targets, sel [B][nc] and ninc [nc] from part 1. */
@@ -481,13 +508,22 @@ void orc_train_update(const orc_cfg *c, int32_t lo, int32_t nc, uint32_t *ta, in
             const uint32_t *x = fired ? lits + ((int64_t)b * P + sp) * W : NULL;
             int k0 = c->coalesced ? 0 : clause_class(c, (int32_t)g);
             int k1 = c->coalesced ? K : k0 + 1;
-            for (int k = k0; k < k1; ++k) { /* kernel.cu:563-568 */
+            int seq[2], nseq = 0;
+            if (c->one_negative) { /* the true class, then one other class */
+                int kt, ko;
+                orc_pair(c, Y + (int64_t)b * K, t, &kt, &ko);
+                if (kt >= k0 && kt < k1) seq[nseq++] = kt;
+                if (ko >= k0 && ko < k1) seq[nseq++] = ko;
+            }
+            int nk = c->one_negative ? nseq : k1 - k0;
+            for (int kq = 0; kq < nk; ++kq) { /* kernel.cu:563-568 */
+                const int k = c->one_negative ? seq[kq] : k0 + kq;
                 int32_t v = clip_cs(c, cs[(int64_t)b * K + k]);
                 int32_t y = Y[(int64_t)b * K + k];
                 int target = 1 - 2 * (v > y); /* kernel.cu:571 */
                 uint32_t r[4];
                 draw(c, g, t, 0, TAG_CLASS, (uint32_t)k, r);
-                if (target == -1 && !((uint64_t)r[0] < c->q_thr)) continue; /* kernel.cu:573 */
+                if (!c->one_negative && target == -1 && !((uint64_t)r[0] < c->q_thr)) continue; /* kernel.cu:573 */
                 int upd = (uint64_t)r[1] < orc_update_threshold(y, v);   /* kernel.cu:582 */
                 int32_t *lw = &w[(int64_t)i * K + k];
                 int sign = (*lw >= 0) - (*lw < 0);

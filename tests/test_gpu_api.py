@@ -149,3 +149,31 @@ def test_thermometer_encoding_on_device(levels, ch, patch):
     lits = tm.encode_thermometer(imgs, levels, on_device=True)
     tm.fit(lits, np.array([0, 1, 0, 1, 1, 0, 1]), is_X_encoded=True)
     assert tm.predict(lits, is_X_encoded=True)[1].shape == (7, 2)
+
+
+def test_pytm_front_end_matches_oracle_pytm_rules():
+    """ytm_b200.pytm.BaseTM follows pytm's rules (one other class per sample,
+    true class first, empty clauses counted at prediction) — checked bit for
+    bit against the oracle run in the same mode."""
+    from ytm_b200.pytm import BaseTM
+    rng = np.random.default_rng(4)
+    X = rng.random((80, 30)) < 0.4
+    y = rng.integers(0, 5, 80)
+    tm = BaseTM(n_clause=40, T=12, s=3.0, q=1.0, n_class=5, dim=(30, 1, 1), n_ta_states=64, seed=9)
+    assert tm.states.dtype == np.uint8 and (tm.states == 31).all()
+    tm.fit(X, y)
+    tm.fit(X, y, shuffle=True)
+    o = O.Oracle(number_of_clauses_per_class=40, T=12, s=3.0, dim=(30, 1, 1), n_classes=5, number_of_ta_states=63,
+                 seed=9, one_negative=True, count_empty=True)
+    ta, w, pw = o.init_state(), o.init_weights(), np.zeros((o.C, 1), np.int32)
+    lits = o.encode(X.astype(np.uint32))
+    Y = O.encode_Y_multiclass(y, 5, 12)
+    t = o.fit(ta, w, pw, lits, Y, 0)
+    iota = np.arange(80)
+    np.random.default_rng(9).shuffle(iota)
+    o.fit(ta, w, pw, lits[iota], Y[iota], t)
+    np.testing.assert_array_equal(tm.states, ta.astype(np.uint8))
+    np.testing.assert_array_equal(tm.weights, w.astype(np.float32))
+    preds, cs = tm.predict(X, return_cs=True)
+    np.testing.assert_array_equal(cs, o.infer(ta, w, lits).astype(np.float32))
+    assert (ta != 31).any()  # training moved the states

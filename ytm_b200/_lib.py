@@ -45,6 +45,7 @@ class Config(ct.Structure):
         ("state_offset", ct.c_int32), ("state_top", ct.c_int32),
         ("s_threshold12", ct.c_uint32), ("q_threshold", ct.c_uint64),
         ("clause_lo", ct.c_int32), ("clause_count", ct.c_int32),
+        ("one_negative", ct.c_int32), ("count_empty", ct.c_int32),
     ]
 
 
@@ -106,7 +107,7 @@ def check(rc: int, what: str = "") -> None:
 
 def make_config(*, clauses_per_class, T, s, dim, n_classes, q=1.0, patch_dim=None, number_of_ta_states=256,
                 max_included_literals=None, append_negated=True, init_neg_weights=True, negative_polarity=True,
-                encode_loc=True, coalesced=True, seed=0) -> Config:
+                encode_loc=True, coalesced=True, seed=0, one_negative=False, count_empty=False) -> Config:
     if patch_dim is None:
         patch_dim = (dim[0], dim[1])
     cfg = Config()
@@ -117,6 +118,8 @@ def make_config(*, clauses_per_class, T, s, dim, n_classes, q=1.0, patch_dim=Non
         int(bool(init_neg_weights)), int(bool(negative_polarity)), int(bool(encode_loc)), int(bool(coalesced)),
         int(seed) & (2 ** 64 - 1))
     check(rc, "ytm_config_init")
+    cfg.one_negative = int(bool(one_negative))
+    cfg.count_empty = int(bool(count_empty))
     return cfg
 
 

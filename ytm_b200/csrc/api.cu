@@ -50,6 +50,7 @@ TrainWs train_ws_layout(const ytm_config *cfg, int64_t B) {
     l.sel = o;   o = align_up(o + (uint64_t)B * C * 4, 256);
     l.fired = o; o = align_up(o + (uint64_t)B * CW * 4, 256);
     l.thr = o;   o = align_up(o + (uint64_t)B * K * 8, 256);
+    l.pair = o;  o = align_up(o + (uint64_t)B * 2 * 4, 256);
     l.total = o;
     return l;
 }

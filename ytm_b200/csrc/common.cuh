@@ -165,6 +165,24 @@ __device__ __forceinline__ uint32_t smask_word_rk(const RoundKeys &rk, uint32_t 
     return lt;
 }
 
+// pytm's per-sample pick (pytm/base.py:139-141): the true class (the first
+// with a positive target, -1 if none) and one other class drawn uniformly
+// among the rest from the counter (clause 0xFFFFFFFF, t, 1, CLASS).
+__device__ __forceinline__ void true_other_pair(uint64_t seed, const int32_t *Yrow, int K, uint64_t t, int *kt,
+                                                int *ko) {
+    int y = -1;
+    for (int k = 0; k < K; ++k)
+        if (Yrow[k] > 0) { y = k; break; }
+    const uint32_t r = draw(seed, 0xFFFFFFFFu, t, 1, TAG_CLASS, 0).x;
+    if (y < 0) {
+        *ko = (int)(((uint64_t)r * (uint64_t)K) >> 32);
+    } else {
+        const int idx = K > 1 ? (int)(((uint64_t)r * (uint64_t)(K - 1)) >> 32) : 0;
+        *ko = K > 1 ? (idx < y ? idx : idx + 1) : -1;
+    }
+    *kt = y;
+}
+
 // floor(p * 2^32) for the update probability p = (y - v) / (2y)
 // (reference update_probability, kernel.cu:508-529).  IEEE double division is
 // correctly rounded on host and device alike.
@@ -262,7 +280,7 @@ ytm_status check_cfg(const ytm_config *cfg);
 
 // Workspace carve-up (offsets in bytes, 256-aligned).
 struct TrainWs {
-    uint64_t ninc, mbits, sel, fired, thr, total;
+    uint64_t ninc, mbits, sel, fired, thr, pair, total;
 };
 TrainWs train_ws_layout(const ytm_config *cfg, int64_t B);
 struct InferWs {

@@ -401,7 +401,8 @@ ytm_status ytm_infer(const ytm_config *cfg, const uint32_t *state, const int32_t
     if ((rc = launch_ninc(cfg, state, ninc, st))) return rc;
     if ((rc = cuda_check(cudaMemsetAsync(fired, 0, (size_t)N * cdiv(C, 32) * 4, st), "memset"))) return rc;
     if ((rc = launch_match<MODE_ANY>(inc, lits, N * P, C, W, P, fired, st))) return rc;
-    return launch_cs_planes(fired, ninc, weights, bias, cfg, N, 0, cs, ws + l.total, st);
+    return launch_cs_planes(fired, cfg->count_empty ? nullptr : ninc, weights, bias, cfg, N, 0, cs, ws + l.total,
+                            st);
 }
 
 ytm_status ytm_infer_include(const ytm_config *cfg, const uint32_t *inc, const int32_t *weights,
@@ -422,7 +423,8 @@ ytm_status ytm_infer_include(const ytm_config *cfg, const uint32_t *inc, const i
     if ((rc = launch_check("include counts"))) return rc;
     if ((rc = cuda_check(cudaMemsetAsync(fired, 0, (size_t)N * cdiv(C, 32) * 4, st), "memset"))) return rc;
     if ((rc = launch_match<MODE_ANY>(inc, lits, N * P, C, W, P, fired, st))) return rc;
-    return launch_cs_planes(fired, ninc, weights, bias, cfg, N, 0, cs, ws + l.total, st);
+    return launch_cs_planes(fired, cfg->count_empty ? nullptr : ninc, weights, bias, cfg, N, 0, cs, ws + l.total,
+                            st);
 }
 
 ytm_status ytm_transform(const ytm_config *cfg, const uint32_t *state, const uint32_t *lits, int64_t N,
@@ -570,5 +572,5 @@ extern "C" ytm_status ytm_infer_noalloc(const ytm_config *cfg, const uint32_t *s
     if ((rc = launch_match<MODE_ANY>(inc, lits, N * P, C, W, P, fired, st))) return rc;
     k_cs_init<<<grid1(N * cfg->n_classes), 256, 0, st>>>(cs, bias, N, cfg->n_classes);
     if ((rc = launch_check("cs init"))) return rc;
-    return launch_class_sums(fired, ninc, weights, cfg, N, 0, cs, st);
+    return launch_class_sums(fired, cfg->count_empty ? nullptr : ninc, weights, cfg, N, 0, cs, st);
 }

@@ -91,6 +91,9 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     }
     if (blockIdx.x == 0 && do_update)
         for (int k = threadIdx.x; k < K; k += blockDim.x) cs_ring[((i + 2) % 3) * K + k] = 0;
+    __shared__ int pair_s[2];  // one_negative: the true class and the other class of sample i
+    if (threadIdx.x == 0 && do_update && cfg.one_negative)
+        true_other_pair(cfg.seed, Y + i * K, K, t, &pair_s[0], &pair_s[1]);
     __syncthreads();
 
     // ---- 1. decisions of sample i: one clause per thread
@@ -109,7 +112,9 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
                 const int target = (th >> 63) ? -1 : 1;
                 th &= ~(1ull << 63);
                 u32x4 r = draw_rk(rk, g, t, 0, TAG_CLASS, (uint32_t)k);
-                if (target == -1 && !((uint64_t)r.x < cfg.q_threshold)) continue;  // kernel.cu:573
+                if (cfg.one_negative ? (k != pair_s[0] && k != pair_s[1])
+                                     : (target == -1 && !((uint64_t)r.x < cfg.q_threshold)))
+                    continue;  // kernel.cu:573
                 if (!((uint64_t)r.y < th)) continue;                                // kernel.cu:582
                 int32_t *lw = &weights[(int64_t)c * K + k];
                 int32_t wv = *lw;
@@ -191,9 +196,12 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
             for (int kb = 0; kb < KB; ++kb) {
                 uint32_t m = ev[kb * 3];
                 const uint32_t m1a = ev[kb * 3 + 1], m2 = ev[kb * 3 + 2];
+                // one_negative: the true class's event first, then the other's
+                const int first = cfg.one_negative ? pair_s[0] - k0 - kb * 32 : -1;
                 while (m) {
-                    const int b = __ffs(m) - 1;
-                    m &= m - 1u;
+                    int b = __ffs(m) - 1;
+                    if (first >= 0 && first < 32 && ((m >> first) & 1u)) b = first;
+                    m &= ~(1u << b);
                     if ((m2 >> b) & 1u) {  // type2_fb, kernel.cu:481-506
                         ctr.inc(~x & vm & ctr.below_top());
                     } else {

@@ -38,6 +38,16 @@ __global__ void k_thresholds(const int32_t *__restrict__ cs, const int32_t *__re
 
 enum : uint32_t { EV_NONE = 0, EV_T1A = 1, EV_T1B = 2, EV_T2 = 3 };
 
+__global__ void k_pairs(uint64_t seed, const int32_t *__restrict__ Y, int B, int K, uint64_t t0,
+                        int32_t *__restrict__ pair) {
+    for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < B; b += gridDim.x * blockDim.x) {
+        int kt, ko;
+        true_other_pair(seed, Y + (int64_t)b * K, K, t0 + (uint64_t)b, &kt, &ko);
+        pair[2 * b] = kt;
+        pair[2 * b + 1] = ko;
+    }
+}
+
 template <int NB>
 #ifndef YTM_UPD_MINB
 #define YTM_UPD_MINB 4  // 64 registers: measured fastest (no spills)
@@ -47,7 +57,8 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                                                 const uint32_t *__restrict__ drop,
                                                 const uint32_t *__restrict__ lits, int B, uint64_t t0,
                                                 const int32_t *__restrict__ sel, const int32_t *__restrict__ ninc,
-                                                int BC, const RoundKeys rk, int rk_ok) {
+                                                int BC, const RoundKeys rk, int rk_ok,
+                                                const int32_t *__restrict__ pair) {
     extern __shared__ __align__(16) unsigned char smraw[];
     const int C = cfg.clause_count, W = cfg.words, K = cfg.n_classes, P = cfg.patches;
     const int c = blockIdx.x;
@@ -81,7 +92,8 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
             th &= ~(1ull << 63);
             const uint64_t tb = t0 + (uint64_t)b;
             u32x4 r = rk_ok ? draw_rk(rk, g, tb, 0, TAG_CLASS, (uint32_t)k) : draw(cfg.seed, g, tb, 0, TAG_CLASS, (uint32_t)k);
-            const bool pass = !(neg && !((uint64_t)r.x < cfg.q_threshold));  // kernel.cu:573
+            const bool pass = cfg.one_negative ? (k == pair[2 * b] || k == pair[2 * b + 1])
+                                               : !(neg && !((uint64_t)r.x < cfg.q_threshold));  // kernel.cu:573
             evt[idx] = (pass && (uint64_t)r.y < th) ? (neg ? 2 : 1) : 0;      // kernel.cu:582
         }
         __syncthreads();
@@ -126,11 +138,19 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                     if (tid >= o) incl += v;
                 }
                 int pos = base + incl - n;
-                if (row < bc)
+                if (row < bc && cfg.one_negative) {  // the true class first, then the other
+                    for (int q = 0; q < 2; ++q) {
+                        const int kk = pair[2 * (b0 + row) + q] - k0;
+                        if (kk < 0 || kk >= nk) continue;
+                        uint32_t ev = evt[row * nk + kk];
+                        if (ev != EV_NONE) list[pos++] = ((uint32_t)row << 24) | (ev << 22) | (uint32_t)kk;
+                    }
+                } else if (row < bc) {
                     for (int kk = 0; kk < nk; ++kk) {
                         uint32_t ev = evt[row * nk + kk];
                         if (ev != EV_NONE) list[pos++] = ((uint32_t)row << 24) | (ev << 22) | (uint32_t)kk;
                     }
+                }
                 base += __shfl_sync(0xFFFFFFFFu, incl, 31);
             }
             if (tid == 0) cnt[0] = base;
@@ -199,6 +219,11 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
     const int32_t *ninc = (const int32_t *)(ws + l.ninc);
     const int32_t *sel = sel_override ? sel_override : (const int32_t *)(ws + l.sel);
     uint64_t *thr = (uint64_t *)(ws + l.thr);
+    int32_t *pair = (int32_t *)(ws + l.pair);
+    if (cfg->one_negative) {
+        k_pairs<<<(unsigned)cdiv(B, 256), 256, 0, st>>>(cfg->seed, Y, B, cfg->n_classes, t0, pair);
+        if ((rc = launch_check("class pairs"))) return rc;
+    }
     {
         int64_t total = (int64_t)B * cfg->n_classes;
         unsigned blocks = (unsigned)std::min<int64_t>((int64_t)cdiv(total, 256), (int64_t)sm_count() * 8);
@@ -224,7 +249,7 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
                 return rc;
         }
         k_update<NB><<<cfg->clause_count, tpb, smem, st>>>(*cfg, state, weights, thr, drop, lits, B, t0, sel, ninc,
-                                                           BC, rk, rk_ok);
+                                                           BC, rk, rk_ok, pair);
     });
     return launch_check("feedback");
 }
