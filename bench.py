@@ -144,6 +144,13 @@ def workload(name, n):
     return X, y
 
 
+def oracle_kw(kw):
+    """Model kwargs -> oracle kwargs (rule variants as flags)."""
+    kw = dict(kw)
+    pytm = kw.pop("rules", "cutm") == "pytm"
+    return dict(kw, one_negative=pytm, count_empty=pytm)
+
+
 def cpu_sample(name, kw, B, budget_s=20.0, threads=None):
     """Oracle (CPU restatement, OpenMP) training throughput on a bounded sample
     of the workload.  Models whose state would not fit a modest host budget
@@ -153,7 +160,7 @@ def cpu_sample(name, kw, B, budget_s=20.0, threads=None):
     from oracle import oracle as O
     if threads:
         O.set_threads(threads)
-    o = O.Oracle(seed=42, **kw)
+    o = O.Oracle(seed=42, **oracle_kw(kw))
     nc = min(o.C, max(64, (256 << 20) // (o.L * 4)))
     b = B if nc == o.C else min(B, 16)
     X, y = workload(name, max(4 * b, 64))
@@ -194,7 +201,7 @@ def run_reference(args):
     B = synthetic.BATCH[args.workload]
     O.build()
     O.set_threads(os.cpu_count())
-    o = O.Oracle(seed=42, **kw)
+    o = O.Oracle(seed=42, **oracle_kw(kw))
     nc = min(o.C, max(64, (256 << 20) // (o.L * 4)))
     b = B if nc == o.C else min(B, 16)
     S = b if b > 1 else 256
@@ -243,7 +250,7 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "p1"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--infer-samples", type=int, default=None)
     args = ap.parse_args()

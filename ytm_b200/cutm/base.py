@@ -62,12 +62,16 @@ class BaseTM:
     ("samples": every rank holds a replica of all include masks and weights,
     gathered once after each change, and scores its slice of the samples;
     "clauses": every rank scores all samples on its clauses and the class sums
-    are all-reduced).
+    are all-reduced) and ``rules`` ("cutm": the rules of src/cutm/cuda/kernel.cu;
+    "pytm": the rule variants of the reference's numpy TM, src/pytm/base.py —
+    feedback for the true class and ONE uniformly drawn other class per
+    sample, true class first, and clauses without includes counted at
+    prediction).
     """
 
     def __init__(self, number_of_clauses_per_class: int, T: int, s: float, dim: tuple[int, int, int],
                  n_classes: int, device=None, process_group=None, inference_sharding: str = "samples",
-                 _engine_factory=None, **opt_args):
+                 rules: str = "cutm", _engine_factory=None, **opt_args):
         self.init_args = {"number_of_clauses_per_class": number_of_clauses_per_class, "T": T, "s": s,
                           "dim": tuple(dim), "n_classes": n_classes}
         self.opt_args: BaseTMOptArgs = {  # base.py:60-74
@@ -141,7 +145,11 @@ class BaseTM:
             patch_dim=self.patch_dim, number_of_ta_states=self.number_of_ta_states,
             max_included_literals=self.max_included_literals, append_negated=self.append_negated,
             init_neg_weights=self.init_neg_weights, negative_polarity=self.negative_clauses,
-            encode_loc=self.encode_loc, coalesced=self.coalesced, seed=self._key)
+            encode_loc=self.encode_loc, coalesced=self.coalesced, seed=self._key,
+            one_negative=rules == "pytm", count_empty=rules == "pytm")
+        if rules not in ("cutm", "pytm"):
+            raise ValueError("rules must be 'cutm' or 'pytm'")
+        self.rules = rules
         self.cfg_full = full
         self.number_of_clause_banks = full.clause_banks
         self.number_of_clauses = full.clauses

@@ -24,8 +24,13 @@ MODELS = {
     "c5": dict(number_of_clauses_per_class=65536, T=20000, s=20.0, dim=(16384, 1, 1), n_classes=100,
                number_of_ta_states=4096),
 }
-BATCH = {"c1": 1, "c2": 256, "c3": 1, "c4": 1, "c5": 1024}
-SEEDS = {"c1": 1001, "c2": 1002, "c3": 1003, "c4": 1004, "c5": 1005}
+# pytm's own rules (src/pytm/base.py) at the 2000-clause, 784-feature size the
+# reference's numpy TM was timed on: 2000 shared clauses, pytm's default 256
+# states (0..255 = this engine's number_of_ta_states 255), batch 1
+MODELS["p1"] = dict(number_of_clauses_per_class=2000, T=50, s=10.0, dim=(28, 28, 1), n_classes=10, coalesced=True,
+                    number_of_ta_states=255, rules="pytm")
+BATCH = {"c1": 1, "c2": 256, "c3": 1, "c4": 1, "c5": 1024, "p1": 1}
+SEEDS = {"c1": 1001, "c2": 1002, "c3": 1003, "c4": 1004, "c5": 1005, "p1": 1001}
 
 
 def prototypes(N, seed=1001, n_classes=10, n_features=784, p_one=0.2, p_flip=0.05):
@@ -98,7 +103,7 @@ def rules(N, seed=1005, n_classes=100, n_features=16384, density=0.01, rules_per
 
 def make(name, N, seed=None):
     seed = SEEDS[name] if seed is None else seed
-    if name in ("c1", "c2"):
+    if name in ("c1", "c2", "p1"):
         return prototypes(N, seed)
     if name == "c3":
         return glyphs(N, seed)
