@@ -114,6 +114,7 @@ ytm_status ytm_config_shard(ytm_config *cfg, int32_t rank, int32_t world);
 #define YTM_OP_TRAIN 4
 #define YTM_OP_TRAIN_B1 5   /* ytm_train_fit_b1 (n ignored) */
 #define YTM_OP_ENCODE_THERMO 6
+#define YTM_OP_TRAIN_LOOP 7  /* ytm_train_fit_batches, n = batch size */
 uint64_t ytm_workspace_bytes(const ytm_config *cfg, int32_t op, int64_t n);
 
 /* Encode raw inputs into per-patch literal words.
@@ -186,7 +187,8 @@ ytm_status ytm_transform_patchwise(const ytm_config *cfg, const uint32_t *state,
 /* Training, part 1, for a batch of B samples whose first global sample
  * counter is t0: freeze include counts, evaluate every clause of the shard on
  * every patch (training semantics: empty clause matches, dropped clause never
- * fires), pick one matching patch per (sample, clause), count it in patch_w,
+ * fires), pick one matching patch per (sample, clause), count it in patch_w
+ * (single-patch models: ytm_train_update counts the picks),
  * and write the shard's partial class sums cs i32 [B][K] (bias added when
  * add_bias != 0).  Replaces pack_clauses + fast_eval + select_active
  * (kernel.cu:155-204, 255-316) of the per-sample loop (base.py:305-337).
@@ -202,11 +204,14 @@ ytm_status ytm_train_eval(const ytm_config *cfg, const uint32_t *state, const in
  * shards) and targets Y i32 [B][K] (+T / -T).  Replaces clause_update and
  * type1a_fb / type1b_fb / type2_fb (kernel.cu:397-613, base.py:339-357).
  * sel_override: i32 [B][C] patch picks to use instead of the ones
- * ytm_train_eval chose (-1 = clause did not fire), or NULL. */
+ * ytm_train_eval chose (-1 = clause did not fire), or NULL.  patch_w: for
+ * single-patch models with up to 256 classes, ytm_train_eval leaves the
+ * counting of picks (kernel.cu:305) to this call, which adds them here. */
 ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, int32_t *weights,
                             const int32_t *cs, const int32_t *Y, const uint32_t *drop,
                             const uint32_t *lits, int32_t B, uint64_t t0,
-                            const int32_t *sel_override, void *workspace, void *stream);
+                            const int32_t *sel_override, int32_t *patch_w, void *workspace,
+                            void *stream);
 
 /* Train on samples 0..N-1 one at a time, in order: the reference's
  * per-sample loop (_fit, base.py:305-357: pack_clauses, fast_eval,
@@ -219,6 +224,24 @@ ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, int32_t *wei
 ytm_status ytm_train_fit_b1(const ytm_config *cfg, uint32_t *state, int32_t *weights, const int32_t *bias,
                             const uint32_t *drop, const uint32_t *lits, const int32_t *Y, int64_t N,
                             uint64_t t0, int32_t *patch_w, void *workspace, void *stream);
+
+/* NCCL communicator for clause-sharded training (no reference counterpart:
+ * the reference is single-GPU).  Rank 0 makes the 128-byte id, every rank
+ * passes it to ytm_nccl_comm_init (the caller distributes it). */
+ytm_status ytm_nccl_unique_id(uint8_t *id_out);
+ytm_status ytm_nccl_comm_init(const uint8_t *id_in, int32_t rank, int32_t world, void **comm_out);
+ytm_status ytm_nccl_comm_destroy(void *comm);
+
+/* Train on samples 0..N-1 in mini-batches of B (the last one ragged), all
+ * queued on `stream` from C: per batch ytm_train_eval, the int32 sum of the
+ * class sums over the clause shards (ncclAllReduce on `comm`; NULL for one
+ * process), ytm_train_update.  The reference's _fit loop (base.py:305-357)
+ * with batch B.  add_bias: add the bias on this shard (one shard only).
+ * workspace: ytm_workspace_bytes(cfg, YTM_OP_TRAIN_LOOP, B). */
+ytm_status ytm_train_fit_batches(const ytm_config *cfg, uint32_t *state, int32_t *weights, const int32_t *bias,
+                                 const uint32_t *drop, const uint32_t *lits, const int32_t *Y, int64_t N,
+                                 int32_t B, uint64_t t0, int32_t add_bias, int32_t *patch_w, void *comm,
+                                 void *workspace, void *stream);
 
 /* Read back the patch picks of the last ytm_train_eval on this workspace:
  * sel i32 [B][C] (-1 = not fired).  Device-to-device copy on `stream`. */

@@ -13,6 +13,7 @@ LIB_PATH = os.path.join(HERE, "libytm.so")
 
 YTM_OK = 0
 YTM_OP_ENCODE, YTM_OP_INFER, YTM_OP_TRANSFORM, YTM_OP_TRAIN, YTM_OP_TRAIN_B1, YTM_OP_ENCODE_THERMO = 1, 2, 3, 4, 5, 6
+YTM_OP_TRAIN_LOOP = 7
 
 # Every function include/ytm.h declares; tests check the library exports them.
 EXPORTS = (
@@ -21,7 +22,8 @@ EXPORTS = (
     "ytm_transform", "ytm_transform_patchwise", "ytm_train_eval", "ytm_train_update",
     "ytm_train_selection", "ytm_last_error", "ytm_version", "ytm_infer_noalloc",
     "ytm_train_fit_b1", "ytm_probe_lop3", "ytm_infer_include",
-    "ytm_encode_thermometer",
+    "ytm_encode_thermometer", "ytm_nccl_unique_id", "ytm_nccl_comm_init", "ytm_nccl_comm_destroy",
+    "ytm_train_fit_batches",
 )
 
 
@@ -68,13 +70,17 @@ _SIGS = {
     "ytm_transform": ([_CFG, _P, _P, _I64, _P, _P, _P], ct.c_int),
     "ytm_transform_patchwise": ([_CFG, _P, _P, _I64, _P, _P], ct.c_int),
     "ytm_train_eval": ([_CFG, _P, _P, _P, _P, _P, _I32, _U64, _I32, _P, _P, _P, _P], ct.c_int),
-    "ytm_train_update": ([_CFG, _P, _P, _P, _P, _P, _P, _I32, _U64, _P, _P, _P], ct.c_int),
+    "ytm_train_update": ([_CFG, _P, _P, _P, _P, _P, _P, _I32, _U64, _P, _P, _P, _P], ct.c_int),
     "ytm_train_selection": ([_CFG, _I32, _P, _P, _P], ct.c_int),
     "ytm_train_fit_b1": ([_CFG, _P, _P, _P, _P, _P, _P, _I64, _U64, _P, _P, _P], ct.c_int),
     "ytm_infer_noalloc": ([_CFG, _P, _P, _P, _P, _I64, _P, _P], ct.c_int),
     "ytm_probe_lop3": ([_I32, _I32, _P, ct.POINTER(ct.c_uint64), _P], ct.c_int),
     "ytm_infer_include": ([_CFG, _P, _P, _P, _P, _I64, _P, _P, _P], ct.c_int),
     "ytm_encode_thermometer": ([_CFG, _P, _I64, _I32, _P, _P, _P], ct.c_int),
+    "ytm_nccl_unique_id": ([_P], ct.c_int),
+    "ytm_nccl_comm_init": ([_P, _I32, _I32, ct.POINTER(ct.c_void_p)], ct.c_int),
+    "ytm_nccl_comm_destroy": ([_P], ct.c_int),
+    "ytm_train_fit_batches": ([_CFG, _P, _P, _P, _P, _P, _P, _I64, _I32, _U64, _I32, _P, _P, _P, _P], ct.c_int),
     "ytm_last_error": ([], ct.c_char_p),
     "ytm_version": ([], ct.c_char_p),
 }

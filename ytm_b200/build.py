@@ -23,6 +23,20 @@ NVCC_FLAGS = [
 ]
 
 
+def nccl_flags() -> list[str]:
+    """Include/link flags for NCCL: the headers of the NCCL wheel that torch
+    loads (same version at run time), else the system's."""
+    try:
+        import nvidia.nccl as n  # the wheel torch depends on
+        base = os.path.dirname(n.__file__) if getattr(n, "__file__", None) else list(n.__path__)[0]
+        inc, lib = os.path.join(base, "include"), os.path.join(base, "lib")
+        if os.path.exists(os.path.join(inc, "nccl.h")):
+            return ["-I" + inc, "-L" + lib, "-l:libnccl.so.2"]
+    except ImportError:
+        pass
+    return ["-lnccl"]
+
+
 def sources() -> list[str]:
     return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
 
@@ -41,7 +55,7 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
         return LIB
     nvcc = os.environ.get("NVCC", "nvcc")
     tmp = LIB + ".tmp"
-    cmd = [nvcc, *NVCC_FLAGS, *(extra or []), *sources(), "-o", tmp]
+    cmd = [nvcc, *NVCC_FLAGS, *(extra or []), *sources(), *nccl_flags(), "-o", tmp]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)

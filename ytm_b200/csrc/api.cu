@@ -47,8 +47,8 @@ TrainWs train_ws_layout(const ytm_config *cfg, int64_t B) {
     uint64_t o = 0;
     l.ninc = o;  o = align_up(o + C * 4, 256);
     l.mbits = o; o = align_up(o + (uint64_t)B * C * PW * 4, 256);
+    l.fired = o; o = align_up(o + (uint64_t)B * CW * 4, 256);  // right after mbits: one memset clears both
     l.sel = o;   o = align_up(o + (uint64_t)B * C * 4, 256);
-    l.fired = o; o = align_up(o + (uint64_t)B * CW * 4, 256);
     l.thr = o;   o = align_up(o + (uint64_t)B * K * 8, 256);
     l.pair = o;  o = align_up(o + (uint64_t)B * 2 * 4, 256);
     l.total = o;
@@ -178,6 +178,9 @@ uint64_t ytm_workspace_bytes(const ytm_config *cfg, int32_t op, int64_t n) {
             return train_ws_layout(cfg, n).total + cs_planes_bytes(cfg);
         case YTM_OP_TRAIN_B1:
             return b1_ws_layout(cfg).total;
+        case YTM_OP_TRAIN_LOOP:
+            return align_up((uint64_t)n * cfg->n_classes * 4, 256) + train_ws_layout(cfg, n).total +
+                   cs_planes_bytes(cfg);
         default:
             return 0;
     }

@@ -275,6 +275,10 @@ __host__ __device__ __forceinline__ uint32_t valid_mask(int w, int W, int L) {
         default: return fail(YTM_ERR_UNSUPPORTED, "number_of_ta_states needs more than 16 bit planes"); \
     }
 
+// Single-patch models with up to 256 classes evaluate training batches in one
+// fused kernel that leaves patch counting to the feedback kernel.
+inline bool single_patch_eval(const ytm_config *cfg) { return cfg->patches == 1 && cfg->n_classes <= 256; }
+
 // Validates the pieces of a config every entry point relies on.
 ytm_status check_cfg(const ytm_config *cfg);
 

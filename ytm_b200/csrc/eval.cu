@@ -23,20 +23,17 @@ enum { MODE_ANY = 0, MODE_PBITS = 1, MODE_PATCHWISE = 2 };
 
 constexpr int RT = 64, CT = 64, KW = 32, XS = RT + 4;
 
-template <int MODE>
-__global__ void __launch_bounds__(256) k_match(const uint32_t *__restrict__ inc, const uint32_t *__restrict__ lits,
-                                               int64_t R, int C, int W, int P, uint32_t *__restrict__ out) {
-    __shared__ __align__(16) uint32_t xs[KW][XS];
-    __shared__ __align__(16) uint32_t is[KW][XS];
+// Violations v[i][j] = OR_w (inc & ~x) of the 4 rows x 4 clauses a thread
+// owns in the 64 x 64 tile at (row0, c0); 32-word chunks staged in shared
+// memory, no work on words past W.
+__device__ __forceinline__ void tile_violations(const uint32_t *__restrict__ inc, const uint32_t *__restrict__ lits,
+                                                int64_t R, int C, int W, int64_t row0, int c0,
+                                                uint32_t (*xs)[XS], uint32_t (*is)[XS], uint32_t (&v)[4][4]) {
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-    const int64_t row0 = (int64_t)blockIdx.x * RT;
-    const int c0 = blockIdx.y * CT;
-    uint32_t v[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) v[i][j] = 0u;
-
     for (int w0 = 0; w0 < W; w0 += KW) {
         const int kwn = min(KW, W - w0);  // no work on words past W
 #pragma unroll
@@ -63,6 +60,18 @@ __global__ void __launch_bounds__(256) k_match(const uint32_t *__restrict__ inc,
         }
         __syncthreads();
     }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(256) k_match(const uint32_t *__restrict__ inc, const uint32_t *__restrict__ lits,
+                                               int64_t R, int C, int W, int P, uint32_t *__restrict__ out) {
+    __shared__ __align__(16) uint32_t xs[KW][XS];
+    __shared__ __align__(16) uint32_t is[KW][XS];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int64_t row0 = (int64_t)blockIdx.x * RT;
+    const int c0 = blockIdx.y * CT;
+    uint32_t v[4][4];
+    tile_violations(inc, lits, R, C, W, row0, c0, xs, is, v);
 
     const int cb = c0 + tx * 4;
 #pragma unroll
@@ -102,6 +111,71 @@ static ytm_status launch_match(const uint32_t *inc, const uint32_t *lits, int64_
     if (gx > 0x7FFFFFFFll || gy > 65535) return fail(YTM_ERR_UNSUPPORTED, "match grid too large; split the batch");
     k_match<MODE><<<dim3((unsigned)gx, (unsigned)gy), 256, 0, st>>>(inc, lits, R, C, W, P, out);
     return launch_check("clause match");
+}
+
+// Training evaluation of single-patch models in one kernel: the tile's
+// matches give each (sample, clause) its pick (patch 0, or -1 when it does not
+// fire or is dropped: fast_eval + select_active, kernel.cu:255-316), the fired
+// bits, and the class sums: per row the weights of the fired clauses
+// (staged in shared memory; non-coalesced clauses count for their own class
+// only, kernel.cu:306-312) are summed over the 16 threads that share the row
+// and added with one int32 atomic per (row, class) and tile.
+__global__ void __launch_bounds__(256) k_train_eval1(ytm_config cfg, const uint32_t *__restrict__ inc,
+                                                     const uint32_t *__restrict__ lits, int B,
+                                                     const int32_t *__restrict__ weights,
+                                                     const uint32_t *__restrict__ drop, int32_t *__restrict__ sel,
+                                                     uint32_t *__restrict__ fired, int32_t *__restrict__ cs) {
+    __shared__ __align__(16) uint32_t xs[KW][XS];
+    __shared__ __align__(16) uint32_t is[KW][XS];
+    extern __shared__ int32_t w_s[];  // [CT][K]
+    const int C = cfg.clause_count, W = cfg.words, K = cfg.n_classes;
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int64_t row0 = (int64_t)blockIdx.x * RT;
+    const int c0 = blockIdx.y * CT;
+    for (int q = tid; q < CT * K; q += 256) {
+        const int cl = q / K, k = q % K, c = c0 + cl;
+        int32_t v = 0;
+        if (c < C && !(drop && drop[c] == 1u)) {
+            const int own = (cfg.clause_lo + c) / cfg.clauses_per_class;
+            if (cfg.coalesced || k == own) v = weights[(int64_t)c * K + k];
+        }
+        w_s[q] = v;
+    }
+    uint32_t v[4][4];
+    tile_violations(inc, lits, B, C, W, row0, c0, xs, is, v);  // its syncs also publish w_s
+    const int cb = c0 + tx * 4;
+    uint32_t keep = 0u;  // clauses of this thread that exist and are not dropped
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        if (cb + j < C && !(drop && drop[cb + j] == 1u)) keep |= 1u << j;
+    const int CWn = (C + 31) / 32;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t row = row0 + ty * 4 + i;
+        const bool rv = row < B;
+        uint32_t nib = 0u;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (v[i][j] == 0u) nib |= 1u << j;
+        nib &= keep;
+        if (rv) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (cb + j < C) sel[row * C + cb + j] = ((nib >> j) & 1u) ? 0 : -1;
+            if (fired && nib) atomicOr(&fired[row * CWn + (cb >> 5)], nib << (cb & 31));
+        }
+        for (int k = 0; k < K; ++k) {
+            int32_t part = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if ((nib >> j) & 1u) part += w_s[(tx * 4 + j) * K + k];
+            part += __shfl_xor_sync(0xFFFFFFFFu, part, 8);
+            part += __shfl_xor_sync(0xFFFFFFFFu, part, 4);
+            part += __shfl_xor_sync(0xFFFFFFFFu, part, 2);
+            part += __shfl_xor_sync(0xFFFFFFFFu, part, 1);
+            if (tx == 0 && rv && part != 0) atomicAdd(&cs[row * K + k], part);
+        }
+    }
 }
 
 __global__ void k_cs_init(int32_t *__restrict__ cs, const int32_t *__restrict__ bias, int64_t N, int K) {
@@ -302,7 +376,7 @@ uint64_t cs_planes_bytes(const ytm_config *cfg) {
 // clause's own class when own_class); scratch: cs_planes_bytes(cfg).
 static ytm_status launch_cs_planes(const uint32_t *fired, const int32_t *ninc, const int32_t *w, const int32_t *bias,
                                    const ytm_config *cfg, int64_t N, int own_class, int32_t *cs, void *scratch,
-                                   cudaStream_t st) {
+                                   cudaStream_t st, bool wmax_cleared = false) {
     const int C = cfg->clause_count, K = cfg->n_classes;
     const int64_t CW = (int64_t)cdiv(C, 32);
     char *p = (char *)scratch;
@@ -310,7 +384,7 @@ static ytm_status launch_cs_planes(const uint32_t *fired, const int32_t *ninc, c
     uint32_t *planes = (uint32_t *)(p + 256);
     uint32_t *keep = (uint32_t *)(p + 256 + align_up(CW * K * 32 * 4, 256));
     ytm_status rc;
-    if ((rc = cuda_check(cudaMemsetAsync(wmax, 0, 4, st), "memset"))) return rc;
+    if (!wmax_cleared && (rc = cuda_check(cudaMemsetAsync(wmax, 0, 4, st), "memset"))) return rc;
     k_wmax<<<grid1((int64_t)C * K), 256, 0, st>>>(w, C, K, own_class, cfg->clause_lo, cfg->clauses_per_class, wmax);
     if ((rc = launch_check("weight range"))) return rc;
     k_wplanes<<<grid1(CW * K * 32), 256, 0, st>>>(w, ninc, C, K, own_class, cfg->clause_lo, cfg->clauses_per_class,
@@ -343,14 +417,18 @@ __global__ void k_expand(const uint32_t *__restrict__ fired, int64_t N, int C, u
 // (reference select_active, kernel.cu:285-316, reservoir sampling; here the
 // TAG_PATCH draw r gives index floor(r * count / 2^32) among the matches in
 // patch order), count it in patch_w and set the fired bit.
+// Also: thread 0 clears the weight-range slot of the class-sum planes that
+// follow.
 __global__ void k_pick(ytm_config cfg, const uint32_t *__restrict__ mbits, const uint32_t *__restrict__ drop,
                        int B, uint64_t t0, int32_t *__restrict__ sel, uint32_t *__restrict__ fired,
-                       int32_t *__restrict__ patch_w) {
+                       int32_t *__restrict__ patch_w, int32_t *__restrict__ wmax) {
     const int C = cfg.clause_count, P = cfg.patches, PW = (P + 31) / 32, CWn = (C + 31) / 32;
+    if (blockIdx.x == 0 && threadIdx.x == 0) *wmax = 0;
     int64_t total = (int64_t)B * C;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
         int b = (int)(i / C), c = (int)(i % C);
+
         int32_t s = -1;
         if (!(drop && drop[c] == 1u)) {
             const uint32_t *m = mbits + i * PW;
@@ -469,20 +547,36 @@ ytm_status ytm_train_eval(const ytm_config *cfg, const uint32_t *state, const in
     const int C = cfg->clause_count, W = cfg->words, P = cfg->patches;
     TrainWs l = train_ws_layout(cfg, B);
     char *ws = (char *)workspace;
-    int32_t *ninc = (int32_t *)(ws + l.ninc);
     uint32_t *mbits = (uint32_t *)(ws + l.mbits);
     int32_t *sel = (int32_t *)(ws + l.sel);
     uint32_t *fired = (uint32_t *)(ws + l.fired);
     const uint32_t *inc = state + (int64_t)(cfg->planes - 1) * C * W;
-    if ((rc = launch_ninc(cfg, state, ninc, st))) return rc;
-    if ((rc = cuda_check(cudaMemsetAsync(mbits, 0, (size_t)B * C * cdiv(P, 32) * 4, st), "memset"))) return rc;
-    if ((rc = cuda_check(cudaMemsetAsync(fired, 0, (size_t)B * cdiv(C, 32) * 4, st), "memset"))) return rc;
+    if (single_patch_eval(cfg)) {
+        // single patch: one fused kernel (picks and class sums; the feedback
+        // kernel counts the picks in patch_w)
+        k_cs_init<<<grid1((int64_t)B * cfg->n_classes), 256, 0, st>>>(cs, add_bias ? bias : nullptr, B,
+                                                                        cfg->n_classes);
+        if ((rc = launch_check("cs init"))) return rc;
+        const size_t smem = (size_t)CT * cfg->n_classes * 4;
+        if (smem > 48 * 1024 &&
+            (rc = cuda_check(cudaFuncSetAttribute(k_train_eval1, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  (int)smem), "train eval smem")))
+            return rc;
+        const int64_t gx = (int64_t)cdiv(B, RT), gy = (int64_t)cdiv(C, CT);
+        if (gy > 65535) return fail(YTM_ERR_UNSUPPORTED, "too many clauses for one launch");
+        k_train_eval1<<<dim3((unsigned)gx, (unsigned)gy), 256, smem, st>>>(*cfg, inc, lits, B, weights, drop, sel,
+                                                                           nullptr, cs);
+        return launch_check("train eval");
+    }
+    // match bits and fired bits are adjacent in the workspace: one clear
+    if ((rc = cuda_check(cudaMemsetAsync(mbits, 0, l.sel - l.mbits, st), "memset"))) return rc;
     // training semantics: an empty clause matches every patch (kernel.cu:273-276)
     if ((rc = launch_match<MODE_PBITS>(inc, lits, (int64_t)B * P, C, W, P, mbits, st))) return rc;
-    k_pick<<<grid1((int64_t)B * C), 256, 0, st>>>(*cfg, mbits, drop, B, t0, sel, fired, patch_w);
+    int32_t *wmax = (int32_t *)(ws + l.total);  // the class-sum planes scratch starts with the weight range
+    k_pick<<<grid1((int64_t)B * C), 256, 0, st>>>(*cfg, mbits, drop, B, t0, sel, fired, patch_w, wmax);
     if ((rc = launch_check("patch pick"))) return rc;
     return launch_cs_planes(fired, nullptr, weights, add_bias ? bias : nullptr, cfg, B, cfg->coalesced ? 0 : 1, cs,
-                            ws + l.total, st);
+                            ws + l.total, st, true);
 }
 
 ytm_status ytm_train_selection(const ytm_config *cfg, int32_t B, const void *workspace, int32_t *sel,

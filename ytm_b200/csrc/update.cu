@@ -56,9 +56,9 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                                                 int32_t *__restrict__ weights, const uint64_t *__restrict__ thr,
                                                 const uint32_t *__restrict__ drop,
                                                 const uint32_t *__restrict__ lits, int B, uint64_t t0,
-                                                const int32_t *__restrict__ sel, const int32_t *__restrict__ ninc,
+                                                const int32_t *__restrict__ sel, int32_t *__restrict__ patch_w,
                                                 int BC, const RoundKeys rk, int rk_ok,
-                                                const int32_t *__restrict__ pair) {
+                                                const int32_t *__restrict__ pair, int count_patch) {
     extern __shared__ __align__(16) unsigned char smraw[];
     const int C = cfg.clause_count, W = cfg.words, K = cfg.n_classes, P = cfg.patches;
     const int c = blockIdx.x;
@@ -72,7 +72,20 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
     uint32_t *list = (uint32_t *)(cnt + 1);               // [BC * nk]
     uint8_t *evt = (uint8_t *)(list + BC * nk);           // [BC * nk]
     const int tid = threadIdx.x, nt = blockDim.x;
-    const bool ok_inc = ninc[c] <= cfg.max_included_literals;
+    // include count of the batch-start state (pack_clauses, kernel.cu:155-204):
+    // this CTA alone writes the clause, so its top plane is still unchanged
+    __shared__ int ninc_s;
+    if (tid == 0) ninc_s = 0;
+    __syncthreads();
+    {
+        int n = 0;
+        for (int w = tid; w < W; w += nt) n += __popc(state[((int64_t)(NB - 1) * C + c) * W + w]);
+        for (int o = 16; o; o >>= 1) n += __shfl_xor_sync(0xFFFFFFFFu, n, o);
+        if ((tid & 31) == 0 && n) atomicAdd(&ninc_s, n);
+    }
+    __syncthreads();
+    const bool ok_inc = ninc_s <= cfg.max_included_literals;
+    int fired_count = 0;  // single-patch models: patch 0 picks of this clause (select_active, kernel.cu:305)
     const uint32_t max_s = (uint32_t)(cfg.max_state + cfg.state_offset);
     const uint32_t zero_s = (uint32_t)cfg.state_offset;
 
@@ -80,7 +93,10 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
 
     for (int b0 = 0; b0 < B; b0 += BC) {
         const int bc = min(BC, B - b0);
-        for (int q = tid; q < bc; q += nt) sel_s[q] = sel[(int64_t)(b0 + q) * C + c];
+        for (int q = tid; q < bc; q += nt) {
+            sel_s[q] = sel[(int64_t)(b0 + q) * C + c];
+            fired_count += sel_s[q] >= 0;
+        }
         __syncthreads();
         // 1a. the chunk's Q-selection and update draws, all (sample, class)
         //     pairs in parallel: 1 = update with target +1, 2 = with target -1
@@ -195,6 +211,10 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
         __syncthreads();
     }
     for (int kk = tid; kk < nk; kk += nt) weights[(int64_t)c * K + k0 + kk] = wk[kk];
+    if (count_patch) {
+        for (int o = 16; o; o >>= 1) fired_count += __shfl_xor_sync(0xFFFFFFFFu, fired_count, o);
+        if ((tid & 31) == 0 && fired_count) atomicAdd(&patch_w[c], fired_count);
+    }
 }
 
 static size_t update_smem(int nk, int bc) {
@@ -207,16 +227,18 @@ using namespace ytm;
 
 extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, int32_t *weights, const int32_t *cs,
                                        const int32_t *Y, const uint32_t *drop, const uint32_t *lits, int32_t B,
-                                       uint64_t t0, const int32_t *sel_override, void *workspace, void *stream) {
+                                       uint64_t t0, const int32_t *sel_override, int32_t *patch_w, void *workspace,
+                                       void *stream) {
     ytm_status rc = check_cfg(cfg);
     if (rc) return rc;
     if (B <= 0) return fail(YTM_ERR_ARG, "batch must be positive");
     if (!state || !weights || !cs || !Y || !lits || !workspace) return fail(YTM_ERR_ARG, "null pointer");
+    const int count_patch = single_patch_eval(cfg) ? 1 : 0;
+    if (count_patch && !patch_w) return fail(YTM_ERR_ARG, "patch_w is NULL");
     if (cfg->n_classes >= (1 << 22)) return fail(YTM_ERR_UNSUPPORTED, "too many classes");
     cudaStream_t st = as_stream(stream);
     TrainWs l = train_ws_layout(cfg, B);
     char *ws = (char *)workspace;
-    const int32_t *ninc = (const int32_t *)(ws + l.ninc);
     const int32_t *sel = sel_override ? sel_override : (const int32_t *)(ws + l.sel);
     uint64_t *thr = (uint64_t *)(ws + l.thr);
     int32_t *pair = (int32_t *)(ws + l.pair);
@@ -248,8 +270,8 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
                                                       (int)smem), "update smem")))
                 return rc;
         }
-        k_update<NB><<<cfg->clause_count, tpb, smem, st>>>(*cfg, state, weights, thr, drop, lits, B, t0, sel, ninc,
-                                                           BC, rk, rk_ok, pair);
+        k_update<NB><<<cfg->clause_count, tpb, smem, st>>>(*cfg, state, weights, thr, drop, lits, B, t0, sel,
+                                                           patch_w, BC, rk, rk_ok, pair, count_patch);
     });
     return launch_check("feedback");
 }

@@ -177,6 +177,28 @@ class BaseTM:
             return torch.device("cuda", torch.cuda.current_device())
         return torch.device("cpu")
 
+    def _nccl(self):
+        """NCCL communicator of the clause shards for the C training loop
+        (None for one process or a non-NCCL group).  Made on first use: rank
+        0's id is broadcast through the process group."""
+        if self.world == 1 or dist.get_backend(self._pg) != "nccl":
+            return None
+        if getattr(self, "_comm", None) is None:
+            import ctypes as ct
+            lib = _lib.load()
+            idb = torch.zeros(128, dtype=torch.uint8)
+            if self.rank == 0:
+                _lib.check(lib.ytm_nccl_unique_id(ct.c_void_p(idb.data_ptr())), "ytm_nccl_unique_id")
+            idd = idb.to(self.device)
+            dist.broadcast(idd, src=dist.get_global_rank(self._pg, 0), group=self._pg)
+            idb = idd.cpu()
+            comm = ct.c_void_p()
+            with torch.cuda.device(self.device):
+                _lib.check(lib.ytm_nccl_comm_init(ct.c_void_p(idb.data_ptr()), self.rank, self.world, ct.byref(comm)),
+                           "ytm_nccl_comm_init")
+            self._comm = comm
+        return self._comm
+
     def _allreduce(self, t: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
             return t
@@ -283,6 +305,12 @@ class BaseTM:
             self.engine.train_fit_b1(lits, Y, t, drop)
             self.sample_counter = t + N
             self.last_class_sums = self.engine.b1_class_sums(N)
+            return
+        if hasattr(self.engine, "train_fit_batches") and (self.world == 1 or self._nccl() is not None):
+            # the batch loop and the class-sum all-reduce queued from C
+            self.last_class_sums = self.engine.train_fit_batches(lits, Y, batch_size, t, drop, self.rank == 0,
+                                                                 self._nccl())
+            self.sample_counter = t + N
             return
         for i in range(0, N, batch_size):
             B = min(batch_size, N - i)

@@ -185,7 +185,8 @@ class CudaEngine:
         ws = self.workspace(_lib.YTM_OP_TRAIN, B)
         with torch.cuda.device(self.device):
             check(self.lib.ytm_train_update(self._cfg, _p(self.state), _p(self.weights), _p(cs), _p(Y_b), _p(drop),
-                                            _p(lits_b), B, int(t0), _p(sel_override), _p(ws), self._stream()),
+                                            _p(lits_b), B, int(t0), _p(sel_override), _p(self.patch_w), _p(ws),
+                                            self._stream()),
                   "ytm_train_update")
 
     def train_fit_b1(self, lits: torch.Tensor, Y: torch.Tensor, t0: int, drop: torch.Tensor | None) -> None:
@@ -199,6 +200,24 @@ class CudaEngine:
             check(self.lib.ytm_train_fit_b1(self._cfg, _p(self.state), _p(self.weights), _p(self.bias), _p(drop),
                                             _p(lits), _p(Y), N, int(t0), _p(self.patch_w), _p(ws), self._stream()),
                   "ytm_train_fit_b1")
+
+    def train_fit_batches(self, lits: torch.Tensor, Y: torch.Tensor, B: int, t0: int, drop: torch.Tensor | None,
+                          add_bias: bool, comm=None) -> torch.Tensor:
+        """Mini-batch training over all samples of lits in order, queued from C
+        (eval, NCCL all-reduce of the class sums on `comm` if given, feedback
+        per batch).  Returns the class sums [b, K] of the last batch."""
+        N = lits.shape[0]
+        if N == 0:
+            return torch.empty((0, self.K), dtype=torch.int32, device=self.device)
+        B = int(min(B, N))
+        ws = self.workspace(_lib.YTM_OP_TRAIN_LOOP, B)
+        with torch.cuda.device(self.device):
+            check(self.lib.ytm_train_fit_batches(self._cfg, _p(self.state), _p(self.weights), _p(self.bias), _p(drop),
+                                                 _p(lits), _p(Y), N, B, int(t0), int(bool(add_bias)),
+                                                 _p(self.patch_w), comm, _p(ws), self._stream()),
+                  "ytm_train_fit_batches")
+        last = N - (N - 1) // B * B
+        return ws[:last * self.K * 4].view(torch.int32).view(last, self.K)
 
     def b1_class_sums(self, N: int) -> torch.Tensor:
         """Class sums [1, K] the last train_fit_b1 call used for its last
