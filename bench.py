@@ -302,8 +302,9 @@ def main():
             tm.sample_counter += S
             return
         if hasattr(eng, "train_fit_batches") and not ev:  # the path MultiClassTM.fit takes at batch > 1
+            par = tm._peer_ar(B * kw["n_classes"])
             eng.train_fit_batches(lits[i * S:(i + 1) * S], Yd[i * S:(i + 1) * S], B, tm.sample_counter, None,
-                                  rank == 0, tm._nccl())
+                                  rank == 0, None if par is not None else tm._nccl(), par)
             tm.sample_counter += S
             return
         for j in range(i * S, (i + 1) * S, B):

@@ -241,7 +241,23 @@ ytm_status ytm_nccl_comm_destroy(void *comm);
 ytm_status ytm_train_fit_batches(const ytm_config *cfg, uint32_t *state, int32_t *weights, const int32_t *bias,
                                  const uint32_t *drop, const uint32_t *lits, const int32_t *Y, int64_t N,
                                  int32_t B, uint64_t t0, int32_t add_bias, int32_t *patch_w, void *comm,
-                                 void *workspace, void *stream);
+                                 void *peer_ar, void *workspace, void *stream);
+
+/* One-shot int32 all-reduce over NVLink peer memory for the ranks of one
+ * node (no reference counterpart).  create: allocate this rank's buffer (room
+ * for max_n values) and return its 64-byte CUDA IPC handle; open: map every
+ * rank's buffer from the handles (world x 64 bytes, rank order); allreduce:
+ * sum data[0..n) over the ranks in place on `stream` (every rank must call it
+ * the same number of times); a rank that never arrives is reported after
+ * `limit` spin iterations (<= 0: default, tens of seconds) through status
+ * (0 = all calls completed, else 1 + the index of the missing peer) and the
+ * call leaves data unchanged.  ytm_train_fit_batches uses it when peer_ar is
+ * given (instead of comm). */
+ytm_status ytm_peer_ar_create(int32_t rank, int32_t world, int64_t max_n, void **ctx_out, uint8_t *handle_out);
+ytm_status ytm_peer_ar_open(void *ctx, const uint8_t *handles);
+ytm_status ytm_peer_allreduce_i32(void *ctx, int32_t *data, int64_t n, int64_t limit, void *stream);
+ytm_status ytm_peer_ar_status(void *ctx, int32_t *status_out);
+ytm_status ytm_peer_ar_destroy(void *ctx);
 
 /* Read back the patch picks of the last ytm_train_eval on this workspace:
  * sel i32 [B][C] (-1 = not fired).  Device-to-device copy on `stream`. */

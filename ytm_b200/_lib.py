@@ -23,7 +23,8 @@ EXPORTS = (
     "ytm_train_selection", "ytm_last_error", "ytm_version", "ytm_infer_noalloc",
     "ytm_train_fit_b1", "ytm_probe_lop3", "ytm_infer_include",
     "ytm_encode_thermometer", "ytm_nccl_unique_id", "ytm_nccl_comm_init", "ytm_nccl_comm_destroy",
-    "ytm_train_fit_batches",
+    "ytm_train_fit_batches", "ytm_peer_ar_create", "ytm_peer_ar_open", "ytm_peer_allreduce_i32",
+    "ytm_peer_ar_status", "ytm_peer_ar_destroy",
 )
 
 
@@ -80,7 +81,12 @@ _SIGS = {
     "ytm_nccl_unique_id": ([_P], ct.c_int),
     "ytm_nccl_comm_init": ([_P, _I32, _I32, ct.POINTER(ct.c_void_p)], ct.c_int),
     "ytm_nccl_comm_destroy": ([_P], ct.c_int),
-    "ytm_train_fit_batches": ([_CFG, _P, _P, _P, _P, _P, _P, _I64, _I32, _U64, _I32, _P, _P, _P, _P], ct.c_int),
+    "ytm_train_fit_batches": ([_CFG, _P, _P, _P, _P, _P, _P, _I64, _I32, _U64, _I32, _P, _P, _P, _P, _P], ct.c_int),
+    "ytm_peer_ar_create": ([_I32, _I32, _I64, ct.POINTER(ct.c_void_p), _P], ct.c_int),
+    "ytm_peer_ar_open": ([_P, _P], ct.c_int),
+    "ytm_peer_allreduce_i32": ([_P, _P, _I64, _I64, _P], ct.c_int),
+    "ytm_peer_ar_status": ([_P, ct.POINTER(ct.c_int32)], ct.c_int),
+    "ytm_peer_ar_destroy": ([_P], ct.c_int),
     "ytm_last_error": ([], ct.c_char_p),
     "ytm_version": ([], ct.c_char_p),
 }

@@ -297,6 +297,9 @@ struct B1Ws {
 B1Ws b1_ws_layout(const ytm_config *cfg);
 uint64_t cs_planes_bytes(const ytm_config *cfg);  // class-sum weight planes scratch (eval.cu)
 
+// Peer all-reduce (peer.cu), used by the training loop.
+extern "C" ytm_status ytm_peer_allreduce_i32(void *ctx, int32_t *data, int64_t n, int64_t limit, void *stream);
+
 // Shared launchers (eval.cu) used by several entry points.
 ytm_status launch_ninc(const ytm_config *cfg, const uint32_t *state, int32_t *ninc, cudaStream_t st);
 

@@ -43,8 +43,8 @@ ytm_status ytm_nccl_comm_destroy(void *comm) {
 
 ytm_status ytm_train_fit_batches(const ytm_config *cfg, uint32_t *state, int32_t *weights, const int32_t *bias,
                                  const uint32_t *drop, const uint32_t *lits, const int32_t *Y, int64_t N, int32_t B,
-                                 uint64_t t0, int32_t add_bias, int32_t *patch_w, void *comm, void *workspace,
-                                 void *stream) {
+                                 uint64_t t0, int32_t add_bias, int32_t *patch_w, void *comm, void *peer_ar,
+                                 void *workspace, void *stream) {
     ytm_status rc = check_cfg(cfg);
     if (rc) return rc;
     if (N < 0 || B <= 0) return fail(YTM_ERR_ARG, "bad N or batch size");
@@ -61,11 +61,14 @@ ytm_status ytm_train_fit_batches(const ytm_config *cfg, uint32_t *state, int32_t
         const uint64_t t = t0 + (uint64_t)i;
         if ((rc = ytm_train_eval(cfg, state, weights, bias, drop, lb, b, t, add_bias, cs, patch_w, train_ws, stream)))
             return rc;
-        if (comm &&
-            (rc = nccl_check(ncclAllReduce(cs, cs, (size_t)b * K, ncclInt32, ncclSum, (ncclComm_t)comm,
-                                           as_stream(stream)),
-                             "ncclAllReduce")))
+        if (peer_ar) {
+            if ((rc = ytm_peer_allreduce_i32(peer_ar, cs, (int64_t)b * K, 0, stream))) return rc;
+        } else if (comm &&
+                   (rc = nccl_check(ncclAllReduce(cs, cs, (size_t)b * K, ncclInt32, ncclSum, (ncclComm_t)comm,
+                                                  as_stream(stream)),
+                                    "ncclAllReduce"))) {
             return rc;
+        }
         if ((rc = ytm_train_update(cfg, state, weights, cs, Y + i * K, drop, lb, b, t, nullptr, patch_w, train_ws,
                                    stream)))
             return rc;

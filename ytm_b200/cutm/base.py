@@ -199,6 +199,36 @@ class BaseTM:
             self._comm = comm
         return self._comm
 
+    def _peer_ar(self, n: int):
+        """One-shot peer-memory all-reduce context for the C training loop
+        (all ranks on one node, NCCL group; YTM_ALLREDUCE=nccl opts out), or
+        None.  Made on first use with room for n values."""
+        if self.world == 1 or dist.get_backend(self._pg) != "nccl" or os.environ.get("YTM_ALLREDUCE") == "nccl":
+            return None
+        ctx = getattr(self, "_par", None)
+        if ctx is not None and self._par_n >= n:
+            return ctx
+        import ctypes as ct
+        import socket
+        hosts = [None] * self.world
+        dist.all_gather_object(hosts, socket.gethostname(), group=self._pg)
+        if len(set(hosts)) != 1 or self.world > 8:
+            return None
+        lib = _lib.load()
+        n = max(n, 1 << 16)
+        ctx = ct.c_void_p()
+        h = (ct.c_uint8 * 64)()
+        with torch.cuda.device(self.device):
+            _lib.check(lib.ytm_peer_ar_create(self.rank, self.world, n, ct.byref(ctx), h), "ytm_peer_ar_create")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(h), group=self._pg)
+        allh = (ct.c_uint8 * (64 * self.world)).from_buffer_copy(b"".join(handles))
+        with torch.cuda.device(self.device):
+            _lib.check(lib.ytm_peer_ar_open(ctx, allh), "ytm_peer_ar_open")
+        dist.barrier(group=self._pg)
+        self._par, self._par_n = ctx, n
+        return ctx
+
     def _allreduce(self, t: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
             return t
@@ -306,10 +336,11 @@ class BaseTM:
             self.sample_counter = t + N
             self.last_class_sums = self.engine.b1_class_sums(N)
             return
-        if hasattr(self.engine, "train_fit_batches") and (self.world == 1 or self._nccl() is not None):
+        if hasattr(self.engine, "train_fit_batches") and (self.world == 1 or dist.get_backend(self._pg) == "nccl"):
             # the batch loop and the class-sum all-reduce queued from C
+            par = self._peer_ar(min(batch_size, N) * self.number_of_outputs)
             self.last_class_sums = self.engine.train_fit_batches(lits, Y, batch_size, t, drop, self.rank == 0,
-                                                                 self._nccl())
+                                                                 None if par is not None else self._nccl(), par)
             self.sample_counter = t + N
             return
         for i in range(0, N, batch_size):

@@ -202,7 +202,7 @@ class CudaEngine:
                   "ytm_train_fit_b1")
 
     def train_fit_batches(self, lits: torch.Tensor, Y: torch.Tensor, B: int, t0: int, drop: torch.Tensor | None,
-                          add_bias: bool, comm=None) -> torch.Tensor:
+                          add_bias: bool, comm=None, peer_ar=None) -> torch.Tensor:
         """Mini-batch training over all samples of lits in order, queued from C
         (eval, NCCL all-reduce of the class sums on `comm` if given, feedback
         per batch).  Returns the class sums [b, K] of the last batch."""
@@ -214,7 +214,7 @@ class CudaEngine:
         with torch.cuda.device(self.device):
             check(self.lib.ytm_train_fit_batches(self._cfg, _p(self.state), _p(self.weights), _p(self.bias), _p(drop),
                                                  _p(lits), _p(Y), N, B, int(t0), int(bool(add_bias)),
-                                                 _p(self.patch_w), comm, _p(ws), self._stream()),
+                                                 _p(self.patch_w), comm, peer_ar, _p(ws), self._stream()),
                   "ytm_train_fit_batches")
         last = N - (N - 1) // B * B
         return ws[:last * self.K * 4].view(torch.int32).view(last, self.K)
