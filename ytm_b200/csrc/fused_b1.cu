@@ -21,10 +21,10 @@
 
 namespace ytm {
 
-#ifndef YTM_FB_CPB
-#define YTM_FB_CPB 64
-#endif
-constexpr int FB_WARPS = 8, FB_CPB = YTM_FB_CPB;  // warps and clauses per block
+// warps per block; clauses per block (CPB) is a template parameter: 64 for
+// single-patch models, 16 for convolutional ones, whose per-clause patch scan
+// wants more blocks in flight (measured: config 3 17k -> 31k samples/s)
+constexpr int FB_WARPS = 8;
 
 
 B1Ws b1_ws_layout(const ytm_config *cfg) {
@@ -38,12 +38,12 @@ B1Ws b1_ws_layout(const ytm_config *cfg) {
     return l;
 }
 
-// Block = 8 warps owning FB_CPB clauses.  Thresholds of sample i
+// Block = 8 warps owning CPB clauses.  Thresholds of sample i
 // are computed once per block; decisions run one clause per thread (the
 // Philox class draws of 32 clauses share each warp instruction); then each
 // warp streams the words of its clauses (8 per warp), applying the events and
 // evaluating sample i+1.
-template <int NB>
+template <int NB, int CPB>
 __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     ytm_config cfg, uint32_t *__restrict__ state, int32_t *__restrict__ weights, const int32_t *__restrict__ bias,
     const uint32_t *__restrict__ drop, const uint32_t *__restrict__ lits, const int32_t *__restrict__ Y, int64_t i,
@@ -60,8 +60,8 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     const int KB = (nk + 31) >> 5;                       // 32-class chunks per clause
     uint64_t *thr_s = (uint64_t *)smraw;                 // [K]  threshold | target bit
     int32_t *cs_blk = (int32_t *)(thr_s + K);            // [K]
-    uint32_t *ev_s = (uint32_t *)(cs_blk + K);           // [FB_CPB][KB][3]: any, type Ia, type II
-    uint32_t *lw_s = ev_s + FB_CPB * KB * 3;              // [FB_WARPS][W] non-zero include words (P > 1)
+    uint32_t *ev_s = (uint32_t *)(cs_blk + K);           // [CPB][KB][3]: any, type Ia, type II
+    uint32_t *lw_s = ev_s + CPB * KB * 3;              // [FB_WARPS][W] non-zero include words (P > 1)
     uint32_t *li_s = lw_s + FB_WARPS * W;                 // [FB_WARPS][W] their include masks
     uint32_t *mb_s = li_s + FB_WARPS * W;                 // [FB_WARPS][PW] patch match bits
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     __syncthreads();
 
     // ---- 1. decisions of sample i: one clause per thread
-    if (do_update && threadIdx.x < FB_CPB) {
+    if (do_update && threadIdx.x < CPB) {
         const int c = (int)threadIdx.x * G + blockIdx.x;
         uint32_t *ev = ev_s + threadIdx.x * KB * 3;
         for (int q = 0; q < KB * 3; ++q) ev[q] = 0u;
@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     const uint32_t max_s = (uint32_t)(cfg.max_state + cfg.state_offset);
     const uint32_t zero_s = (uint32_t)cfg.state_offset;
     const uint32_t *x_next = lits + e_next * P * W;  // patch 0 of sample i+1 (single-patch eval)
-    constexpr int CPW = FB_CPB / FB_WARPS;  // clauses per warp
+    constexpr int CPW = CPB / FB_WARPS;  // clauses per warp
     bool has_ev[CPW];
 #pragma unroll
     for (int q = 0; q < CPW; ++q) {
@@ -332,6 +332,44 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
 
 using namespace ytm;
 
+template <int NB, int CPB>
+static ytm_status launch_b1(const ytm_config *cfg, uint32_t *state, int32_t *weights, const int32_t *bias,
+                            const uint32_t *drop, const uint32_t *lits, const int32_t *Y, int64_t N, uint64_t t0,
+                            int32_t *cs_ring, int32_t *sel, int32_t *ninc, int32_t *patch_w, cudaStream_t st) {
+    ytm_status rc;
+    const int C = cfg->clause_count;
+    const int blocks = (int)cdiv(C, CPB);
+    const int nk = cfg->coalesced ? cfg->n_classes : 1;
+    size_t smem = (size_t)cfg->n_classes * 12 + (size_t)CPB * ((nk + 31) / 32) * 12 + 16;
+    if (cfg->patches > 1) smem += (size_t)FB_WARPS * (2 * cfg->words + (cfg->patches + 31) / 32) * 4;
+    if (smem > 200 * 1024) return fail(YTM_ERR_UNSUPPORTED, "ytm_train_fit_b1: literal vector too long");
+    if (smem > 48 * 1024 &&
+        (rc = cuda_check(cudaFuncSetAttribute(k_fused_b1<NB, CPB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)smem), "fused b1 smem")))
+        return rc;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)blocks);
+    lc.blockDim = dim3(FB_WARPS * 32);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    const ytm_config c = *cfg;
+    for (int64_t i = -1; i < N; ++i) {  // i = -1: the prologue evaluating sample 0
+        const int64_t ii = i < 0 ? 0 : i;
+        const int upd = i < 0 ? 0 : 1;
+        const RoundKeys rk = round_keys(c.seed, (uint32_t)((t0 + (uint64_t)ii) >> 32));  // keys of sample ii
+        if ((rc = cuda_check(cudaLaunchKernelEx(&lc, k_fused_b1<NB, CPB>, c, state, weights, bias, drop, lits, Y, ii,
+                                                N, t0, upd, cs_ring, sel, ninc, patch_w, rk),
+                             "fused b1 launch")))
+            return rc;
+    }
+    return YTM_OK;
+}
+
 extern "C" ytm_status ytm_train_fit_b1(const ytm_config *cfg, uint32_t *state, int32_t *weights, const int32_t *bias,
                                        const uint32_t *drop, const uint32_t *lits, const int32_t *Y, int64_t N,
                                        uint64_t t0, int32_t *patch_w, void *workspace, void *stream) {
@@ -350,38 +388,13 @@ extern "C" ytm_status ytm_train_fit_b1(const ytm_config *cfg, uint32_t *state, i
     int32_t *sel = (int32_t *)(ws + l.fired);
     int32_t *ninc = (int32_t *)(ws + l.ninc);
     if ((rc = cuda_check(cudaMemsetAsync(cs_ring, 0, 3 * (size_t)cfg->n_classes * 4, st), "memset"))) return rc;
-    const int C = cfg->clause_count;
-    const int blocks = (int)cdiv(C, FB_CPB);
-    const int nk = cfg->coalesced ? cfg->n_classes : 1;
-    size_t smem = (size_t)cfg->n_classes * 12 + (size_t)FB_CPB * ((nk + 31) / 32) * 12 + 16;
-    if (cfg->patches > 1) smem += (size_t)FB_WARPS * (2 * cfg->words + (cfg->patches + 31) / 32) * 4;
-    if (smem > 200 * 1024) return fail(YTM_ERR_UNSUPPORTED, "ytm_train_fit_b1: literal vector too long");
+    const int cpb = cfg->patches > 1 ? 16 : 64;
     YTM_DISPATCH_PLANES(cfg->planes, {
-        if (smem > 48 * 1024) {
-            if ((rc = cuda_check(cudaFuncSetAttribute(k_fused_b1<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                      (int)smem), "fused b1 smem")))
-                return rc;
-        }
-        cudaLaunchConfig_t lc = {};
-        lc.gridDim = dim3((unsigned)blocks);
-        lc.blockDim = dim3(FB_WARPS * 32);
-        lc.dynamicSmemBytes = smem;
-        lc.stream = st;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        lc.attrs = attr;
-        lc.numAttrs = 1;
-        const ytm_config c = *cfg;
-        for (int64_t i = -1; i < N; ++i) {  // i = -1: the prologue evaluating sample 0
-            const int64_t ii = i < 0 ? 0 : i;
-            const int upd = i < 0 ? 0 : 1;
-            const RoundKeys rk = round_keys(c.seed, (uint32_t)((t0 + (uint64_t)ii) >> 32));  // keys of sample ii
-            if ((rc = cuda_check(cudaLaunchKernelEx(&lc, k_fused_b1<NB>, c, state, weights, bias, drop, lits, Y, ii, N,
-                                                    t0, upd, cs_ring, sel, ninc, patch_w, rk),
-                                 "fused b1 launch")))
-                return rc;
-        }
+        rc = cpb == 16 ? launch_b1<NB, 16>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel, ninc,
+                                           patch_w, st)
+                       : launch_b1<NB, 64>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel, ninc,
+                                           patch_w, st);
+        if (rc) return rc;
     });
     return launch_check("fused b1");
 }
