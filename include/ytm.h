@@ -290,6 +290,10 @@ const char *ytm_last_error(void);
 /* Library version string. */
 const char *ytm_version(void);
 
+/* sizeof(ytm_config) as compiled into the library (bindings check their
+ * mirror of the struct against it). */
+int32_t ytm_config_size(void);
+
 #ifdef __cplusplus
 }
 #endif

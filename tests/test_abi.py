@@ -70,3 +70,22 @@ def test_workspace_sizes_grow_with_batch():
     a = lib.ytm_workspace_bytes(cfg, _lib.YTM_OP_TRAIN, 1)
     b = lib.ytm_workspace_bytes(cfg, _lib.YTM_OP_TRAIN, 8)
     assert 0 < a < b and a % 256 == 0
+
+
+def test_config_struct_size_matches_binding():
+    import ctypes as ct
+    assert _lib.load().ytm_config_size() == ct.sizeof(_lib.Config)
+
+
+def test_entry_points_reject_bad_arguments_without_a_gpu():
+    """Argument checks run before any CUDA call: null pointers, negative
+    sizes and out-of-range shards come back as status codes."""
+    import ctypes as ct
+    lib = _lib.load()
+    cfg = _lib.make_config(clauses_per_class=8, T=5, s=3.0, dim=(16, 1, 1), n_classes=2)
+    assert lib.ytm_infer(ct.byref(cfg), None, None, None, None, 4, None, None, None) == 1
+    assert lib.ytm_encode(ct.byref(cfg), None, -1, None, None, None) == 1
+    assert lib.ytm_train_eval(ct.byref(cfg), None, None, None, None, None, 0, 0, 0, None, None, None, None) == 1
+    assert lib.ytm_peer_allreduce_i32(None, None, 4, 0, None) == 1
+    assert lib.ytm_infer(ct.byref(cfg), None, None, None, None, 0, None, None, None) == 0  # N = 0: nothing to do
+    assert lib.ytm_last_error()  # the last failure left a message

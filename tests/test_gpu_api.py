@@ -177,3 +177,19 @@ def test_pytm_front_end_matches_oracle_pytm_rules():
     preds, cs = tm.predict(X, return_cs=True)
     np.testing.assert_array_equal(cs, o.infer(ta, w, lits).astype(np.float32))
     assert (ta != 31).any()  # training moved the states
+
+
+def test_empty_and_single_sample_inputs():
+    tm = MultiClassTM(**KW)
+    X0 = np.zeros((0, 64), np.uint32)
+    assert tm.encode(X0).shape == (0, tm.number_of_patches, tm.number_of_literal_chunks)
+    preds, cs = tm.predict(X0)
+    assert preds.shape == (0,) and cs.shape == (0, 3)
+    tm.fit(X0, np.zeros(0, np.uint32))
+    assert tm.sample_counter == 0
+    X1, y1 = data(1)
+    tm.fit(X1, y1)
+    tm.fit(X1, y1, batch_size=4)
+    assert tm.sample_counter == 2
+    assert tm.transform(X1).shape == (1, tm.number_of_clauses)
+    assert tm.transform_patchwise(X1).shape == (1, tm.number_of_clauses, tm.number_of_patches)

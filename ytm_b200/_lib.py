@@ -24,7 +24,7 @@ EXPORTS = (
     "ytm_train_fit_b1", "ytm_probe_lop3", "ytm_infer_include",
     "ytm_encode_thermometer", "ytm_nccl_unique_id", "ytm_nccl_comm_init", "ytm_nccl_comm_destroy",
     "ytm_train_fit_batches", "ytm_peer_ar_create", "ytm_peer_ar_open", "ytm_peer_allreduce_i32",
-    "ytm_peer_ar_status", "ytm_peer_ar_destroy",
+    "ytm_peer_ar_status", "ytm_peer_ar_destroy", "ytm_config_size",
 )
 
 
@@ -89,6 +89,7 @@ _SIGS = {
     "ytm_peer_ar_destroy": ([_P], ct.c_int),
     "ytm_last_error": ([], ct.c_char_p),
     "ytm_version": ([], ct.c_char_p),
+    "ytm_config_size": ([], ct.c_int32),
 }
 
 _lib = None
@@ -107,6 +108,9 @@ def load(path: str = LIB_PATH):
         f = getattr(lib, name)
         f.argtypes = args
         f.restype = res
+    if lib.ytm_config_size() != ct.sizeof(Config):
+        raise YTMError(f"{path} was built with a different ytm_config ({lib.ytm_config_size()} bytes, binding "
+                       f"{ct.sizeof(Config)}): rebuild it")
     _lib = lib
     return lib
 

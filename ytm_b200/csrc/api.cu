@@ -190,4 +190,6 @@ const char *ytm_last_error(void) { return g_err.c_str(); }
 
 const char *ytm_version(void) { return "ytm-b200 0.1.0 (sm_100a)"; }
 
+int32_t ytm_config_size(void) { return (int32_t)sizeof(ytm_config); }
+
 }  // extern "C"

@@ -314,15 +314,18 @@ __global__ void k_wplanes(const int32_t *__restrict__ w, const int32_t *__restri
     }
 }
 
-// WARP: one warp per (sample, 16 classes), lanes striding over the clause
-// words (few samples: training batches); else one thread per (sample, 16
-// classes) walking all words (many samples: inference).
+// WARP: one warp per (sample, 16 classes, segment of seg_words clause words),
+// lanes striding over the segment's words (few samples: training batches);
+// with more than one segment (gridDim.y) the partial sums are added
+// atomically onto cs, which then holds the bias already.  Else one thread per
+// (sample, 16 classes) walking all words (many samples: inference).
 template <bool WARP>
 __global__ void __launch_bounds__(256) k_cs_planes(const uint32_t *__restrict__ fired,
                                                    const uint32_t *__restrict__ keep,
                                                    const uint32_t *__restrict__ planes,
                                                    const int32_t *__restrict__ wmax, const int32_t *__restrict__ bias,
-                                                   int C, int K, int64_t N, int32_t *__restrict__ cs) {
+                                                   int C, int K, int64_t N, int seg_words,
+                                                   int32_t *__restrict__ cs) {
     const int lane = WARP ? (threadIdx.x & 31) : 0;
     const int step = WARP ? 32 : 1;
     const int CWn = (C + 31) / 32;
@@ -342,7 +345,9 @@ __global__ void __launch_bounds__(256) k_cs_planes(const uint32_t *__restrict__ 
         for (int j = 0; j < CSP_KCH; ++j) acc[j] = 0u;
         uint32_t nf = 0u;
         const uint32_t *fr = fired + n * CWn;
-        for (int wd = lane; wd < CWn; wd += step) {
+        const int wlo = WARP ? (int)blockIdx.y * seg_words : 0;
+        const int whi = WARP ? min(CWn, wlo + seg_words) : CWn;
+        for (int wd = wlo + lane; wd < whi; wd += step) {
             const uint32_t f = fr[wd] & keep[wd];
             if (!f) continue;
             nf += (uint32_t)__popc(f);
@@ -361,7 +366,12 @@ __global__ void __launch_bounds__(256) k_cs_planes(const uint32_t *__restrict__ 
         for (int j = 0; j < CSP_KCH; ++j) {
             if (j < kn) {
                 const uint32_t t = WARP ? __reduce_add_sync(0xFFFFFFFFu, acc[j]) : acc[j];
-                if (lane == 0) cs[n * K + k0 + j] = (int32_t)(t - off * nf) + (bias ? bias[k0 + j] : 0);
+                if (lane == 0) {
+                    if (WARP && gridDim.y > 1)
+                        atomicAdd(&cs[n * K + k0 + j], (int32_t)(t - off * nf));
+                    else
+                        cs[n * K + k0 + j] = (int32_t)(t - off * nf) + (bias ? bias[k0 + j] : 0);
+                }
             }
         }
     }
@@ -393,11 +403,21 @@ static ytm_status launch_cs_planes(const uint32_t *fired, const int32_t *ninc, c
     const int64_t units = N * (int64_t)cdiv(K, CSP_KCH);
     const int sms = sm_count();
     if (units < (int64_t)sms * 32) {
-        k_cs_planes<true><<<(unsigned)std::min<int64_t>(cdiv(units * 32, 256), (int64_t)sms * 64), 256, 0, st>>>(
-            fired, keep, planes, wmax, bias, C, K, N, cs);
+        // split the clause words so that about 16 warps per SM run; a segment
+        // keeps at least one word per lane
+        int64_t segs = std::max<int64_t>(1, (int64_t)sms * 16 / units);
+        segs = std::min<int64_t>(segs, std::max<int64_t>(1, CW / 32));
+        const int seg_words = (int)cdiv(CW, segs);
+        segs = cdiv(CW, seg_words);
+        if (segs > 1) {
+            k_cs_init<<<grid1(N * K), 256, 0, st>>>(cs, bias, N, K);
+            if ((rc = launch_check("class sums init"))) return rc;
+        }
+        k_cs_planes<true><<<dim3((unsigned)cdiv(units * 32, 256), (unsigned)segs), 256, 0, st>>>(
+            fired, keep, planes, wmax, bias, C, K, N, seg_words, cs);
     } else {
         k_cs_planes<false><<<(unsigned)std::min<int64_t>(cdiv(units, 256), (int64_t)sms * 64), 256, 0, st>>>(
-            fired, keep, planes, wmax, bias, C, K, N, cs);
+            fired, keep, planes, wmax, bias, C, K, N, 0, cs);
     }
     return launch_check("class sums");
 }
