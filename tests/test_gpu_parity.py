@@ -96,6 +96,12 @@ TRAIN_CASES = {
     "noneg_noloc": (dict(number_of_clauses_per_class=16, T=10, s=3.0, dim=(8, 8, 1), n_classes=2,
                          patch_dim=(4, 4), encode_loc=False, append_negated=False), 1),
     "many_classes": (dict(number_of_clauses_per_class=70, T=50, s=10.0, dim=(30, 1, 1), n_classes=70), 2),
+    # 289 patches: three 128-patch tiles of the sparse match, the last ragged
+    "conv_tiles_b2": (dict(number_of_clauses_per_class=20, T=20, s=3.0, dim=(19, 19, 2), n_classes=3,
+                           patch_dim=(3, 3)), 2),
+    # 37 literal words: more include words per clause than lanes
+    "conv_wide_b4": (dict(number_of_clauses_per_class=20, T=20, s=3.0, dim=(12, 12, 16), n_classes=3,
+                          patch_dim=(6, 6)), 4),
 }
 
 
@@ -259,3 +265,29 @@ def test_sample_counter_crossing_2_32(path):
         e.train_fit_b1(lits, Yd, t0, None)
     np.testing.assert_array_equal(e.get_ta_state(), ta)
     np.testing.assert_array_equal(host(e.weights), w)
+
+
+@pytest.mark.parametrize("case,p_inc", [("conv_wide_b4", 0.02), ("conv_wide_b4", 0.3), ("conv_tiles_b2", 0.05),
+                                        ("conv_tiles_b2", 0.0)])
+def test_patch_match_on_random_states(case, p_inc):
+    """Patch picks and class sums of one training batch from random TA
+    states with a given share of included literals (dense and sparse include
+    words, empty clauses, more include words than lanes)."""
+    kw, bs = TRAIN_CASES[case]
+    o = O.Oracle(**oracle_kwargs(kw, 5))
+    e = engine_for(kw, 5)
+    rng = np.random.default_rng(int(p_inc * 100) + 1)
+    ta = np.where(rng.random((o.C, o.L)) < p_inc, rng.integers(o.half_state + 1, 2 * o.half_state, (o.C, o.L)),
+                  rng.integers(0, o.half_state + 1, (o.C, o.L))).astype(np.uint32)
+    ta[::7] = rng.integers(0, o.half_state + 1, (len(ta[::7]), o.L))  # every 7th clause empty
+    e.set_ta_state(ta)
+    D = kw["dim"][0] * kw["dim"][1] * kw["dim"][2]
+    X = (rng.random((bs, D)) < 0.5).astype(np.uint32)
+    lits_h = o.encode(X)
+    Y = O.encode_Y_multiclass(rng.integers(0, kw["n_classes"], bs), kw["n_classes"], kw["T"])
+    w, pw = o.init_weights(), np.zeros((o.C, o.P), np.int32)
+    cs_o, sel_o = o.train_batch(ta.copy(), w, pw, lits_h, Y, 99, drop=None)
+    cs = e.train_eval(dev(lits_h), 99, None, add_bias=True)
+    np.testing.assert_array_equal(host(cs), cs_o)
+    np.testing.assert_array_equal(host(e.selection(bs)), sel_o)
+    assert (sel_o >= 0).any() and (sel_o < 0).any() if p_inc > 0 else (sel_o >= 0).all()

@@ -51,6 +51,10 @@ TrainWs train_ws_layout(const ytm_config *cfg, int64_t B) {
     l.sel = o;   o = align_up(o + (uint64_t)B * C * 4, 256);
     l.thr = o;   o = align_up(o + (uint64_t)B * K * 8, 256);
     l.pair = o;  o = align_up(o + (uint64_t)B * 2 * 4, 256);
+    // compacted include words of every clause (sparse patch match, P > 1)
+    const uint64_t Wd = P > 1 ? (uint64_t)cfg->words : 0;
+    l.lcnt = o;  o = align_up(o + (P > 1 ? C * 4 : 0), 256);
+    l.lent = o;  o = align_up(o + C * Wd * 8, 256);
     l.total = o;
     return l;
 }

@@ -113,6 +113,133 @@ static ytm_status launch_match(const uint32_t *inc, const uint32_t *lits, int64_
     return launch_check("clause match");
 }
 
+// ---- sparse patch match ---------------------------------------------------
+// Trained clauses include few literals: most include words are zero.  The
+// compacted list of a clause's non-zero include words (index, word) lets a
+// warp test 128 patches against only those words.  The patch tile of one
+// sample is staged word-major in shared memory, [W][SP_STRIDE] with
+// SP_STRIDE = 129, so that the 32 lanes (32 consecutive patches) read 32
+// banks and the staging writes (consecutive words) do too.
+
+static unsigned grid1(int64_t threads);
+
+constexpr int SP_PT = 128, SP_STRIDE = SP_PT + 1, SP_WARPS = 32;
+
+inline size_t sparse_smem_bytes(int W) { return (size_t)W * SP_STRIDE * 4; }
+inline bool sparse_match_fits(int W) { return sparse_smem_bytes(W) <= 220 * 1024; }
+
+// One warp per clause: cnt[c] = non-zero include words, ent[c][0..cnt) =
+// (word index, include word) in word order.
+__global__ void k_compact(const uint32_t *__restrict__ inc, int C, int W, int32_t *__restrict__ cnt,
+                          uint2 *__restrict__ ent) {
+    const int lane = threadIdx.x & 31;
+    for (int64_t c = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; c < C;
+         c += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+        const uint32_t *row = inc + c * W;
+        uint2 *out = ent + c * W;
+        int base = 0;
+        for (int w0 = 0; w0 < W; w0 += 32) {
+            const int w = w0 + lane;
+            const uint32_t v = w < W ? row[w] : 0u;
+            const uint32_t m = __ballot_sync(0xFFFFFFFFu, v != 0u);
+            if (v) out[base + __popc(m & ((1u << lane) - 1u))] = make_uint2((uint32_t)w, v);
+            base += __popc(m);
+        }
+        if (lane == 0) cnt[c] = base;
+    }
+}
+
+// mbits[n][c][PW] = patches of sample n that clause c matches (an empty
+// clause matches all).  Grid: x = 128-patch tiles, y = clause blocks of cpb
+// clauses, z = samples.  Every mbits word is written once (no clear needed).
+__global__ void __launch_bounds__(SP_WARPS * 32, 2) k_match_sparse(const uint32_t *__restrict__ lits,
+                                                                const int32_t *__restrict__ cnt,
+                                                                const uint2 *__restrict__ ent, int C, int W, int P,
+                                                                int cpb, uint32_t *__restrict__ mbits) {
+    extern __shared__ uint32_t sl[];  // [W][SP_STRIDE]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t n = blockIdx.z;
+    const int p0 = blockIdx.x * SP_PT;
+    const int np = min(SP_PT, P - p0);
+    const uint32_t *src = lits + ((int64_t)n * P + p0) * W;
+    for (int idx = tid; idx < SP_PT * W; idx += SP_WARPS * 32) {
+        const int p = idx / W, w = idx - p * W;
+        sl[w * SP_STRIDE + p] = p < np ? __ldg(&src[idx]) : 0u;
+    }
+    __syncthreads();
+    const int PW = (P + 31) / 32;
+    const int c_lo = blockIdx.y * cpb, c_hi = min(C, c_lo + cpb);
+    const int ng = (np + 31) / 32;
+    // the count and the first 32 entries of the next clause are loaded while
+    // the current one is tested (entries past the count are never used; a
+    // row holds W entries, so lanes below W stay inside it)
+    int c = c_lo + warp;
+    int k_nx = 0;
+    uint2 e_nx = make_uint2(0u, 0u);
+    if (c < c_hi) {
+        k_nx = __ldg(&cnt[c]);
+        if (lane < W) e_nx = ent[(int64_t)c * W + lane];
+    }
+    for (; c < c_hi; c += SP_WARPS) {
+        const int k = k_nx;
+        uint2 my = e_nx;
+        const int cn = c + SP_WARPS;
+        if (cn < c_hi) {
+            k_nx = __ldg(&cnt[cn]);
+            if (lane < W) e_nx = ent[(int64_t)cn * W + lane];
+        }
+        const uint2 *e = ent + (int64_t)c * W;
+        uint32_t v0 = 0u, v1 = 0u, v2 = 0u, v3 = 0u;
+        for (int e0 = 0; e0 < k; e0 += 32) {
+            if (e0 > 0) my = e0 + lane < k ? e[e0 + lane] : make_uint2(0u, 0u);
+            const int m = min(32, k - e0);
+            for (int j = 0; j < m; ++j) {
+                const uint32_t off = __shfl_sync(0xFFFFFFFFu, my.x, j) * SP_STRIDE + lane;
+                const uint32_t iv = __shfl_sync(0xFFFFFFFFu, my.y, j);
+                v0 |= iv & ~sl[off];
+                v1 |= iv & ~sl[off + 32];
+                v2 |= iv & ~sl[off + 64];
+                v3 |= iv & ~sl[off + 96];
+                // every patch of the tile already violated: nothing can match
+                if ((j & 3) == 3 && __all_sync(0xFFFFFFFFu, (v0 != 0u) & (v1 != 0u) & (v2 != 0u) & (v3 != 0u)))
+                    goto done;
+            }
+        }
+    done:
+        const uint32_t v[4] = {v0, v1, v2, v3};
+        uint32_t *o = mbits + ((int64_t)n * C + c) * PW + (p0 >> 5);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            if (g < ng) {
+                const uint32_t b = __ballot_sync(0xFFFFFFFFu, v[g] == 0u && g * 32 + lane < np);
+                if (lane == 0) o[g] = b;
+            }
+        }
+    }
+}
+
+static ytm_status launch_match_sparse(const uint32_t *inc, const uint32_t *lits, int64_t B, int C, int W, int P,
+                                      int32_t *cnt, uint2 *ent, uint32_t *mbits, cudaStream_t st) {
+    k_compact<<<grid1((int64_t)C * 32), 256, 0, st>>>(inc, C, W, cnt, ent);
+    ytm_status rc = launch_check("include compaction");
+    if (rc) return rc;
+    const size_t smem = sparse_smem_bytes(W);
+    if (smem > 48 * 1024 &&
+        (rc = cuda_check(cudaFuncSetAttribute(k_match_sparse, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                         "sparse match smem")))
+        return rc;
+    if (B > 65535) return fail(YTM_ERR_UNSUPPORTED, "batch above 65535 samples");
+    const int tiles = (int)cdiv(P, SP_PT);
+    // about two CTAs per SM over the whole grid; at least 32 clauses a block
+    int64_t cb = std::max<int64_t>(1, (int64_t)sm_count() * 2 / ((int64_t)tiles * B));
+    cb = std::min<int64_t>(cb, std::max<int64_t>(1, C / 32));
+    const int cpb = (int)cdiv(C, cb);
+    cb = cdiv(C, cpb);
+    k_match_sparse<<<dim3((unsigned)tiles, (unsigned)cb, (unsigned)B), SP_WARPS * 32, smem, st>>>(lits, cnt, ent, C, W,
+                                                                                               P, cpb, mbits);
+    return launch_check("sparse match");
+}
+
 // Training evaluation of single-patch models in one kernel: the tile's
 // matches give each (sample, clause) its pick (patch 0, or -1 when it does not
 // fire or is dropped: fast_eval + select_active, kernel.cu:255-316), the fired
@@ -588,10 +715,17 @@ ytm_status ytm_train_eval(const ytm_config *cfg, const uint32_t *state, const in
                                                                            nullptr, cs);
         return launch_check("train eval");
     }
-    // match bits and fired bits are adjacent in the workspace: one clear
-    if ((rc = cuda_check(cudaMemsetAsync(mbits, 0, l.sel - l.mbits, st), "memset"))) return rc;
     // training semantics: an empty clause matches every patch (kernel.cu:273-276)
-    if ((rc = launch_match<MODE_PBITS>(inc, lits, (int64_t)B * P, C, W, P, mbits, st))) return rc;
+    if (P > 1 && sparse_match_fits(W)) {
+        if ((rc = cuda_check(cudaMemsetAsync(fired, 0, l.sel - l.fired, st), "memset"))) return rc;
+        if ((rc = launch_match_sparse(inc, lits, B, C, W, P, (int32_t *)(ws + l.lcnt), (uint2 *)(ws + l.lent),
+                                      mbits, st)))
+            return rc;
+    } else {
+        // match bits and fired bits are adjacent in the workspace: one clear
+        if ((rc = cuda_check(cudaMemsetAsync(mbits, 0, l.sel - l.mbits, st), "memset"))) return rc;
+        if ((rc = launch_match<MODE_PBITS>(inc, lits, (int64_t)B * P, C, W, P, mbits, st))) return rc;
+    }
     int32_t *wmax = (int32_t *)(ws + l.total);  // the class-sum planes scratch starts with the weight range
     k_pick<<<grid1((int64_t)B * C), 256, 0, st>>>(*cfg, mbits, drop, B, t0, sel, fired, patch_w, wmax);
     if ((rc = launch_check("patch pick"))) return rc;

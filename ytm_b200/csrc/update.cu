@@ -14,6 +14,10 @@
 //     per instruction), and store the planes once.
 // The state therefore makes one read-modify-write trip through HBM per chunk,
 // however many events the chunk holds.
+//
+// Small batches (at most 32 samples) run the same steps with one WARP per
+// clause (WPC): the decision phases then cost warp syncs instead of CTA
+// barriers, and a block holds 8 clauses.
 #include "common.cuh"
 
 namespace ytm {
@@ -36,6 +40,19 @@ __global__ void k_thresholds(const int32_t *__restrict__ cs, const int32_t *__re
     }
 }
 
+template <bool WPC>
+__device__ __forceinline__ void block_sync() {
+    if (WPC)
+        __syncwarp();
+    else
+        __syncthreads();
+}
+
+static __host__ __device__ inline size_t update_smem(int nk, int bc) {
+    return (size_t)nk * 4 + (size_t)bc * 4 + 4 + (size_t)bc * nk * 4 + (size_t)bc * nk + 16;
+}
+static __host__ __device__ inline size_t update_smem_aligned(int nk, int bc) { return (update_smem(nk, bc) + 15) & ~(size_t)15; }
+
 enum : uint32_t { EV_NONE = 0, EV_T1A = 1, EV_T1B = 2, EV_T2 = 3 };
 
 __global__ void k_pairs(uint64_t seed, const int32_t *__restrict__ Y, int B, int K, uint64_t t0,
@@ -48,7 +65,7 @@ __global__ void k_pairs(uint64_t seed, const int32_t *__restrict__ Y, int B, int
     }
 }
 
-template <int NB>
+template <int NB, bool WPC>
 #ifndef YTM_UPD_MINB
 #define YTM_UPD_MINB 4  // 64 registers: measured fastest (no spills)
 #endif
@@ -59,32 +76,40 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                                                 const int32_t *__restrict__ sel, int32_t *__restrict__ patch_w,
                                                 int BC, const RoundKeys rk, int rk_ok,
                                                 const int32_t *__restrict__ pair, int count_patch) {
-    extern __shared__ __align__(16) unsigned char smraw[];
+    extern __shared__ __align__(16) unsigned char small[];
     const int C = cfg.clause_count, W = cfg.words, K = cfg.n_classes, P = cfg.patches;
-    const int c = blockIdx.x;
+    const int c = WPC ? (int)(blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) : (int)blockIdx.x;
+    if (c >= C) return;
     const uint32_t g = (uint32_t)(cfg.clause_lo + c);
     if (drop && drop[c] == 1u) return;  // kernel.cu:555
     const int k0 = cfg.coalesced ? 0 : (int)(g / (uint32_t)cfg.clauses_per_class);
     const int nk = cfg.coalesced ? K : 1;
+    unsigned char *smraw = WPC ? small + (threadIdx.x >> 5) * update_smem_aligned(nk, BC) : small;
     int32_t *wk = (int32_t *)smraw;                       // [nk]
     int32_t *sel_s = wk + nk;                             // [BC]
     int32_t *cnt = sel_s + BC;                            // [1]
     uint32_t *list = (uint32_t *)(cnt + 1);               // [BC * nk]
     uint8_t *evt = (uint8_t *)(list + BC * nk);           // [BC * nk]
-    const int tid = threadIdx.x, nt = blockDim.x;
+    const int tid = WPC ? (int)(threadIdx.x & 31) : (int)threadIdx.x, nt = WPC ? 32 : (int)blockDim.x;
     // include count of the batch-start state (pack_clauses, kernel.cu:155-204):
-    // this CTA alone writes the clause, so its top plane is still unchanged
-    __shared__ int ninc_s;
-    if (tid == 0) ninc_s = 0;
-    __syncthreads();
-    {
+    // this CTA alone writes the clause, so its top plane is still unchanged.
+    // Not needed when the cap cannot bind.
+    bool ok_inc = true;
+    if (cfg.max_included_literals < cfg.literals) {
         int n = 0;
         for (int w = tid; w < W; w += nt) n += __popc(state[((int64_t)(NB - 1) * C + c) * W + w]);
         for (int o = 16; o; o >>= 1) n += __shfl_xor_sync(0xFFFFFFFFu, n, o);
-        if ((tid & 31) == 0 && n) atomicAdd(&ninc_s, n);
+        if (WPC) {
+            ok_inc = n <= cfg.max_included_literals;
+        } else {
+            __shared__ int ninc_s;
+            if (tid == 0) ninc_s = 0;
+            __syncthreads();
+            if ((tid & 31) == 0 && n) atomicAdd(&ninc_s, n);
+            __syncthreads();
+            ok_inc = ninc_s <= cfg.max_included_literals;
+        }
     }
-    __syncthreads();
-    const bool ok_inc = ninc_s <= cfg.max_included_literals;
     int fired_count = 0;  // single-patch models: patch 0 picks of this clause (select_active, kernel.cu:305)
     const uint32_t max_s = (uint32_t)(cfg.max_state + cfg.state_offset);
     const uint32_t zero_s = (uint32_t)cfg.state_offset;
@@ -97,7 +122,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
             sel_s[q] = sel[(int64_t)(b0 + q) * C + c];
             fired_count += sel_s[q] >= 0;
         }
-        __syncthreads();
+        block_sync<WPC>();
         // 1a. the chunk's Q-selection and update draws, all (sample, class)
         //     pairs in parallel: 1 = update with target +1, 2 = with target -1
         for (int idx = tid; idx < bc * nk; idx += nt) {
@@ -112,7 +137,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                                                : !(neg && !((uint64_t)r.x < cfg.q_threshold));  // kernel.cu:573
             evt[idx] = (pass && (uint64_t)r.y < th) ? (neg ? 2 : 1) : 0;      // kernel.cu:582
         }
-        __syncthreads();
+        block_sync<WPC>();
         // 1b. feedback types, class-parallel and sample-sequential (weights evolve)
         for (int kk = tid; kk < nk; kk += nt) {
             int32_t wv = wk[kk];
@@ -139,9 +164,9 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
             }
             wk[kk] = wv;
         }
-        __syncthreads();
+        block_sync<WPC>();
         // 2. compaction in (sample, class) order
-        if (tid < 32) {
+        if (tid < 32) {  // WPC: the whole warp
             int base = 0;
             for (int r0 = 0; r0 < bc; r0 += 32) {
                 const int row = r0 + tid;
@@ -171,7 +196,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
             }
             if (tid == 0) cnt[0] = base;
         }
-        __syncthreads();
+        block_sync<WPC>();
         const int nev = cnt[0];
         // 3. stream the literal words
         if (nev > 0) {
@@ -208,17 +233,13 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                 for (int i = 0; i < NB; ++i) state[((int64_t)i * C + c) * W + w] = ctr.p[i];
             }
         }
-        __syncthreads();
+        block_sync<WPC>();
     }
     for (int kk = tid; kk < nk; kk += nt) weights[(int64_t)c * K + k0 + kk] = wk[kk];
     if (count_patch) {
         for (int o = 16; o; o >>= 1) fired_count += __shfl_xor_sync(0xFFFFFFFFu, fired_count, o);
         if ((tid & 31) == 0 && fired_count) atomicAdd(&patch_w[c], fired_count);
     }
-}
-
-static size_t update_smem(int nk, int bc) {
-    return (size_t)nk * 4 + (size_t)bc * 4 + 4 + (size_t)bc * nk * 4 + (size_t)bc * nk + 16;
 }
 
 }  // namespace ytm
@@ -263,15 +284,25 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
     const RoundKeys rk = round_keys(cfg->seed, (uint32_t)(t0 >> 32));
     const int rk_ok = (t0 >> 32) == ((t0 + (uint64_t)B - 1) >> 32);
     const int W = cfg->words;
+    // small batches: one warp per clause, 8 clauses per block
+    const size_t smem_wpc = 8 * update_smem_aligned(nk, 32);
+    if (B <= 32 && smem_wpc <= 48 * 1024) {
+        YTM_DISPATCH_PLANES(cfg->planes, {
+            k_update<NB, true><<<(unsigned)cdiv(cfg->clause_count, 8), 256, smem_wpc, st>>>(
+                *cfg, state, weights, thr, drop, lits, B, t0, sel, patch_w, 32, rk, rk_ok, pair, count_patch);
+        });
+        return launch_check("feedback");
+    }
     const int tpb = W <= 32 ? 32 : (W <= 64 ? 64 : (W <= 128 ? 128 : 256));
     YTM_DISPATCH_PLANES(cfg->planes, {
         if (smem > 48 * 1024) {
-            if ((rc = cuda_check(cudaFuncSetAttribute(k_update<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                      (int)smem), "update smem")))
+            if ((rc = cuda_check(cudaFuncSetAttribute(k_update<NB, false>,
+                                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                                 "update smem")))
                 return rc;
         }
-        k_update<NB><<<cfg->clause_count, tpb, smem, st>>>(*cfg, state, weights, thr, drop, lits, B, t0, sel,
-                                                           patch_w, BC, rk, rk_ok, pair, count_patch);
+        k_update<NB, false><<<cfg->clause_count, tpb, smem, st>>>(*cfg, state, weights, thr, drop, lits, B, t0, sel,
+                                                                  patch_w, BC, rk, rk_ok, pair, count_patch);
     });
     return launch_check("feedback");
 }
