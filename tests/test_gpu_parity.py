@@ -291,3 +291,9 @@ def test_patch_match_on_random_states(case, p_inc):
     np.testing.assert_array_equal(host(cs), cs_o)
     np.testing.assert_array_equal(host(e.selection(bs)), sel_o)
     assert (sel_o >= 0).any() and (sel_o < 0).any() if p_inc > 0 else (sel_o >= 0).all()
+    # inference and transforms on the same states and samples (any-patch match)
+    ta_now = e.get_ta_state()
+    X2 = (rng.random((37, D)) < 0.5).astype(np.uint32)
+    l2 = o.encode(X2)
+    np.testing.assert_array_equal(host(e.infer(dev(l2))), o.infer(ta_now, host(e.weights), l2))
+    np.testing.assert_array_equal(host(e.transform(dev(l2))), o.transform(ta_now, l2))

@@ -51,10 +51,7 @@ TrainWs train_ws_layout(const ytm_config *cfg, int64_t B) {
     l.sel = o;   o = align_up(o + (uint64_t)B * C * 4, 256);
     l.thr = o;   o = align_up(o + (uint64_t)B * K * 8, 256);
     l.pair = o;  o = align_up(o + (uint64_t)B * 2 * 4, 256);
-    // compacted include words of every clause (sparse patch match, P > 1)
-    const uint64_t Wd = P > 1 ? (uint64_t)cfg->words : 0;
-    l.lcnt = o;  o = align_up(o + (P > 1 ? C * 4 : 0), 256);
-    l.lent = o;  o = align_up(o + C * Wd * 8, 256);
+    l.sparse = o; o += sparse_ws_bytes(cfg);  // compacted include words (sparse patch match)
     l.total = o;
     return l;
 }
@@ -177,7 +174,7 @@ uint64_t ytm_workspace_bytes(const ytm_config *cfg, int32_t op, int64_t n) {
         }
         case YTM_OP_INFER:
         case YTM_OP_TRANSFORM:
-            return infer_ws_layout(cfg, n).total + cs_planes_bytes(cfg);
+            return infer_ws_layout(cfg, n).total + cs_planes_bytes(cfg) + sparse_ws_bytes(cfg);
         case YTM_OP_TRAIN:
             return train_ws_layout(cfg, n).total + cs_planes_bytes(cfg);
         case YTM_OP_TRAIN_B1:

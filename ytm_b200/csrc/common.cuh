@@ -284,7 +284,7 @@ ytm_status check_cfg(const ytm_config *cfg);
 
 // Workspace carve-up (offsets in bytes, 256-aligned).
 struct TrainWs {
-    uint64_t ninc, mbits, sel, fired, thr, pair, lcnt, lent, total;
+    uint64_t ninc, mbits, sel, fired, thr, pair, sparse, total;
 };
 TrainWs train_ws_layout(const ytm_config *cfg, int64_t B);
 struct InferWs {
@@ -296,6 +296,7 @@ struct B1Ws {
 };
 B1Ws b1_ws_layout(const ytm_config *cfg);
 uint64_t cs_planes_bytes(const ytm_config *cfg);  // class-sum weight planes scratch (eval.cu)
+uint64_t sparse_ws_bytes(const ytm_config *cfg);  // sparse patch-match scratch (eval.cu)
 
 // Peer all-reduce (peer.cu), used by the training loop.
 extern "C" ytm_status ytm_peer_allreduce_i32(void *ctx, int32_t *data, int64_t n, int64_t limit, void *stream);

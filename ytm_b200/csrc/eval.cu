@@ -149,13 +149,16 @@ __global__ void k_compact(const uint32_t *__restrict__ inc, int C, int W, int32_
     }
 }
 
-// mbits[n][c][PW] = patches of sample n that clause c matches (an empty
-// clause matches all).  Grid: x = 128-patch tiles, y = clause blocks of cpb
-// clauses, z = samples.  Every mbits word is written once (no clear needed).
+// MODE_PBITS: out[n][c][PW] = patches of sample n that clause c matches (an
+// empty clause matches all); every word is written once (no clear needed).
+// MODE_ANY: bit c of out[n][CW] is set when clause c matches some patch
+// (out cleared beforehand).  Grid: x = 128-patch tiles, y = clause blocks of
+// cpb clauses, z = samples.
+template <int MODE>
 __global__ void __launch_bounds__(SP_WARPS * 32, 2) k_match_sparse(const uint32_t *__restrict__ lits,
                                                                 const int32_t *__restrict__ cnt,
                                                                 const uint2 *__restrict__ ent, int C, int W, int P,
-                                                                int cpb, uint32_t *__restrict__ mbits) {
+                                                                int cpb, uint32_t *__restrict__ out) {
     extern __shared__ uint32_t sl[];  // [W][SP_STRIDE]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t n = blockIdx.z;
@@ -207,37 +210,73 @@ __global__ void __launch_bounds__(SP_WARPS * 32, 2) k_match_sparse(const uint32_
         }
     done:
         const uint32_t v[4] = {v0, v1, v2, v3};
-        uint32_t *o = mbits + ((int64_t)n * C + c) * PW + (p0 >> 5);
+        if (MODE == MODE_PBITS) {
+            uint32_t *o = out + ((int64_t)n * C + c) * PW + (p0 >> 5);
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-            if (g < ng) {
-                const uint32_t b = __ballot_sync(0xFFFFFFFFu, v[g] == 0u && g * 32 + lane < np);
-                if (lane == 0) o[g] = b;
+            for (int g = 0; g < 4; ++g) {
+                if (g < ng) {
+                    const uint32_t b = __ballot_sync(0xFFFFFFFFu, v[g] == 0u && g * 32 + lane < np);
+                    if (lane == 0) o[g] = b;
+                }
             }
+        } else {
+            bool any = false;
+#pragma unroll
+            for (int g = 0; g < 4; ++g) any |= v[g] == 0u && g * 32 + lane < np;
+            if (__any_sync(0xFFFFFFFFu, any) && lane == 0)
+                atomicOr(&out[(int64_t)n * ((C + 31) / 32) + (c >> 5)], 1u << (c & 31));
         }
     }
 }
 
-static ytm_status launch_match_sparse(const uint32_t *inc, const uint32_t *lits, int64_t B, int C, int W, int P,
-                                      int32_t *cnt, uint2 *ent, uint32_t *mbits, cudaStream_t st) {
+// Scratch of the sparse match: include-word counts [C] and lists [C][W].
+uint64_t sparse_ws_bytes(const ytm_config *cfg) {
+    if (cfg->patches <= 1) return 0;
+    const uint64_t C = cfg->clause_count;
+    return align_up(C * 4, 256) + align_up(C * (uint64_t)cfg->words * 8, 256);
+}
+
+inline bool use_sparse_match(const ytm_config *cfg) { return cfg->patches > 1 && sparse_match_fits(cfg->words); }
+
+// Samples [0, N) of lits; out as k_match_sparse<MODE> describes.
+template <int MODE>
+static ytm_status launch_match_sparse(const uint32_t *inc, const uint32_t *lits, int64_t N, int C, int W, int P,
+                                      void *scratch, uint32_t *out, cudaStream_t st) {
+    int32_t *cnt = (int32_t *)scratch;
+    uint2 *ent = (uint2 *)((char *)scratch + align_up((uint64_t)C * 4, 256));
     k_compact<<<grid1((int64_t)C * 32), 256, 0, st>>>(inc, C, W, cnt, ent);
     ytm_status rc = launch_check("include compaction");
     if (rc) return rc;
     const size_t smem = sparse_smem_bytes(W);
     if (smem > 48 * 1024 &&
-        (rc = cuda_check(cudaFuncSetAttribute(k_match_sparse, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+        (rc = cuda_check(cudaFuncSetAttribute(k_match_sparse<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)smem),
                          "sparse match smem")))
         return rc;
-    if (B > 65535) return fail(YTM_ERR_UNSUPPORTED, "batch above 65535 samples");
     const int tiles = (int)cdiv(P, SP_PT);
-    // about two CTAs per SM over the whole grid; at least 32 clauses a block
-    int64_t cb = std::max<int64_t>(1, (int64_t)sm_count() * 2 / ((int64_t)tiles * B));
-    cb = std::min<int64_t>(cb, std::max<int64_t>(1, C / 32));
-    const int cpb = (int)cdiv(C, cb);
-    cb = cdiv(C, cpb);
-    k_match_sparse<<<dim3((unsigned)tiles, (unsigned)cb, (unsigned)B), SP_WARPS * 32, smem, st>>>(lits, cnt, ent, C, W,
-                                                                                               P, cpb, mbits);
-    return launch_check("sparse match");
+    const int64_t PW = (int64_t)cdiv(P, 32), CW = (int64_t)cdiv(C, 32);
+    for (int64_t n0 = 0; n0 < N; n0 += 65535) {
+        const int64_t nb = std::min<int64_t>(65535, N - n0);
+        // about two CTAs per SM over the whole grid; at least 32 clauses a block
+        int64_t cb = std::max<int64_t>(1, (int64_t)sm_count() * 2 / ((int64_t)tiles * nb));
+        cb = std::min<int64_t>(cb, std::max<int64_t>(1, C / 32));
+        const int cpb = (int)cdiv(C, cb);
+        cb = cdiv(C, cpb);
+        uint32_t *o = out + n0 * (MODE == MODE_PBITS ? (int64_t)C * PW : CW);
+        k_match_sparse<MODE><<<dim3((unsigned)tiles, (unsigned)cb, (unsigned)nb), SP_WARPS * 32, smem, st>>>(
+            lits + n0 * P * W, cnt, ent, C, W, P, cpb, o);
+        if ((rc = launch_check("sparse match"))) return rc;
+    }
+    return YTM_OK;
+}
+
+// The fired bitmap of inference and transforms (out cleared beforehand).
+static ytm_status launch_match_any(const ytm_config *cfg, const uint32_t *inc, const uint32_t *lits, int64_t N,
+                                   void *sparse_scratch, uint32_t *fired, cudaStream_t st) {
+    const int C = cfg->clause_count, W = cfg->words, P = cfg->patches;
+    if (sparse_scratch && use_sparse_match(cfg))
+        return launch_match_sparse<MODE_ANY>(inc, lits, N, C, W, P, sparse_scratch, fired, st);
+    return launch_match<MODE_ANY>(inc, lits, N * P, C, W, P, fired, st);
 }
 
 // Training evaluation of single-patch models in one kernel: the tile's
@@ -617,7 +656,7 @@ ytm_status ytm_infer(const ytm_config *cfg, const uint32_t *state, const int32_t
     if (N == 0) return YTM_OK;
     if (!state || !weights || !lits || !cs || !workspace) return fail(YTM_ERR_ARG, "null pointer");
     cudaStream_t st = as_stream(stream);
-    const int C = cfg->clause_count, W = cfg->words, P = cfg->patches;
+    const int C = cfg->clause_count, W = cfg->words;
     InferWs l = infer_ws_layout(cfg, N);
     char *ws = (char *)workspace;
     int32_t *ninc = (int32_t *)(ws + l.ninc);
@@ -625,7 +664,7 @@ ytm_status ytm_infer(const ytm_config *cfg, const uint32_t *state, const int32_t
     const uint32_t *inc = state + (int64_t)(cfg->planes - 1) * C * W;
     if ((rc = launch_ninc(cfg, state, ninc, st))) return rc;
     if ((rc = cuda_check(cudaMemsetAsync(fired, 0, (size_t)N * cdiv(C, 32) * 4, st), "memset"))) return rc;
-    if ((rc = launch_match<MODE_ANY>(inc, lits, N * P, C, W, P, fired, st))) return rc;
+    if ((rc = launch_match_any(cfg, inc, lits, N, ws + l.total + cs_planes_bytes(cfg), fired, st))) return rc;
     return launch_cs_planes(fired, cfg->count_empty ? nullptr : ninc, weights, bias, cfg, N, 0, cs, ws + l.total,
                             st);
 }
@@ -639,7 +678,7 @@ ytm_status ytm_infer_include(const ytm_config *cfg, const uint32_t *inc, const i
     if (N == 0) return YTM_OK;
     if (!inc || !weights || !lits || !cs || !workspace) return fail(YTM_ERR_ARG, "null pointer");
     cudaStream_t st = as_stream(stream);
-    const int C = cfg->clause_count, W = cfg->words, P = cfg->patches;
+    const int C = cfg->clause_count, W = cfg->words;
     InferWs l = infer_ws_layout(cfg, N);
     char *ws = (char *)workspace;
     int32_t *ninc = (int32_t *)(ws + l.ninc);
@@ -647,7 +686,7 @@ ytm_status ytm_infer_include(const ytm_config *cfg, const uint32_t *inc, const i
     k_ninc<<<grid1((int64_t)C * 32), 256, 0, st>>>(C, W, inc, ninc, nullptr);
     if ((rc = launch_check("include counts"))) return rc;
     if ((rc = cuda_check(cudaMemsetAsync(fired, 0, (size_t)N * cdiv(C, 32) * 4, st), "memset"))) return rc;
-    if ((rc = launch_match<MODE_ANY>(inc, lits, N * P, C, W, P, fired, st))) return rc;
+    if ((rc = launch_match_any(cfg, inc, lits, N, ws + l.total + cs_planes_bytes(cfg), fired, st))) return rc;
     return launch_cs_planes(fired, cfg->count_empty ? nullptr : ninc, weights, bias, cfg, N, 0, cs, ws + l.total,
                             st);
 }
@@ -660,13 +699,14 @@ ytm_status ytm_transform(const ytm_config *cfg, const uint32_t *state, const uin
     if (N == 0) return YTM_OK;
     if (!state || !lits || !out || !workspace) return fail(YTM_ERR_ARG, "null pointer");
     cudaStream_t st = as_stream(stream);
-    const int C = cfg->clause_count, W = cfg->words, P = cfg->patches;
+    const int C = cfg->clause_count, W = cfg->words;
     InferWs l = infer_ws_layout(cfg, N);
     uint32_t *fired = (uint32_t *)((char *)workspace + l.fired);
     const uint32_t *inc = state + (int64_t)(cfg->planes - 1) * C * W;
     if ((rc = cuda_check(cudaMemsetAsync(fired, 0, (size_t)N * cdiv(C, 32) * 4, st), "memset"))) return rc;
     // empty clauses match every patch, so they come out as 1 (kernel.cu:354-357)
-    if ((rc = launch_match<MODE_ANY>(inc, lits, N * P, C, W, P, fired, st))) return rc;
+    if ((rc = launch_match_any(cfg, inc, lits, N, (char *)workspace + l.total + cs_planes_bytes(cfg), fired, st)))
+        return rc;
     k_expand<<<grid1(N * C), 256, 0, st>>>(fired, N, C, out);
     return launch_check("transform expand");
 }
@@ -716,11 +756,9 @@ ytm_status ytm_train_eval(const ytm_config *cfg, const uint32_t *state, const in
         return launch_check("train eval");
     }
     // training semantics: an empty clause matches every patch (kernel.cu:273-276)
-    if (P > 1 && sparse_match_fits(W)) {
+    if (use_sparse_match(cfg)) {
         if ((rc = cuda_check(cudaMemsetAsync(fired, 0, l.sel - l.fired, st), "memset"))) return rc;
-        if ((rc = launch_match_sparse(inc, lits, B, C, W, P, (int32_t *)(ws + l.lcnt), (uint2 *)(ws + l.lent),
-                                      mbits, st)))
-            return rc;
+        if ((rc = launch_match_sparse<MODE_PBITS>(inc, lits, B, C, W, P, ws + l.sparse, mbits, st))) return rc;
     } else {
         // match bits and fired bits are adjacent in the workspace: one clear
         if ((rc = cuda_check(cudaMemsetAsync(mbits, 0, l.sel - l.mbits, st), "memset"))) return rc;
