@@ -117,19 +117,23 @@ __device__ __forceinline__ u32x4 draw_rk(const RoundKeys &rk, uint32_t clause, u
 // feedback for class k of sample t: literal j is set iff the 12-bit number
 // whose bit 11-i is bit j of random word i is below thr; three Philox4x32-7
 // draws give the 12 words.  (Stands in for the reference's per-literal
-// `curand_uniform(rng) <= S_INV`.)
-__device__ __forceinline__ uint32_t smask_word(uint64_t seed, uint32_t thr, uint32_t g, uint64_t t, uint32_t k,
-                                               uint32_t w) {
-    if (thr >= 4096u) return 0xFFFFFFFFu;
+// `curand_uniform(rng) <= S_INV`.)  Only the literals in `cand` are wanted:
+// the comparison runs most significant bit first, so once every candidate
+// literal is decided the remaining draws cannot change the result and are
+// skipped.  Returns the bits within cand.
+template <typename DrawFn>
+__device__ __forceinline__ uint32_t smask_compare(uint32_t thr, uint32_t cand, DrawFn drawj) {
+    if (thr >= 4096u) return cand;
     if (thr == 0u) return 0u;
-    uint32_t lt = 0u, eq = 0xFFFFFFFFu;
+    uint32_t lt = 0u, eq = cand;
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
-        u32x4 r = draw<7>(seed, g, t, w * 4u + (uint32_t)j, TAG_SMASK, k);
-        uint32_t R[4] = {r.x, r.y, r.z, r.w};
+        if (eq == 0u) break;
+        const u32x4 r = drawj((uint32_t)j);
+        const uint32_t R[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            int bit = 11 - (4 * j + i);
+            const int bit = 11 - (4 * j + i);
             if ((thr >> bit) & 1u) {
                 lt |= eq & ~R[i];
                 eq &= R[i];
@@ -141,28 +145,15 @@ __device__ __forceinline__ uint32_t smask_word(uint64_t seed, uint32_t thr, uint
     return lt;
 }
 
+__device__ __forceinline__ uint32_t smask_word(uint64_t seed, uint32_t thr, uint32_t cand, uint32_t g, uint64_t t,
+                                               uint32_t k, uint32_t w) {
+    return smask_compare(thr, cand, [&](uint32_t j) { return draw<7>(seed, g, t, w * 4u + j, TAG_SMASK, k); });
+}
+
 // smask_word with precomputed round keys.
-__device__ __forceinline__ uint32_t smask_word_rk(const RoundKeys &rk, uint32_t thr, uint32_t g, uint64_t t,
-                                                  uint32_t k, uint32_t w) {
-    if (thr >= 4096u) return 0xFFFFFFFFu;
-    if (thr == 0u) return 0u;
-    uint32_t lt = 0u, eq = 0xFFFFFFFFu;
-#pragma unroll
-    for (int j = 0; j < 3; ++j) {
-        u32x4 r = draw_rk<7>(rk, g, t, w * 4u + (uint32_t)j, TAG_SMASK, k);
-        uint32_t R[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            int bit = 11 - (4 * j + i);
-            if ((thr >> bit) & 1u) {
-                lt |= eq & ~R[i];
-                eq &= R[i];
-            } else {
-                eq &= ~R[i];
-            }
-        }
-    }
-    return lt;
+__device__ __forceinline__ uint32_t smask_word_rk(const RoundKeys &rk, uint32_t thr, uint32_t cand, uint32_t g,
+                                                  uint64_t t, uint32_t k, uint32_t w) {
+    return smask_compare(thr, cand, [&](uint32_t j) { return draw_rk<7>(rk, g, t, w * 4u + j, TAG_SMASK, k); });
 }
 
 // pytm's per-sample pick (pytm/base.py:139-141): the true class (the first

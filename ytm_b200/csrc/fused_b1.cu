@@ -213,8 +213,8 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
                             cand = vm & ctr.ne(zero_s);
                         }
                         if (cand)
-                            ctr.dec(cand & smask_word_rk(rk, cfg.s_threshold12, g, t,
-                                                      (uint32_t)(k0 + kb * 32 + b), (uint32_t)w));
+                            ctr.dec(smask_word_rk(rk, cfg.s_threshold12, cand, g, t,
+                                                  (uint32_t)(k0 + kb * 32 + b), (uint32_t)w));
                     }
                 }
             }

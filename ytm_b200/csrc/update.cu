@@ -225,8 +225,9 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                             cand = vm & ctr.ne(zero_s);
                         }
                         if (cand)
-                            ctr.dec(cand & (rk_ok ? smask_word_rk(rk, cfg.s_threshold12, g, t, (uint32_t)k, (uint32_t)w)
-                                                  : smask_word(cfg.seed, cfg.s_threshold12, g, t, (uint32_t)k, (uint32_t)w)));
+                            ctr.dec(rk_ok ? smask_word_rk(rk, cfg.s_threshold12, cand, g, t, (uint32_t)k, (uint32_t)w)
+                                          : smask_word(cfg.seed, cfg.s_threshold12, cand, g, t, (uint32_t)k,
+                                                       (uint32_t)w));
                     }
                 }
 #pragma unroll
