@@ -50,6 +50,12 @@ TrainWs train_ws_layout(const ytm_config *cfg, int64_t B) {
     l.fired = o; o = align_up(o + (uint64_t)B * CW * 4, 256);  // right after mbits: one memset clears both
     l.sel = o;   o = align_up(o + (uint64_t)B * C * 4, 256);
     l.thr = o;   o = align_up(o + (uint64_t)B * K * 8, 256);
+    // (sample, class) pairs that can update: bits per sample, bits per class,
+    // and the list in feedback order with each sample's offset into it
+    l.amask = o; o = align_up(o + (uint64_t)B * cdiv(K, 32) * 4, 256);
+    l.colm = o;  o = align_up(o + K * cdiv(B, 32) * 4, 256);
+    l.row_off = o; o = align_up(o + ((uint64_t)B + 1) * 4, 256);
+    l.alist = o; o = align_up(o + (uint64_t)B * K * 4, 256);
     l.pair = o;  o = align_up(o + (uint64_t)B * 2 * 4, 256);
     l.sparse = o; o += sparse_ws_bytes(cfg);  // compacted include words (sparse patch match)
     l.total = o;

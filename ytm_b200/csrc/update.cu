@@ -24,20 +24,91 @@ namespace ytm {
 
 constexpr int UPD_BC_MAX = 256;  // samples per chunk at most (list entries hold 8-bit rows)
 
-// thr[b][k] = floor(p * 2^32) of the update probability, bit 63 set when the
-// target is -1 (kernel.cu:544-551, 569-571).
-__global__ void k_thresholds(const int32_t *__restrict__ cs, const int32_t *__restrict__ Y, int B, int K, int T,
-                             uint64_t *__restrict__ thr) {
-    int64_t total = (int64_t)B * K;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        int32_t v = cs[i];
-        v = v > T ? T : (v < -T ? -T : v);  // clip_cs, kernel.cu:397
-        int32_t y = Y[i];
-        uint64_t t = update_threshold(y, v);
-        if (v > y) t |= 1ull << 63;
-        thr[i] = t;
+// One block prepares the batch's decisions, which every clause shares.
+//  * thr[b][k] = floor(p * 2^32) of the update probability, bit 63 set when
+//    the target is -1 (kernel.cu:544-551, 569-571).
+//  * The pair (b, k) is active when thr is non-zero (the update draw is
+//    r < thr, so an inactive pair never updates a clause) and, under pytm's
+//    rules, k is one of the sample's two classes.  Once a model has converged
+//    most class sums sit at +-T and few pairs stay active.
+//  * amask[b][k / 32] and colm[k][b / 32] hold the active pairs as bits per
+//    sample and per class; alist lists them in feedback order (sample by
+//    sample; classes in order, or pytm's true class first) and row_off[b] is
+//    the position of sample b's first pair in it (row_off[B] = the count).
+__global__ void __launch_bounds__(1024) k_thresholds(const int32_t *__restrict__ cs, const int32_t *__restrict__ Y,
+                                                     int B, int K, int T, int one_neg,
+                                                     const int32_t *__restrict__ pair, uint64_t *__restrict__ thr,
+                                                     uint32_t *__restrict__ amask, uint32_t *__restrict__ colm,
+                                                     int32_t *__restrict__ row_off, uint32_t *__restrict__ alist) {
+    __shared__ int wsum[32];
+    __shared__ int base_s;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int KWm = (K + 31) >> 5, BW = (B + 31) >> 5;
+    for (int64_t u = wid; u < (int64_t)B * KWm; u += nw) {
+        const int64_t b = u / KWm;
+        const int k = (int)(u - b * KWm) * 32 + lane;
+        bool act = false;
+        if (k < K) {
+            int32_t v = cs[b * K + k];
+            v = v > T ? T : (v < -T ? -T : v);  // clip_cs, kernel.cu:397
+            const int32_t y = Y[b * K + k];
+            uint64_t t = update_threshold(y, v);
+            act = t != 0ull && (!one_neg || k == pair[2 * b] || k == pair[2 * b + 1]);
+            if (v > y) t |= 1ull << 63;
+            thr[b * K + k] = t;
+        }
+        const uint32_t m = __ballot_sync(0xFFFFFFFFu, act);
+        if (lane == 0) amask[u] = m;
     }
+    if (threadIdx.x == 0) base_s = 0;
+    __syncthreads();
+    for (int64_t u = wid; u < (int64_t)K * BW; u += nw) {
+        const int k = (int)(u / BW), row = (int)(u - (int64_t)k * BW) * 32 + lane;
+        const bool a = row < B && ((amask[(int64_t)row * KWm + (k >> 5)] >> (k & 31)) & 1u);
+        const uint32_t m = __ballot_sync(0xFFFFFFFFu, a);
+        if (lane == 0) colm[u] = m;
+    }
+    for (int r0 = 0; r0 < B; r0 += blockDim.x) {
+        const int row = r0 + threadIdx.x;
+        int n = 0;
+        if (row < B)
+            for (int m = 0; m < KWm; ++m) n += __popc(amask[(int64_t)row * KWm + m]);
+        int incl = n;
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        if (lane == 31) wsum[wid] = incl;
+        __syncthreads();
+        if (wid == 0) {
+            int v = lane < nw ? wsum[lane] : 0;
+            for (int o = 1; o < 32; o <<= 1) {
+                const int x = __shfl_up_sync(0xFFFFFFFFu, v, o);
+                if (lane >= o) v += x;
+            }
+            wsum[lane] = v;
+        }
+        __syncthreads();
+        int pos = base_s + (wid ? wsum[wid - 1] : 0) + incl - n;
+        if (row < B) {
+            row_off[row] = pos;
+            const uint32_t *am = amask + (int64_t)row * KWm;
+            if (one_neg) {
+                for (int q = 0; q < 2; ++q) {
+                    const int k = pair[2 * row + q];
+                    if (k >= 0 && ((am[k >> 5] >> (k & 31)) & 1u)) alist[pos++] = (uint32_t)row * (uint32_t)K + k;
+                }
+            } else {
+                for (int m = 0; m < KWm; ++m)
+                    for (uint32_t v = am[m]; v; v &= v - 1u)
+                        alist[pos++] = (uint32_t)row * (uint32_t)K + (uint32_t)(m * 32 + __ffs(v) - 1);
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) base_s += wsum[nw - 1];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) row_off[B] = base_s;
 }
 
 template <bool WPC>
@@ -48,6 +119,8 @@ __device__ __forceinline__ void block_sync() {
         __syncthreads();
 }
 
+// Shared memory of one clause: weights [nk], picks [bc], count, event list
+// [bc*nk], event types [bc*nk].
 static __host__ __device__ inline size_t update_smem(int nk, int bc) {
     return (size_t)nk * 4 + (size_t)bc * 4 + 4 + (size_t)bc * nk * 4 + (size_t)bc * nk + 16;
 }
@@ -65,6 +138,21 @@ __global__ void k_pairs(uint64_t seed, const int32_t *__restrict__ Y, int B, int
     }
 }
 
+// The Q-selection and update draws of clause g for the active pair (b, k):
+// 1 = update with target +1, 2 = with target -1, 0 = none.  Pairs reach here
+// only when active (under pytm's rules: one of the sample's two classes).
+__device__ __forceinline__ uint8_t decide(const ytm_config &cfg, const RoundKeys &rk, int rk_ok,
+                                          const uint64_t *__restrict__ thr, uint32_t g, uint64_t t0, int b, int k,
+                                          int K) {
+    uint64_t th = thr[(int64_t)b * K + k];
+    const bool neg = (th >> 63) != 0;
+    th &= ~(1ull << 63);
+    const uint64_t tb = t0 + (uint64_t)b;
+    const u32x4 r = rk_ok ? draw_rk(rk, g, tb, 0, TAG_CLASS, (uint32_t)k) : draw(cfg.seed, g, tb, 0, TAG_CLASS, (uint32_t)k);
+    const bool pass = cfg.one_negative || !(neg && !((uint64_t)r.x < cfg.q_threshold));  // kernel.cu:573
+    return (pass && (uint64_t)r.y < th) ? (neg ? 2 : 1) : 0;                             // kernel.cu:582
+}
+
 template <int NB, bool WPC>
 #ifndef YTM_UPD_MINB
 #define YTM_UPD_MINB 4  // 64 registers: measured fastest (no spills)
@@ -75,7 +163,9 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                                                 const uint32_t *__restrict__ lits, int B, uint64_t t0,
                                                 const int32_t *__restrict__ sel, int32_t *__restrict__ patch_w,
                                                 int BC, const RoundKeys rk, int rk_ok,
-                                                const int32_t *__restrict__ pair, int count_patch) {
+                                                int count_patch, const uint32_t *__restrict__ colm,
+                                                const int32_t *__restrict__ row_off,
+                                                const uint32_t *__restrict__ alist) {
     extern __shared__ __align__(16) unsigned char small[];
     const int C = cfg.clause_count, W = cfg.words, K = cfg.n_classes, P = cfg.patches;
     const int c = WPC ? (int)(blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) : (int)blockIdx.x;
@@ -84,13 +174,15 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
     if (drop && drop[c] == 1u) return;  // kernel.cu:555
     const int k0 = cfg.coalesced ? 0 : (int)(g / (uint32_t)cfg.clauses_per_class);
     const int nk = cfg.coalesced ? K : 1;
+    const int BW = (B + 31) >> 5;
     unsigned char *smraw = WPC ? small + (threadIdx.x >> 5) * update_smem_aligned(nk, BC) : small;
     int32_t *wk = (int32_t *)smraw;                       // [nk]
     int32_t *sel_s = wk + nk;                             // [BC]
     int32_t *cnt = sel_s + BC;                            // [1]
     uint32_t *list = (uint32_t *)(cnt + 1);               // [BC * nk]
-    uint8_t *evt = (uint8_t *)(list + BC * nk);           // [BC * nk]
+    uint8_t *evt = (uint8_t *)(list + BC * nk);           // [BC * nk], valid at active pairs only
     const int tid = WPC ? (int)(threadIdx.x & 31) : (int)threadIdx.x, nt = WPC ? 32 : (int)blockDim.x;
+    const int lane = tid & 31;
     // include count of the batch-start state (pack_clauses, kernel.cu:155-204):
     // this CTA alone writes the clause, so its top plane is still unchanged.
     // Not needed when the cap cannot bind.
@@ -113,88 +205,89 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
     int fired_count = 0;  // single-patch models: patch 0 picks of this clause (select_active, kernel.cu:305)
     const uint32_t max_s = (uint32_t)(cfg.max_state + cfg.state_offset);
     const uint32_t zero_s = (uint32_t)cfg.state_offset;
+    const uint32_t *mycol = colm + (int64_t)k0 * BW;  // non-coalesced: the active samples of the bank's class
 
     for (int kk = tid; kk < nk; kk += nt) wk[kk] = weights[(int64_t)c * K + k0 + kk];
 
-    for (int b0 = 0; b0 < B; b0 += BC) {
+    for (int b0 = 0; b0 < B; b0 += BC) {  // BC is a multiple of 32
         const int bc = min(BC, B - b0);
         for (int q = tid; q < bc; q += nt) {
             sel_s[q] = sel[(int64_t)(b0 + q) * C + c];
             fired_count += sel_s[q] >= 0;
         }
-        block_sync<WPC>();
-        // 1a. the chunk's Q-selection and update draws, all (sample, class)
-        //     pairs in parallel: 1 = update with target +1, 2 = with target -1
-        for (int idx = tid; idx < bc * nk; idx += nt) {
-            const int bl = idx / nk, kk = idx - bl * nk;
-            const int b = b0 + bl, k = k0 + kk;
-            uint64_t th = thr[(int64_t)b * K + k];
-            const bool neg = (th >> 63) != 0;
-            th &= ~(1ull << 63);
-            const uint64_t tb = t0 + (uint64_t)b;
-            u32x4 r = rk_ok ? draw_rk(rk, g, tb, 0, TAG_CLASS, (uint32_t)k) : draw(cfg.seed, g, tb, 0, TAG_CLASS, (uint32_t)k);
-            const bool pass = cfg.one_negative ? (k == pair[2 * b] || k == pair[2 * b + 1])
-                                               : !(neg && !((uint64_t)r.x < cfg.q_threshold));  // kernel.cu:573
-            evt[idx] = (pass && (uint64_t)r.y < th) ? (neg ? 2 : 1) : 0;      // kernel.cu:582
+        const int lo = cfg.coalesced ? row_off[b0] : 0, hi = cfg.coalesced ? row_off[b0 + bc] : 0;
+        // 1a. the Q-selection and update draws of the active pairs, in
+        //     parallel: 1 = update with target +1, 2 = with target -1
+        for (int idx = lo + tid; idx < hi; idx += nt) {  // coalesced: the chunk's pairs
+            const uint32_t e = alist[idx];
+            const int b = (int)(e / (uint32_t)K), k = (int)(e - (uint32_t)b * (uint32_t)K);
+            evt[(b - b0) * nk + k] = decide(cfg, rk, rk_ok, thr, g, t0, b, k, K);
         }
+        if (!cfg.coalesced)
+            for (int bl = tid; bl < bc; bl += nt)
+                if ((mycol[(b0 + bl) >> 5] >> ((b0 + bl) & 31)) & 1u)
+                    evt[bl] = decide(cfg, rk, rk_ok, thr, g, t0, b0 + bl, k0, K);
         block_sync<WPC>();
-        // 1b. feedback types, class-parallel and sample-sequential (weights evolve)
+        // 1b. feedback types, class-parallel and sample-sequential over the
+        //     class's active samples (weights evolve)
         for (int kk = tid; kk < nk; kk += nt) {
             int32_t wv = wk[kk];
-            for (int bl = 0; bl < bc; ++bl) {
-                const uint8_t a = evt[bl * nk + kk];
-                uint8_t ev = EV_NONE;
-                if (a) {
-                    const int target = a == 1 ? 1 : -1;
-                    const int sign = (wv >= 0) - (wv < 0);
-                    const bool fired = sel_s[bl] > -1;
-                    const int ts = target * sign;
-                    if (ts > 0 && fired && ok_inc) {
-                        ev = EV_T1A;
-                        wv += sign;
-                    } else if (ts > 0) {
-                        ev = EV_T1B;
-                    } else if (ts < 0 && fired) {
-                        ev = EV_T2;
-                        wv -= sign;
-                        if (!cfg.negative_polarity && wv < 1) wv = 1;  // kernel.cu:603-606
+            const uint32_t *cm = colm + (int64_t)(k0 + kk) * BW + (b0 >> 5);
+            for (int gi = 0; gi < (bc + 31) >> 5; ++gi) {
+                for (uint32_t mm = cm[gi]; mm; mm &= mm - 1u) {
+                    const int bl = gi * 32 + __ffs(mm) - 1;
+                    const uint8_t a = evt[bl * nk + kk];
+                    uint8_t ev = EV_NONE;
+                    if (a) {
+                        const int target = a == 1 ? 1 : -1;
+                        const int sign = (wv >= 0) - (wv < 0);
+                        const bool fired = sel_s[bl] > -1;
+                        const int ts = target * sign;
+                        if (ts > 0 && fired && ok_inc) {
+                            ev = EV_T1A;
+                            wv += sign;
+                        } else if (ts > 0) {
+                            ev = EV_T1B;
+                        } else if (ts < 0 && fired) {
+                            ev = EV_T2;
+                            wv -= sign;
+                            if (!cfg.negative_polarity && wv < 1) wv = 1;  // kernel.cu:603-606
+                        }
                     }
+                    evt[bl * nk + kk] = ev;
                 }
-                evt[bl * nk + kk] = ev;
             }
             wk[kk] = wv;
         }
         block_sync<WPC>();
-        // 2. compaction in (sample, class) order
+        // 2. the events in the active pairs' order
         if (tid < 32) {  // WPC: the whole warp
             int base = 0;
-            for (int r0 = 0; r0 < bc; r0 += 32) {
-                const int row = r0 + tid;
-                int n = 0;
-                if (row < bc)
-                    for (int kk = 0; kk < nk; ++kk) n += evt[row * nk + kk] != EV_NONE;
-                int incl = n;
-                for (int o = 1; o < 32; o <<= 1) {
-                    int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-                    if (tid >= o) incl += v;
-                }
-                int pos = base + incl - n;
-                if (row < bc && cfg.one_negative) {  // the true class first, then the other
-                    for (int q = 0; q < 2; ++q) {
-                        const int kk = pair[2 * (b0 + row) + q] - k0;
-                        if (kk < 0 || kk >= nk) continue;
-                        uint32_t ev = evt[row * nk + kk];
-                        if (ev != EV_NONE) list[pos++] = ((uint32_t)row << 24) | (ev << 22) | (uint32_t)kk;
+            const int n = cfg.coalesced ? hi - lo : bc;
+            for (int r0 = 0; r0 < n; r0 += 32) {
+                const int i = r0 + lane;
+                uint32_t ent = 0u;
+                if (i < n) {
+                    int bl, kk;
+                    bool act = true;
+                    if (cfg.coalesced) {
+                        const uint32_t e = alist[lo + i];
+                        const int b = (int)(e / (uint32_t)K);
+                        bl = b - b0;
+                        kk = (int)(e - (uint32_t)b * (uint32_t)K);
+                    } else {
+                        bl = i;
+                        kk = 0;
+                        act = (mycol[(b0 + bl) >> 5] >> ((b0 + bl) & 31)) & 1u;
                     }
-                } else if (row < bc) {
-                    for (int kk = 0; kk < nk; ++kk) {
-                        uint32_t ev = evt[row * nk + kk];
-                        if (ev != EV_NONE) list[pos++] = ((uint32_t)row << 24) | (ev << 22) | (uint32_t)kk;
-                    }
+                    const uint32_t ev = act ? evt[bl * nk + kk] : EV_NONE;
+                    if (ev != EV_NONE) ent = ((uint32_t)bl << 24) | (ev << 22) | (uint32_t)kk;
                 }
-                base += __shfl_sync(0xFFFFFFFFu, incl, 31);
+                const uint32_t bal = __ballot_sync(0xFFFFFFFFu, ent != 0u);
+                if (ent) list[base + __popc(bal & ((1u << lane) - 1u))] = ent;
+                base += __popc(bal);
             }
-            if (tid == 0) cnt[0] = base;
+            if (lane == 0) cnt[0] = base;
         }
         block_sync<WPC>();
         const int nev = cnt[0];
@@ -258,22 +351,24 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
     const int count_patch = single_patch_eval(cfg) ? 1 : 0;
     if (count_patch && !patch_w) return fail(YTM_ERR_ARG, "patch_w is NULL");
     if (cfg->n_classes >= (1 << 22)) return fail(YTM_ERR_UNSUPPORTED, "too many classes");
+    if ((int64_t)B * cfg->n_classes >= (1ll << 32)) return fail(YTM_ERR_UNSUPPORTED, "batch x classes above 2^32");
     cudaStream_t st = as_stream(stream);
     TrainWs l = train_ws_layout(cfg, B);
     char *ws = (char *)workspace;
     const int32_t *sel = sel_override ? sel_override : (const int32_t *)(ws + l.sel);
     uint64_t *thr = (uint64_t *)(ws + l.thr);
     int32_t *pair = (int32_t *)(ws + l.pair);
+    uint32_t *amask = (uint32_t *)(ws + l.amask);
+    uint32_t *colm = (uint32_t *)(ws + l.colm);
+    int32_t *row_off = (int32_t *)(ws + l.row_off);
+    uint32_t *alist = (uint32_t *)(ws + l.alist);
     if (cfg->one_negative) {
         k_pairs<<<(unsigned)cdiv(B, 256), 256, 0, st>>>(cfg->seed, Y, B, cfg->n_classes, t0, pair);
         if ((rc = launch_check("class pairs"))) return rc;
     }
-    {
-        int64_t total = (int64_t)B * cfg->n_classes;
-        unsigned blocks = (unsigned)std::min<int64_t>((int64_t)cdiv(total, 256), (int64_t)sm_count() * 8);
-        k_thresholds<<<blocks, 256, 0, st>>>(cs, Y, B, cfg->n_classes, cfg->T, thr);
-        if ((rc = launch_check("update thresholds"))) return rc;
-    }
+    k_thresholds<<<1, 1024, 0, st>>>(cs, Y, B, cfg->n_classes, cfg->T, cfg->one_negative, pair, thr, amask, colm,
+                                     row_off, alist);
+    if ((rc = launch_check("update thresholds"))) return rc;
     const int nk = cfg->coalesced ? cfg->n_classes : 1;
     // the largest chunk (multiple of 32, at most 256 and the batch) whose
     // event list fits 32 KB of shared memory (keeps several CTAs per SM)
@@ -290,7 +385,7 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
     if (B <= 32 && smem_wpc <= 48 * 1024) {
         YTM_DISPATCH_PLANES(cfg->planes, {
             k_update<NB, true><<<(unsigned)cdiv(cfg->clause_count, 8), 256, smem_wpc, st>>>(
-                *cfg, state, weights, thr, drop, lits, B, t0, sel, patch_w, 32, rk, rk_ok, pair, count_patch);
+                *cfg, state, weights, thr, drop, lits, B, t0, sel, patch_w, 32, rk, rk_ok, count_patch, colm, row_off, alist);
         });
         return launch_check("feedback");
     }
@@ -303,7 +398,8 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
                 return rc;
         }
         k_update<NB, false><<<cfg->clause_count, tpb, smem, st>>>(*cfg, state, weights, thr, drop, lits, B, t0, sel,
-                                                                  patch_w, BC, rk, rk_ok, pair, count_patch);
+                                                                  patch_w, BC, rk, rk_ok, count_patch, colm,
+                                                                  row_off, alist);
     });
     return launch_check("feedback");
 }
