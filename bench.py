@@ -376,7 +376,7 @@ def main():
         kernel = "k_fused_b1 (feedback of sample i + evaluation of sample i+1), per 256 launches"
     else:
         nk = cfg.n_classes if cfg.coalesced else 1
-        bc = min(256, (B + 31) // 32 * 32)  # k_update's chunk: event list within 32 KB of shared memory
+        bc = min(128, (B + 31) // 32 * 32)  # k_update's chunk: event list within 32 KB of shared memory
         while bc > 32 and nk * 4 + bc * 4 + 4 + bc * nk * 5 + 16 > 32 * 1024:
             bc -= 32
         chunks = (B + bc - 1) // bc

@@ -121,6 +121,18 @@ __device__ __forceinline__ u32x4 draw_rk(const RoundKeys &rk, uint32_t clause, u
 // the comparison runs most significant bit first, so once every candidate
 // literal is decided the remaining draws cannot change the result and are
 // skipped.  Returns the bits within cand.
+// One Philox draw j of the comparison: planes 11-4j .. 8-4j of the 12-bit
+// values against the same bits of thr (branch-free: thr is uniform).
+__device__ __forceinline__ void smask_planes(uint32_t thr, int j, const u32x4 &r, uint32_t &lt, uint32_t &eq) {
+    const uint32_t R[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t tb = 0u - ((thr >> (11 - (4 * j + i))) & 1u);
+        lt |= eq & ~R[i] & tb;
+        eq &= ~(R[i] ^ tb);
+    }
+}
+
 template <typename DrawFn>
 __device__ __forceinline__ uint32_t smask_compare(uint32_t thr, uint32_t cand, DrawFn drawj) {
     if (thr >= 4096u) return cand;
@@ -129,18 +141,7 @@ __device__ __forceinline__ uint32_t smask_compare(uint32_t thr, uint32_t cand, D
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
         if (eq == 0u) break;
-        const u32x4 r = drawj((uint32_t)j);
-        const uint32_t R[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int bit = 11 - (4 * j + i);
-            if ((thr >> bit) & 1u) {
-                lt |= eq & ~R[i];
-                eq &= R[i];
-            } else {
-                eq &= ~R[i];
-            }
-        }
+        smask_planes(thr, j, drawj((uint32_t)j), lt, eq);
     }
     return lt;
 }

@@ -4,16 +4,20 @@
 // (kernel.cu:397-613): one thread per clause walks classes and then all L
 // literals as u32 states, drawing one curand uniform per eligible literal.
 //
-// Here a CTA owns one clause.  Per chunk of up to 256 samples:
-//  1. all (sample, class) Q-selection and update draws run in parallel; then
-//     threads over classes walk the samples in order to fix each feedback type
-//     (it depends on the weight sign), updating weights in shared memory;
-//  2. the decided events are compacted into a list in (sample, class) order;
+// Here a CTA owns one clause.  A one-block kernel first turns the batch's
+// class sums into update thresholds and the list of (sample, class) pairs
+// whose threshold is non-zero (only those can update any clause; once a model
+// has converged most pairs drop out).  Then per chunk of up to 128 samples:
+//  1. the Q-selection and update draws of the active pairs run in parallel;
+//     threads over classes walk their active samples in order to fix each
+//     feedback type (it depends on the weight sign), updating weights in
+//     shared memory;
+//  2. the decided events are compacted into a list in feedback order;
 //  3. threads over literal words load the word's bit planes once, apply every
 //     event of the chunk in order with bit-parallel ripple adders (32 literals
 //     per instruction), and store the planes once.
-// The state therefore makes one read-modify-write trip through HBM per chunk,
-// however many events the chunk holds.
+// The state therefore makes one read-modify-write trip through memory per
+// chunk, however many events the chunk holds.
 //
 // Small batches (at most 32 samples) run the same steps with one WARP per
 // clause (WPC): the decision phases then cost warp syncs instead of CTA
@@ -22,7 +26,9 @@
 
 namespace ytm {
 
-constexpr int UPD_BC_MAX = 256;  // samples per chunk at most (list entries hold 8-bit rows)
+// samples per chunk at most (list entries hold 8-bit rows); 128 keeps the
+// event list small enough for ~16 clause CTAs per SM at 10 classes
+constexpr int UPD_BC_MAX = 128;
 
 // One block prepares the batch's decisions, which every clause shares.
 //  * thr[b][k] = floor(p * 2^32) of the update probability, bit 63 set when
