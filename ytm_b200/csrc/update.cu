@@ -169,7 +169,8 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                                                 const uint32_t *__restrict__ lits, int B, uint64_t t0,
                                                 const int32_t *__restrict__ sel, int32_t *__restrict__ patch_w,
                                                 int BC, const RoundKeys rk, int rk_ok,
-                                                int count_patch, const uint32_t *__restrict__ colm,
+                                                int count_patch, const int32_t *__restrict__ pair,
+                                                const uint32_t *__restrict__ amask, const uint32_t *__restrict__ colm,
                                                 const int32_t *__restrict__ row_off,
                                                 const uint32_t *__restrict__ alist) {
     extern __shared__ __align__(16) unsigned char small[];
@@ -180,7 +181,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
     if (drop && drop[c] == 1u) return;  // kernel.cu:555
     const int k0 = cfg.coalesced ? 0 : (int)(g / (uint32_t)cfg.clauses_per_class);
     const int nk = cfg.coalesced ? K : 1;
-    const int BW = (B + 31) >> 5;
+    const int BW = (B + 31) >> 5, KWm = (K + 31) >> 5;
     unsigned char *smraw = WPC ? small + (threadIdx.x >> 5) * update_smem_aligned(nk, BC) : small;
     int32_t *wk = (int32_t *)smraw;                       // [nk]
     int32_t *sel_s = wk + nk;                             // [BC]
@@ -266,32 +267,48 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
             wk[kk] = wv;
         }
         block_sync<WPC>();
-        // 2. the events in the active pairs' order
+        // 2. the events in feedback order: a lane per sample counts and then
+        //    writes its events (classes in order; pytm's rules: the true
+        //    class first); only active pairs hold event types
         if (tid < 32) {  // WPC: the whole warp
             int base = 0;
-            const int n = cfg.coalesced ? hi - lo : bc;
-            for (int r0 = 0; r0 < n; r0 += 32) {
-                const int i = r0 + lane;
-                uint32_t ent = 0u;
-                if (i < n) {
-                    int bl, kk;
-                    bool act = true;
+            for (int r0 = 0; r0 < bc; r0 += 32) {
+                const int row = r0 + lane;
+                const int64_t b = b0 + row;
+                int n = 0;
+                if (row < bc) {
                     if (cfg.coalesced) {
-                        const uint32_t e = alist[lo + i];
-                        const int b = (int)(e / (uint32_t)K);
-                        bl = b - b0;
-                        kk = (int)(e - (uint32_t)b * (uint32_t)K);
+                        for (int m = 0; m < KWm; ++m)
+                            for (uint32_t v = amask[b * KWm + m]; v; v &= v - 1u)
+                                n += evt[row * nk + m * 32 + __ffs(v) - 1] != EV_NONE;
                     } else {
-                        bl = i;
-                        kk = 0;
-                        act = (mycol[(b0 + bl) >> 5] >> ((b0 + bl) & 31)) & 1u;
+                        n = ((mycol[b >> 5] >> (b & 31)) & 1u) && evt[row] != EV_NONE;
                     }
-                    const uint32_t ev = act ? evt[bl * nk + kk] : EV_NONE;
-                    if (ev != EV_NONE) ent = ((uint32_t)bl << 24) | (ev << 22) | (uint32_t)kk;
                 }
-                const uint32_t bal = __ballot_sync(0xFFFFFFFFu, ent != 0u);
-                if (ent) list[base + __popc(bal & ((1u << lane) - 1u))] = ent;
-                base += __popc(bal);
+                int incl = n;
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                    if (lane >= o) incl += v;
+                }
+                int pos = base + incl - n;
+                if (n && !cfg.coalesced) {
+                    list[pos] = ((uint32_t)row << 24) | ((uint32_t)evt[row] << 22);
+                } else if (n && cfg.one_negative) {
+                    for (int q = 0; q < 2; ++q) {
+                        const int k = pair[2 * b + q];
+                        if (k < 0 || !((amask[b * KWm + (k >> 5)] >> (k & 31)) & 1u)) continue;
+                        const uint32_t ev = evt[row * nk + k];
+                        if (ev != EV_NONE) list[pos++] = ((uint32_t)row << 24) | (ev << 22) | (uint32_t)k;
+                    }
+                } else if (n) {
+                    for (int m = 0; m < KWm; ++m)
+                        for (uint32_t v = amask[b * KWm + m]; v; v &= v - 1u) {
+                            const int k = m * 32 + __ffs(v) - 1;
+                            const uint32_t ev = evt[row * nk + k];
+                            if (ev != EV_NONE) list[pos++] = ((uint32_t)row << 24) | (ev << 22) | (uint32_t)k;
+                        }
+                }
+                base += __shfl_sync(0xFFFFFFFFu, incl, 31);
             }
             if (lane == 0) cnt[0] = base;
         }
@@ -391,7 +408,8 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
     if (B <= 32 && smem_wpc <= 48 * 1024) {
         YTM_DISPATCH_PLANES(cfg->planes, {
             k_update<NB, true><<<(unsigned)cdiv(cfg->clause_count, 8), 256, smem_wpc, st>>>(
-                *cfg, state, weights, thr, drop, lits, B, t0, sel, patch_w, 32, rk, rk_ok, count_patch, colm, row_off, alist);
+                *cfg, state, weights, thr, drop, lits, B, t0, sel, patch_w, 32, rk, rk_ok, count_patch, pair, amask, colm, row_off,
+                alist);
         });
         return launch_check("feedback");
     }
@@ -404,8 +422,8 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
                 return rc;
         }
         k_update<NB, false><<<cfg->clause_count, tpb, smem, st>>>(*cfg, state, weights, thr, drop, lits, B, t0, sel,
-                                                                  patch_w, BC, rk, rk_ok, count_patch, colm,
-                                                                  row_off, alist);
+                                                                  patch_w, BC, rk, rk_ok, count_patch, pair,
+                                                                  amask, colm, row_off, alist);
     });
     return launch_check("feedback");
 }
