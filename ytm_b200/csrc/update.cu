@@ -126,11 +126,17 @@ __device__ __forceinline__ void block_sync() {
 }
 
 // Shared memory of one clause: weights [nk], picks [bc], count, event list
-// [bc*nk], event types [bc*nk].
+// [bc*nk], fired samples [bc/32], event types [bc*nk], simple classes [nk].
+// update_smem() (without the last two small arrays' padding) sizes the chunk.
 static __host__ __device__ inline size_t update_smem(int nk, int bc) {
     return (size_t)nk * 4 + (size_t)bc * 4 + 4 + (size_t)bc * nk * 4 + (size_t)bc * nk + 16;
 }
-static __host__ __device__ inline size_t update_smem_aligned(int nk, int bc) { return (update_smem(nk, bc) + 15) & ~(size_t)15; }
+static __host__ __device__ inline size_t update_smem_total(int nk, int bc) {
+    return update_smem(nk, bc) + (size_t)(bc / 32) * 4 + (size_t)nk;
+}
+static __host__ __device__ inline size_t update_smem_aligned(int nk, int bc) {
+    return (update_smem_total(nk, bc) + 15) & ~(size_t)15;
+}
 
 enum : uint32_t { EV_NONE = 0, EV_T1A = 1, EV_T1B = 2, EV_T2 = 3 };
 
@@ -187,7 +193,9 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
     int32_t *sel_s = wk + nk;                             // [BC]
     int32_t *cnt = sel_s + BC;                            // [1]
     uint32_t *list = (uint32_t *)(cnt + 1);               // [BC * nk]
-    uint8_t *evt = (uint8_t *)(list + BC * nk);           // [BC * nk], valid at active pairs only
+    uint32_t *fm = list + BC * nk;                        // [BC / 32] samples whose clause output is 1
+    uint8_t *evt = (uint8_t *)(fm + BC / 32);             // [BC * nk], valid at active pairs only
+    uint8_t *simple = evt + BC * nk;                      // [nk] no active sample of the class fired
     const int tid = WPC ? (int)(threadIdx.x & 31) : (int)threadIdx.x, nt = WPC ? 32 : (int)blockDim.x;
     const int lane = tid & 31;
     // include count of the batch-start state (pack_clauses, kernel.cu:155-204):
@@ -218,26 +226,52 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
 
     for (int b0 = 0; b0 < B; b0 += BC) {  // BC is a multiple of 32
         const int bc = min(BC, B - b0);
-        for (int q = tid; q < bc; q += nt) {
-            sel_s[q] = sel[(int64_t)(b0 + q) * C + c];
-            fired_count += sel_s[q] >= 0;
+        for (int q0 = tid & ~31; q0 < bc; q0 += nt) {  // warp-uniform
+            const int q = q0 + lane;
+            int32_t sv = -1;
+            if (q < bc) {
+                sv = sel[(int64_t)(b0 + q) * C + c];
+                sel_s[q] = sv;
+                fired_count += sv >= 0;
+            }
+            const uint32_t f = __ballot_sync(0xFFFFFFFFu, sv >= 0);
+            if (lane == 0) fm[q0 >> 5] = f;
         }
+        block_sync<WPC>();
+        // A class none of whose active samples fired the clause is simple:
+        // its events are Type Ib or none, fixed by the weight's sign, and its
+        // weight stays as it is for the chunk (kernel.cu:584-606).
+        for (int kk = tid; kk < nk; kk += nt) {
+            const uint32_t *cm = colm + (int64_t)(k0 + kk) * BW + (b0 >> 5);
+            uint32_t hit = 0u;
+            for (int gi = 0; gi < (bc + 31) >> 5; ++gi) hit |= cm[gi] & fm[gi];
+            simple[kk] = hit == 0u;
+        }
+        block_sync<WPC>();
         const int lo = cfg.coalesced ? row_off[b0] : 0, hi = cfg.coalesced ? row_off[b0 + bc] : 0;
         // 1a. the Q-selection and update draws of the active pairs, in
-        //     parallel: 1 = update with target +1, 2 = with target -1
+        //     parallel: 1 = update with target +1, 2 = with target -1; simple
+        //     classes get their event type here (Ib when target and weight
+        //     sign agree)
         for (int idx = lo + tid; idx < hi; idx += nt) {  // coalesced: the chunk's pairs
             const uint32_t e = alist[idx];
             const int b = (int)(e / (uint32_t)K), k = (int)(e - (uint32_t)b * (uint32_t)K);
-            evt[(b - b0) * nk + k] = decide(cfg, rk, rk_ok, thr, g, t0, b, k, K);
+            uint8_t a = decide(cfg, rk, rk_ok, thr, g, t0, b, k, K);
+            if (simple[k]) a = (a && ((a == 1) == (wk[k] >= 0))) ? EV_T1B : EV_NONE;
+            evt[(b - b0) * nk + k] = a;
         }
         if (!cfg.coalesced)
             for (int bl = tid; bl < bc; bl += nt)
-                if ((mycol[(b0 + bl) >> 5] >> ((b0 + bl) & 31)) & 1u)
-                    evt[bl] = decide(cfg, rk, rk_ok, thr, g, t0, b0 + bl, k0, K);
+                if ((mycol[(b0 + bl) >> 5] >> ((b0 + bl) & 31)) & 1u) {
+                    uint8_t a = decide(cfg, rk, rk_ok, thr, g, t0, b0 + bl, k0, K);
+                    if (simple[0]) a = (a && ((a == 1) == (wk[0] >= 0))) ? EV_T1B : EV_NONE;
+                    evt[bl] = a;
+                }
         block_sync<WPC>();
         // 1b. feedback types, class-parallel and sample-sequential over the
         //     class's active samples (weights evolve)
         for (int kk = tid; kk < nk; kk += nt) {
+            if (simple[kk]) continue;
             int32_t wv = wk[kk];
             const uint32_t *cm = colm + (int64_t)(k0 + kk) * BW + (b0 >> 5);
             for (int gi = 0; gi < (bc + 31) >> 5; ++gi) {
@@ -397,7 +431,7 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
     // event list fits 32 KB of shared memory (keeps several CTAs per SM)
     int BC = std::min(UPD_BC_MAX, ((B + 31) / 32) * 32);
     while (BC > 32 && update_smem(nk, BC) > 32 * 1024) BC -= 32;
-    const size_t smem = update_smem(nk, BC);
+    const size_t smem = update_smem_total(nk, BC);
     if (smem > 227 * 1024) return fail(YTM_ERR_UNSUPPORTED, "too many classes for the feedback kernel");
     // round keys for the batch's samples when they share the counter's high word
     const RoundKeys rk = round_keys(cfg->seed, (uint32_t)(t0 >> 32));
