@@ -231,6 +231,14 @@ struct Counter {
         return l;
     }
     // literals whose stored value is not all ones (below the top)
+    // literals whose stored value is not v (= the stored zero state, offset):
+    // when offset + 1 == 2^(NB-2) (state counts that are powers of two, e.g.
+    // 256 on 9 planes) a stored value is above the offset exactly when one of
+    // the two top planes is set
+    __device__ __forceinline__ uint32_t nonzero(uint32_t v, bool top2) const {
+        if (NB >= 2 && top2) return p[NB - 1] | p[NB - 2];
+        return ne(v);
+    }
     __device__ __forceinline__ uint32_t below_top() const {
         uint32_t a = 0xFFFFFFFFu;
 #pragma unroll

@@ -143,6 +143,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     // ---- 2. per clause: feedback over the words, then evaluation of sample i+1
     const uint32_t max_s = (uint32_t)(cfg.max_state + cfg.state_offset);
     const uint32_t zero_s = (uint32_t)cfg.state_offset;
+    const bool top2 = NB >= 2 && (uint32_t)cfg.state_offset + 1u == (1u << (NB >= 2 ? NB - 2 : 0));
     const uint32_t *x_next = lits + e_next * P * W;  // patch 0 of sample i+1 (single-patch eval)
     constexpr int CPW = CPB / FB_WARPS;  // clauses per warp
     bool has_ev[CPW];
@@ -208,9 +209,9 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
                         uint32_t cand;
                         if ((m1a >> b) & 1u) {  // type1a_fb, kernel.cu:410-443
                             ctr.inc(x & vm & ctr.lt(max_s));
-                            cand = ~x & vm & ctr.ne(zero_s);
+                            cand = ~x & vm & ctr.nonzero(zero_s, top2);
                         } else {  // type1b_fb, kernel.cu:453-470
-                            cand = vm & ctr.ne(zero_s);
+                            cand = vm & ctr.nonzero(zero_s, top2);
                         }
                         if (cand)
                             ctr.dec(smask_word_rk(rk, cfg.s_threshold12, cand, g, t,

@@ -220,6 +220,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
     int fired_count = 0;  // single-patch models: patch 0 picks of this clause (select_active, kernel.cu:305)
     const uint32_t max_s = (uint32_t)(cfg.max_state + cfg.state_offset);
     const uint32_t zero_s = (uint32_t)cfg.state_offset;
+    const bool top2 = NB >= 2 && (uint32_t)cfg.state_offset + 1u == (1u << (NB >= 2 ? NB - 2 : 0));
     const uint32_t *mycol = colm + (int64_t)k0 * BW;  // non-coalesced: the active samples of the bank's class
 
     for (int kk = tid; kk < nk; kk += nt) wk[kk] = weights[(int64_t)c * K + k0 + kk];
@@ -370,9 +371,9 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                         if (ev == EV_T1A) {  // type1a_fb, kernel.cu:410-443
                             const uint32_t x = lits[((int64_t)b * P + sel_s[bl]) * W + w];
                             ctr.inc(x & vm & ctr.lt(max_s));
-                            cand = ~x & vm & ctr.ne(zero_s);
+                            cand = ~x & vm & ctr.nonzero(zero_s, top2);
                         } else {  // type1b_fb, kernel.cu:453-470
-                            cand = vm & ctr.ne(zero_s);
+                            cand = vm & ctr.nonzero(zero_s, top2);
                         }
                         if (cand)
                             ctr.dec(rk_ok ? smask_word_rk(rk, cfg.s_threshold12, cand, g, t, (uint32_t)k, (uint32_t)w)
