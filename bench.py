@@ -375,12 +375,10 @@ def main():
         alg_bytes = S * (cfg.clause_count * cfg.planes * cfg.words * 4 * 2 + cfg.words * 4 * cfg.patches)
         kernel = "k_fused_b1 (feedback of sample i + evaluation of sample i+1), per 256 launches"
     else:
-        nk = cfg.n_classes if cfg.coalesced else 1
-        bc = min(128, (B + 31) // 32 * 32)  # k_update's chunk: event list within 32 KB of shared memory
-        while bc > 32 and nk * 4 + bc * 4 + 4 + bc * nk * 5 + 16 > 32 * 1024:
-            bc -= 32
-        chunks = (B + bc - 1) // bc
-        alg_bytes = cfg.clause_count * chunks * cfg.planes * cfg.words * 4 * 2 + B * cfg.words * 4 * cfg.patches
+        # one read and one write of every clause's bit planes per launch (the
+        # kernel streams them once per chunk of samples; the roofline counts
+        # the minimum), plus the batch's literals
+        alg_bytes = cfg.clause_count * cfg.planes * cfg.words * 4 * 2 + B * cfg.words * 4 * cfg.patches
         kernel = "k_update (feedback)"
     # this library's kernels in one step, counted from the CUDA activity trace
     launches = count_launches(lambda: step((args.warmup + args.steps) % max(1, n_train // S)))

@@ -46,31 +46,54 @@ __global__ void __launch_bounds__(1024) k_thresholds(const int32_t *__restrict__
                                                      const int32_t *__restrict__ pair, uint64_t *__restrict__ thr,
                                                      uint32_t *__restrict__ amask, uint32_t *__restrict__ colm,
                                                      int32_t *__restrict__ row_off, uint32_t *__restrict__ alist) {
+    constexpr int AM_SMEM = 8192;  // words of amask kept in shared memory
+    __shared__ uint32_t am_s[AM_SMEM];
     __shared__ int wsum[32];
     __shared__ int base_s;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int KWm = (K + 31) >> 5, BW = (B + 31) >> 5;
-    for (int64_t u = wid; u < (int64_t)B * KWm; u += nw) {
-        const int64_t b = u / KWm;
-        const int k = (int)(u - b * KWm) * 32 + lane;
-        bool act = false;
-        if (k < K) {
-            int32_t v = cs[b * K + k];
+    const int64_t nam = (int64_t)B * KWm;
+    const bool in_smem = nam <= AM_SMEM;
+    if (in_smem) {  // a thread per pair; the bits gather in shared memory
+        for (int i = threadIdx.x; i < nam; i += blockDim.x) am_s[i] = 0u;
+        __syncthreads();
+        for (int i = threadIdx.x; i < B * K; i += blockDim.x) {
+            const int b = i / K, k = i - b * K;
+            int32_t v = cs[i];
             v = v > T ? T : (v < -T ? -T : v);  // clip_cs, kernel.cu:397
-            const int32_t y = Y[b * K + k];
+            const int32_t y = Y[i];
             uint64_t t = update_threshold(y, v);
-            act = t != 0ull && (!one_neg || k == pair[2 * b] || k == pair[2 * b + 1]);
+            if (t != 0ull && (!one_neg || k == pair[2 * b] || k == pair[2 * b + 1]))
+                atomicOr(&am_s[b * KWm + (k >> 5)], 1u << (k & 31));
             if (v > y) t |= 1ull << 63;
-            thr[b * K + k] = t;
+            thr[i] = t;
         }
-        const uint32_t m = __ballot_sync(0xFFFFFFFFu, act);
-        if (lane == 0) amask[u] = m;
+        __syncthreads();
+        for (int i = threadIdx.x; i < nam; i += blockDim.x) amask[i] = am_s[i];
+    } else {  // a warp per (sample, 32 classes)
+        for (int64_t u = wid; u < nam; u += nw) {
+            const int64_t b = u / KWm;
+            const int k = (int)(u - b * KWm) * 32 + lane;
+            bool act = false;
+            if (k < K) {
+                int32_t v = cs[b * K + k];
+                v = v > T ? T : (v < -T ? -T : v);
+                const int32_t y = Y[b * K + k];
+                uint64_t t = update_threshold(y, v);
+                act = t != 0ull && (!one_neg || k == pair[2 * b] || k == pair[2 * b + 1]);
+                if (v > y) t |= 1ull << 63;
+                thr[b * K + k] = t;
+            }
+            const uint32_t m = __ballot_sync(0xFFFFFFFFu, act);
+            if (lane == 0) amask[u] = m;
+        }
     }
+    const uint32_t *am_all = in_smem ? am_s : amask;
     if (threadIdx.x == 0) base_s = 0;
     __syncthreads();
     for (int64_t u = wid; u < (int64_t)K * BW; u += nw) {
         const int k = (int)(u / BW), row = (int)(u - (int64_t)k * BW) * 32 + lane;
-        const bool a = row < B && ((amask[(int64_t)row * KWm + (k >> 5)] >> (k & 31)) & 1u);
+        const bool a = row < B && ((am_all[(int64_t)row * KWm + (k >> 5)] >> (k & 31)) & 1u);
         const uint32_t m = __ballot_sync(0xFFFFFFFFu, a);
         if (lane == 0) colm[u] = m;
     }
@@ -78,7 +101,7 @@ __global__ void __launch_bounds__(1024) k_thresholds(const int32_t *__restrict__
         const int row = r0 + threadIdx.x;
         int n = 0;
         if (row < B)
-            for (int m = 0; m < KWm; ++m) n += __popc(amask[(int64_t)row * KWm + m]);
+            for (int m = 0; m < KWm; ++m) n += __popc(am_all[(int64_t)row * KWm + m]);
         int incl = n;
         for (int o = 1; o < 32; o <<= 1) {
             const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
@@ -98,7 +121,7 @@ __global__ void __launch_bounds__(1024) k_thresholds(const int32_t *__restrict__
         int pos = base_s + (wid ? wsum[wid - 1] : 0) + incl - n;
         if (row < B) {
             row_off[row] = pos;
-            const uint32_t *am = amask + (int64_t)row * KWm;
+            const uint32_t *am = am_all + (int64_t)row * KWm;
             if (one_neg) {
                 for (int q = 0; q < 2; ++q) {
                     const int k = pair[2 * row + q];
