@@ -49,6 +49,7 @@ TrainWs train_ws_layout(const ytm_config *cfg, int64_t B) {
     l.mbits = o; o = align_up(o + (uint64_t)B * C * PW * 4, 256);
     l.fired = o; o = align_up(o + (uint64_t)B * CW * 4, 256);  // right after mbits: one memset clears both
     l.sel = o;   o = align_up(o + (uint64_t)B * C * 4, 256);
+    l.fcm = o;   o = align_up(o + C * cdiv(B, 32) * 4, 256);  // single patch: clause-major fired bits
     l.thr = o;   o = align_up(o + (uint64_t)B * K * 8, 256);
     // (sample, class) pairs that can update: bits per sample, bits per class,
     // and the list in feedback order with each sample's offset into it

@@ -284,7 +284,7 @@ ytm_status check_cfg(const ytm_config *cfg);
 
 // Workspace carve-up (offsets in bytes, 256-aligned).
 struct TrainWs {
-    uint64_t ninc, mbits, sel, fired, thr, amask, colm, row_off, alist, pair, sparse, total;
+    uint64_t ninc, mbits, sel, fired, fcm, thr, amask, colm, row_off, alist, pair, sparse, total;
 };
 TrainWs train_ws_layout(const ytm_config *cfg, int64_t B);
 struct InferWs {

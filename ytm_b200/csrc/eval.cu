@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(256) k_train_eval1(ytm_config cfg, const uint3
                                                      const uint32_t *__restrict__ lits, int B,
                                                      const int32_t *__restrict__ weights,
                                                      const uint32_t *__restrict__ drop, int32_t *__restrict__ sel,
-                                                     uint32_t *__restrict__ fired, int32_t *__restrict__ cs) {
+                                                     uint32_t *__restrict__ fcm, int32_t *__restrict__ cs) {
     __shared__ __align__(16) uint32_t xs[KW][XS];
     __shared__ __align__(16) uint32_t is[KW][XS];
     extern __shared__ int32_t w_s[];  // [CT][K]
@@ -314,7 +314,7 @@ __global__ void __launch_bounds__(256) k_train_eval1(ytm_config cfg, const uint3
 #pragma unroll
     for (int j = 0; j < 4; ++j)
         if (cb + j < C && !(drop && drop[cb + j] == 1u)) keep |= 1u << j;
-    const int CWn = (C + 31) / 32;
+    uint32_t cbits[4] = {0u, 0u, 0u, 0u};  // per clause of this thread: its 4 rows' outputs
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int64_t row = row0 + ty * 4 + i;
@@ -324,11 +324,14 @@ __global__ void __launch_bounds__(256) k_train_eval1(ytm_config cfg, const uint3
         for (int j = 0; j < 4; ++j)
             if (v[i][j] == 0u) nib |= 1u << j;
         nib &= keep;
+        if (!rv) nib = 0u;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) cbits[j] |= ((nib >> j) & 1u) << i;
         if (rv) {
 #pragma unroll
             for (int j = 0; j < 4; ++j)
                 if (cb + j < C) sel[row * C + cb + j] = ((nib >> j) & 1u) ? 0 : -1;
-            if (fired && nib) atomicOr(&fired[row * CWn + (cb >> 5)], nib << (cb & 31));
+
         }
         for (int k = 0; k < K; ++k) {
             int32_t part = 0;
@@ -342,13 +345,23 @@ __global__ void __launch_bounds__(256) k_train_eval1(ytm_config cfg, const uint3
             if (tx == 0 && rv && part != 0) atomicAdd(&cs[row * K + k], part);
         }
     }
+    if (fcm) {  // clause-major fired bits [C][ceil(B/32)] for the feedback kernel
+        const int BWn = (B + 31) / 32;
+        const int64_t r4 = row0 + ty * 4;  // 4-aligned: the 4 rows share one word
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (cbits[j]) atomicOr(&fcm[(int64_t)(cb + j) * BWn + (r4 >> 5)], cbits[j] << (r4 & 31));
+    }
 }
 
-__global__ void k_cs_init(int32_t *__restrict__ cs, const int32_t *__restrict__ bias, int64_t N, int K) {
+__global__ void k_cs_init(int32_t *__restrict__ cs, const int32_t *__restrict__ bias, int64_t N, int K,
+                          uint32_t *__restrict__ zero = nullptr, int64_t nzero = 0) {
     int64_t total = N * K;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x)
         cs[i] = bias ? bias[i % K] : 0;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nzero; i += (int64_t)gridDim.x * blockDim.x)
+        zero[i] = 0u;
 }
 
 // cs[n][k] += sum over fired clauses c of w[c][k].  A warp takes 32 bitmap
@@ -741,8 +754,10 @@ ytm_status ytm_train_eval(const ytm_config *cfg, const uint32_t *state, const in
     if (single_patch_eval(cfg)) {
         // single patch: one fused kernel (picks and class sums; the feedback
         // kernel counts the picks in patch_w)
-        k_cs_init<<<grid1((int64_t)B * cfg->n_classes), 256, 0, st>>>(cs, add_bias ? bias : nullptr, B,
-                                                                        cfg->n_classes);
+        uint32_t *fcm = (uint32_t *)(ws + l.fcm);
+        const int64_t nfcm = (int64_t)C * cdiv(B, 32);
+        k_cs_init<<<grid1(std::max<int64_t>((int64_t)B * cfg->n_classes, nfcm)), 256, 0, st>>>(
+            cs, add_bias ? bias : nullptr, B, cfg->n_classes, fcm, nfcm);
         if ((rc = launch_check("cs init"))) return rc;
         const size_t smem = (size_t)CT * cfg->n_classes * 4;
         if (smem > 48 * 1024 &&
@@ -752,7 +767,7 @@ ytm_status ytm_train_eval(const ytm_config *cfg, const uint32_t *state, const in
         const int64_t gx = (int64_t)cdiv(B, RT), gy = (int64_t)cdiv(C, CT);
         if (gy > 65535) return fail(YTM_ERR_UNSUPPORTED, "too many clauses for one launch");
         k_train_eval1<<<dim3((unsigned)gx, (unsigned)gy), 256, smem, st>>>(*cfg, inc, lits, B, weights, drop, sel,
-                                                                           nullptr, cs);
+                                                                           fcm, cs);
         return launch_check("train eval");
     }
     // training semantics: an empty clause matches every patch (kernel.cu:273-276)

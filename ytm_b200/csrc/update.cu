@@ -201,7 +201,8 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                                                 int count_patch, const int32_t *__restrict__ pair,
                                                 const uint32_t *__restrict__ amask, const uint32_t *__restrict__ colm,
                                                 const int32_t *__restrict__ row_off,
-                                                const uint32_t *__restrict__ alist) {
+                                                const uint32_t *__restrict__ alist,
+                                                const uint32_t *__restrict__ fcm) {
     extern __shared__ __align__(16) unsigned char small[];
     const int C = cfg.clause_count, W = cfg.words, K = cfg.n_classes, P = cfg.patches;
     const int c = WPC ? (int)(blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) : (int)blockIdx.x;
@@ -253,8 +254,13 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
         for (int q0 = tid & ~31; q0 < bc; q0 += nt) {  // warp-uniform
             const int q = q0 + lane;
             int32_t sv = -1;
-            if (q < bc) {
+            if (fcm) {  // single patch: the clause's fired bits (pick = patch 0)
+                const uint32_t f = fcm[(int64_t)c * BW + ((b0 + q0) >> 5)];
+                if (q < bc) sv = ((f >> lane) & 1u) ? 0 : -1;
+            } else if (q < bc) {
                 sv = sel[(int64_t)(b0 + q) * C + c];
+            }
+            if (q < bc) {
                 sel_s[q] = sv;
                 fired_count += sv >= 0;
             }
@@ -437,6 +443,9 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
     TrainWs l = train_ws_layout(cfg, B);
     char *ws = (char *)workspace;
     const int32_t *sel = sel_override ? sel_override : (const int32_t *)(ws + l.sel);
+    // single-patch batches evaluated by ytm_train_eval leave clause-major
+    // fired bits, which the feedback reads instead of the [B][C] picks
+    const uint32_t *fcm = (!sel_override && count_patch) ? (const uint32_t *)(ws + l.fcm) : nullptr;
     uint64_t *thr = (uint64_t *)(ws + l.thr);
     int32_t *pair = (int32_t *)(ws + l.pair);
     uint32_t *amask = (uint32_t *)(ws + l.amask);
@@ -467,7 +476,7 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
         YTM_DISPATCH_PLANES(cfg->planes, {
             k_update<NB, true><<<(unsigned)cdiv(cfg->clause_count, 8), 256, smem_wpc, st>>>(
                 *cfg, state, weights, thr, drop, lits, B, t0, sel, patch_w, 32, rk, rk_ok, count_patch, pair, amask, colm, row_off,
-                alist);
+                alist, fcm);
         });
         return launch_check("feedback");
     }
@@ -481,7 +490,7 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
         }
         k_update<NB, false><<<cfg->clause_count, tpb, smem, st>>>(*cfg, state, weights, thr, drop, lits, B, t0, sel,
                                                                   patch_w, BC, rk, rk_ok, count_patch, pair,
-                                                                  amask, colm, row_off, alist);
+                                                                  amask, colm, row_off, alist, fcm);
     });
     return launch_check("feedback");
 }

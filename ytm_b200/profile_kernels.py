@@ -10,13 +10,36 @@ cudaProfilerStart; the profiled range then holds one training batch and one
 inference pass of configuration 2 (65,536 samples), a transform, an encode,
 two fused batch-1 samples each of configurations 1 and 3, a patch-wise
 transform and a thermometer encode.
+
+    python -m ytm_b200.profile_kernels --converged N
+
+instead trains the configuration-2 model for N batches of 256 samples (no
+profiler range) and then profiles one more batch (evaluation, thresholds,
+feedback): the feedback of a converged model, where few (sample, class)
+pairs are still active.
 """
+import sys
+
 import numpy as np
 import torch
 
 from ytm_b200 import synthetic
 from ytm_b200.cutm import MultiClassTM
 torch.cuda.set_device(0)
+if len(sys.argv) > 2 and sys.argv[1] == '--converged':
+    nb = int(sys.argv[2])
+    X, y = synthetic.make('c2', 256 * (nb + 1))
+    tm = MultiClassTM(seed=42, **synthetic.MODELS['c2'])
+    lits = tm._encode_device(X); Y = torch.from_numpy(tm.encode_Y(y)).cuda(); e = tm.engine
+    for i in range(nb + 1):
+        if i == nb:
+            torch.cuda.synchronize()
+            torch.cuda.profiler.start()
+        cs = e.train_eval(lits[i*256:(i+1)*256], i*256, None, True); e.train_update(cs, Y[i*256:(i+1)*256], lits[i*256:(i+1)*256], i*256, None)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    print('done', flush=True)
+    sys.exit(0)
 X, y = synthetic.make('c2', 256 * 5)
 tm = MultiClassTM(seed=42, **synthetic.MODELS['c2'])
 lits = tm._encode_device(X); Y = torch.from_numpy(tm.encode_Y(y)).cuda(); e = tm.engine
