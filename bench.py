@@ -29,9 +29,11 @@ sys.path.insert(0, ROOT)
 
 METRIC = "train & infer samples/s (1/2/4/8 B200) + % of HBM/INT-pipe roofline vs CPU"
 L2_BYTES = 126 * 1024 * 1024
-# DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
-# capture each (profiles/k_update_c2.md); None where no capture was made.
-TRAFFIC = {"c2": 28.37e6 + 0.056e6}
+# DRAM bytes (read + write) per launch of the dominant kernel in the regime
+# bench.py times it in (a converged model), from one ncu capture of
+# `python -m ytm_b200.profile_kernels --converged 100`; None where no capture
+# was made.
+TRAFFIC = {"c2": 11.8976e6}
 
 
 def load_peaks():
