@@ -147,6 +147,58 @@ def test_training_matches_oracle(case):
     np.testing.assert_array_equal(host(e.transform_patchwise(lits)), o.transform_patchwise(ta, lits_h))
 
 
+CONVERGED_CASES = {
+    # name: (model, batch, oracle/engine modes); batch 150 spans two feedback
+    # chunks, batches of at most 32 take the warp-per-clause kernel
+    "coalesced_b150": (dict(number_of_clauses_per_class=40, T=8, s=4.0, dim=(40, 1, 1), n_classes=5), 150, {}),
+    "coalesced_b8": (dict(number_of_clauses_per_class=40, T=8, s=4.0, dim=(40, 1, 1), n_classes=5), 8, {}),
+    "vanilla_b16": (dict(number_of_clauses_per_class=12, T=6, s=4.0, dim=(40, 1, 1), n_classes=4, coalesced=False),
+                    16, {}),
+    "pytm_rules_b20": (dict(number_of_clauses_per_class=40, T=8, s=4.0, dim=(40, 1, 1), n_classes=5), 20,
+                       dict(one_negative=True)),
+}
+
+
+@pytest.mark.parametrize("case", sorted(CONVERGED_CASES))
+def test_training_to_convergence_matches_oracle(case):
+    """Twelve epochs on separable prototype data with a small T: the class sums
+    saturate at +-T, so most (sample, class) pairs get a zero update
+    probability (the feedback decides only the active pairs, and classes none
+    of whose active samples fired take the parallel Type Ib path) while about
+    a fifth of the clauses fire.  The engine must stay bit-exact with the
+    oracle, and the run must reach that regime."""
+    kw, bs, modes = CONVERGED_CASES[case]
+    seed, N, D, K = 77, 300, 40, kw["n_classes"]
+    o = O.Oracle(**oracle_kwargs(kw, seed), **modes)
+    cfg = _lib.make_config(**lib_kwargs(kw, seed), **modes)
+    e = CudaEngine(cfg, "cuda:0")
+    rng = np.random.default_rng(5)
+    proto = rng.random((K, D)) < 0.3
+    labels = rng.integers(0, K, N)
+    X = (proto[labels] ^ (rng.random((N, D)) < 0.03)).astype(np.uint32)
+    Y = O.encode_Y_multiclass(labels, K, kw["T"])
+    lits_h, lits, Yd = o.encode(X), e.encode(dev(X)), dev(Y, np.int32)
+    ta, w, pw = o.init_state(), o.init_weights(), np.zeros((o.C, o.P), np.int32)
+    t = 0
+    for epoch in range(12):
+        inactive, fired = [], []
+        for i in range(0, N, bs):
+            B = min(bs, N - i)
+            cs_o, sel_o = o.train_batch(ta, w, pw, lits_h[i:i + B], Y[i:i + B], t)
+            cs = e.train_eval(lits[i:i + B], t, None, add_bias=True)
+            np.testing.assert_array_equal(host(cs), cs_o, err_msg=f"class sums, epoch {epoch}, batch at {i}")
+            e.train_update(cs, Yd[i:i + B], lits[i:i + B], t, None)
+            t += B
+            v = np.clip(cs_o, -kw["T"], kw["T"])
+            inactive.append(np.mean((Y[i:i + B] - v) / (2.0 * Y[i:i + B]) <= 0))
+            fired.append(np.mean(sel_o >= 0))
+        np.testing.assert_array_equal(e.get_ta_state(), ta, err_msg=f"TA states after epoch {epoch}")
+        np.testing.assert_array_equal(host(e.weights), w, err_msg=f"weights after epoch {epoch}")
+        np.testing.assert_array_equal(host(e.patch_w), pw, err_msg=f"patch weights after epoch {epoch}")
+    assert np.mean(inactive) > 0.8, "the run did not reach the converged regime"
+    assert 0.05 < np.mean(fired) < 0.9
+
+
 def test_sharded_engines_match_oracle():
     """Two clause shards on one GPU, class sums summed between the halves of
     each batch, equal the unsharded oracle (the multi-GPU schedule)."""
