@@ -206,7 +206,10 @@ ytm_status ytm_train_eval(const ytm_config *cfg, const uint32_t *state, const in
  * sel_override: i32 [B][C] patch picks to use instead of the ones
  * ytm_train_eval chose (-1 = clause did not fire), or NULL.  patch_w: for
  * single-patch models with up to 256 classes, ytm_train_eval leaves the
- * counting of picks (kernel.cu:305) to this call, which adds them here. */
+ * counting of picks (kernel.cu:305) to this call, which adds them here.
+ * workspace: the one ytm_train_eval filled for this batch; without
+ * sel_override this call reads the picks from it (single-patch models: the
+ * clause outputs, kept there clause by clause). */
 ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, int32_t *weights,
                             const int32_t *cs, const int32_t *Y, const uint32_t *drop,
                             const uint32_t *lits, int32_t B, uint64_t t0,
