@@ -1,8 +1,11 @@
-// probe.cu — LOP3 throughput probe: the INT/logic-pipe ceiling that the
+// bench_probe.cu — measurement helper of bench.py (not part of libytm's
+// ABI): a LOP3 throughput probe giving the INT/logic-pipe ceiling that the
 // clause-evaluation kernels (one LOP3 per word test) are measured against.
-#include "common.cuh"
+// Built into bench_probe.so by ytm_b200.build.build_probe().
+#include <cuda_runtime.h>
+#include <stdint.h>
 
-namespace ytm {
+namespace {
 
 constexpr int PROBE_CHAINS = 8;
 
@@ -22,13 +25,14 @@ __global__ void __launch_bounds__(256) k_probe_lop3(int iters, uint32_t seed, ui
     if (r == 0x12345678u) out[0] = r;  // keeps the chains alive
 }
 
-}  // namespace ytm
+}  // namespace
 
-using namespace ytm;
-
-extern "C" ytm_status ytm_probe_lop3(int32_t blocks, int32_t iters, uint32_t *out, uint64_t *ops, void *stream) {
-    if (blocks <= 0 || iters <= 0 || !out || !ops) return fail(YTM_ERR_ARG, "bad argument");
-    k_probe_lop3<<<blocks, 256, 0, as_stream(stream)>>>(iters, 0x2545F491u, out);
+// Launch `blocks` x 256 threads that each run `iters` x 8 dependent-free LOP3
+// operations (the word-test operation a |= b & ~c); *ops receives the
+// operation count.  Time it with events on `stream`.  Returns a cudaError_t.
+extern "C" int bench_probe_lop3(int32_t blocks, int32_t iters, uint32_t *out, uint64_t *ops, void *stream) {
+    if (blocks <= 0 || iters <= 0 || !out || !ops) return (int)cudaErrorInvalidValue;
+    k_probe_lop3<<<blocks, 256, 0, (cudaStream_t)stream>>>(iters, 0x2545F491u, out);
     *ops = (uint64_t)blocks * 256 * (uint64_t)iters * PROBE_CHAINS;
-    return launch_check("lop3 probe");
+    return (int)cudaGetLastError();
 }

@@ -253,8 +253,10 @@ ytm_status ytm_train_fit_batches(const ytm_config *cfg, uint32_t *state, int32_t
  * sum data[0..n) over the ranks in place on `stream` (every rank must call it
  * the same number of times); a rank that never arrives is reported after
  * `limit` spin iterations (<= 0: default, tens of seconds) through status
- * (0 = all calls completed, else 1 + the index of the missing peer) and the
- * call leaves data unchanged.  ytm_train_fit_batches uses it when peer_ar is
+ * (0 = all calls since the last status read completed, else 1 + the index
+ * of the missing peer; reading it synchronises the device and clears it) and
+ * the call leaves data unchanged: the caller must treat a non-zero status as
+ * fatal for the training run.  ytm_train_fit_batches uses it when peer_ar is
  * given (instead of comm). */
 ytm_status ytm_peer_ar_create(int32_t rank, int32_t world, int64_t max_n, void **ctx_out, uint8_t *handle_out);
 ytm_status ytm_peer_ar_open(void *ctx, const uint8_t *handles);
@@ -268,24 +270,20 @@ ytm_status ytm_train_selection(const ytm_config *cfg, int32_t B, const void *wor
                                int32_t *sel, void *stream);
 
 /* Inference without a workspace, for callers that cannot allocate device
- * memory (code inside a stream capture, embedders whose device memory is
- * handed out by another runtime).  No counterpart in the reference.
+ * memory (embedders whose device memory is handed out by another runtime,
+ * services that forbid allocation after start-up).  No counterpart in the
+ * reference.
  * Same inputs and output as ytm_infer; scratch comes from a fixed array of
  * YTM_NOALLOC_SCRATCH_BYTES that every GPU loading the library keeps until
  * exit.  Calls needing more scratch (include counts + N * ceil(C/32) words of
  * fired bits) fail with YTM_ERR_ARG: split N.  The first call on a device
- * looks up the array's device address and should precede any stream capture.
- * Calls share the array: calls that overlap on the GPU race. */
+ * looks up the array's device address and should precede any stream capture;
+ * the address stays cached, so do not call this after cudaDeviceReset of that
+ * device.  Calls share the array: calls that overlap on the GPU race. */
 #define YTM_NOALLOC_SCRATCH_BYTES (16u << 20)
 ytm_status ytm_infer_noalloc(const ytm_config *cfg, const uint32_t *state, const int32_t *weights,
                              const int32_t *bias, const uint32_t *lits, int64_t N, int32_t *cs,
                              void *stream);
-
-/* Measurement helper (no reference counterpart): launch `blocks` x 256
- * threads that each run `iters` x 8 dependent-free LOP3 operations (the
- * word-test operation a |= b & ~c); *ops receives the operation count.  Time
- * it with events on `stream` to get the logic-pipe ceiling. */
-ytm_status ytm_probe_lop3(int32_t blocks, int32_t iters, uint32_t *out, uint64_t *ops, void *stream);
 
 /* Message of the last failing call on this thread ("" if none). */
 const char *ytm_last_error(void);

@@ -19,7 +19,9 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
-DEFAULT_REF = "/root/reference"
+# the reference checkout: $YTM_REFERENCE, else a `reference` directory beside
+# this repository's root
+DEFAULT_REF = os.environ.get("YTM_REFERENCE") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 KERNEL_REL = os.path.join("src", "cutm", "cuda", "kernel.cu")
 
 # name -> reference constructor kwargs (BaseTM.__init__, base.py:42-74).

@@ -67,8 +67,9 @@ def cutm_reference():
     return out
 
 
-def pytm_reference(ref_root="/root/reference"):
-    sys.path.insert(0, os.path.join(ref_root, "src"))
+def pytm_reference(ref_root=None):
+    from oracle.ref_build import DEFAULT_REF
+    sys.path.insert(0, os.path.join(ref_root or DEFAULT_REF, "src"))
     from pytm.base import BaseTM
     Xtr, ytr, Xte, yte = data()
     accs = []

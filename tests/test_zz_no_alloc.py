@@ -1,6 +1,6 @@
 """ytm_infer_noalloc: inference for callers that cannot allocate device memory
-(work recorded inside a stream capture, or an embedding runtime that hands out
-all device memory itself).  It must give exactly what ytm_infer gives, call
+(an embedding runtime that hands out all device memory itself, or a service
+that forbids allocation after start-up).  It must give exactly what ytm_infer gives, call
 after call, although all calls share one fixed scratch array.
 
 Named test_zz_* so that pytest collects it last."""
@@ -20,9 +20,9 @@ def _p(t):
     return ct.c_void_p(t.data_ptr())
 
 
-def _model(seed):
-    cfg = _lib.make_config(clauses_per_class=300, T=50, s=10.0, dim=(28, 28, 1), n_classes=10, patch_dim=(24, 24),
-                           seed=seed)
+def _model(seed, patch_dim=(24, 24), count_empty=False):
+    cfg = _lib.make_config(clauses_per_class=300, T=50, s=10.0, dim=(28, 28, 1), n_classes=10, patch_dim=patch_dim,
+                           seed=seed, count_empty=count_empty)
     eng = CudaEngine(cfg, "cuda:0")
     rng = np.random.default_rng(seed)
     half = cfg.number_of_ta_states // 2
@@ -47,8 +47,11 @@ def _noalloc(eng, lits):
     return cs
 
 
-def test_noalloc_matches_workspace_inference_twice():
-    eng, rng = _model(21)
+@pytest.mark.parametrize("patch_dim,count_empty", [((24, 24), False), (None, True)])
+def test_noalloc_matches_workspace_inference_twice(patch_dim, count_empty):
+    """Convolutional model (25 patches), and a single-patch model that counts
+    empty clauses (pytm's inference rule)."""
+    eng, rng = _model(21, patch_dim, count_empty)
     for n in (96, 40):  # second call smaller: stale scratch from the first must not leak in
         X = (rng.random((n, 784)) < 0.3).astype(np.uint32)
         lits = eng.encode(torch.from_numpy(X.view(np.int32)).cuda())

@@ -21,7 +21,7 @@ EXPORTS = (
     "ytm_state_from_u32", "ytm_state_to_u32", "ytm_include_mask", "ytm_weights_init", "ytm_infer",
     "ytm_transform", "ytm_transform_patchwise", "ytm_train_eval", "ytm_train_update",
     "ytm_train_selection", "ytm_last_error", "ytm_version", "ytm_infer_noalloc",
-    "ytm_train_fit_b1", "ytm_probe_lop3", "ytm_infer_include",
+    "ytm_train_fit_b1", "ytm_infer_include",
     "ytm_encode_thermometer", "ytm_nccl_unique_id", "ytm_nccl_comm_init", "ytm_nccl_comm_destroy",
     "ytm_train_fit_batches", "ytm_peer_ar_create", "ytm_peer_ar_open", "ytm_peer_allreduce_i32",
     "ytm_peer_ar_status", "ytm_peer_ar_destroy", "ytm_config_size",
@@ -75,7 +75,6 @@ _SIGS = {
     "ytm_train_selection": ([_CFG, _I32, _P, _P, _P], ct.c_int),
     "ytm_train_fit_b1": ([_CFG, _P, _P, _P, _P, _P, _P, _I64, _U64, _P, _P, _P], ct.c_int),
     "ytm_infer_noalloc": ([_CFG, _P, _P, _P, _P, _I64, _P, _P], ct.c_int),
-    "ytm_probe_lop3": ([_I32, _I32, _P, ct.POINTER(ct.c_uint64), _P], ct.c_int),
     "ytm_infer_include": ([_CFG, _P, _P, _P, _P, _I64, _P, _P, _P], ct.c_int),
     "ytm_encode_thermometer": ([_CFG, _P, _I64, _I32, _P, _P, _P], ct.c_int),
     "ytm_nccl_unique_id": ([_P], ct.c_int),

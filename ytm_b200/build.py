@@ -63,6 +63,22 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
     return LIB
 
 
+PROBE_SRC = os.path.join(HERE, "..", "bench_probe.cu")
+PROBE_LIB = os.path.join(HERE, "..", "bench_probe.so")
+
+
+def build_probe(force: bool = False) -> str | None:
+    """bench.py's LOP3 throughput probe (not part of libytm), beside bench.py."""
+    if not os.path.exists(PROBE_SRC):
+        return None
+    if not force and os.path.exists(PROBE_LIB) and os.path.getmtime(PROBE_LIB) >= os.path.getmtime(PROBE_SRC):
+        return PROBE_LIB
+    nvcc = os.environ.get("NVCC", "nvcc")
+    subprocess.run([nvcc, *NVCC_FLAGS, PROBE_SRC, "-o", PROBE_LIB + ".tmp"], check=True)
+    os.replace(PROBE_LIB + ".tmp", PROBE_LIB)
+    return PROBE_LIB
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose=True,
                 extra=["-Xptxas", "-v"] if "--ptxas" in sys.argv else None))

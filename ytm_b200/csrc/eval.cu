@@ -802,10 +802,12 @@ ytm_status ytm_train_selection(const ytm_config *cfg, int32_t B, const void *wor
 // ---------------------------------------------------------------------------
 // Allocation-free inference.
 //
-// Some callers cannot allocate device memory: code running inside a CUDA
-// stream capture, embedders whose memory is carved up in advance by another
-// runtime, or hosts that forbid cudaMalloc after start-up.  ytm_infer_noalloc
-// gives them inference without a workspace argument.  Its scratch (include
+// Some callers cannot allocate device memory: embedders whose device memory
+// is carved up in advance by another runtime or pool allocator (a cudaMalloc
+// of their own would fail or break that runtime's accounting), and services
+// that forbid allocation after start-up so that a request can never fail or
+// stall on it.  ytm_infer_noalloc gives them inference without a workspace
+// argument.  Its scratch (include
 // counts and the fired-clause bitmap) lives in the fixed array below, which
 // every GPU that loads this library holds until the process exits.
 //
@@ -813,7 +815,10 @@ ytm_status ytm_train_selection(const ytm_config *cfg, int32_t B, const void *wor
 // that name is only a host-side stand-in for the symbol.  The device address is
 // looked up once per device with cudaGetSymbolAddress, with that device
 // current, the first time the entry point runs on it; that first call should
-// therefore come before any stream capture.
+// therefore come before any stream capture.  The address is cached for the
+// life of the process: after cudaDeviceReset (which unloads this module from
+// the device) the cache is stale, so a process that resets a device must not
+// call ytm_infer_noalloc on it afterwards.
 //
 // All calls share the array and it keeps the previous call's contents; the
 // bitmap is cleared on every call.  Calls that overlap on the GPU (different

@@ -168,12 +168,15 @@ ytm_status ytm_peer_allreduce_i32(void *ctx, int32_t *data, int64_t n, int64_t l
     return launch_check("peer all-reduce");
 }
 
-// 0 if every call so far completed; else (peer index + 1) of a peer that
-// never signalled.  Synchronises the device.
+// 0 if every call since the last read completed; else (peer index + 1) of
+// a peer that never signalled.  Synchronises the device and clears the
+// status word (the kernel only raises it, with atomicMax).
 ytm_status ytm_peer_ar_status(void *ctx, int32_t *status_out) {
     PeerAr *a = (PeerAr *)ctx;
     if (!a || !status_out) return fail(YTM_ERR_ARG, "bad argument");
-    return cuda_check(cudaMemcpy(status_out, a->status, 4, cudaMemcpyDeviceToHost), "status copy");
+    ytm_status rc = cuda_check(cudaMemcpy(status_out, a->status, 4, cudaMemcpyDeviceToHost), "status copy");
+    if (rc == YTM_OK && *status_out != 0) rc = cuda_check(cudaMemset(a->status, 0, 4), "status clear");
+    return rc;
 }
 
 ytm_status ytm_peer_ar_destroy(void *ctx) {

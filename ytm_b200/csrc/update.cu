@@ -460,7 +460,7 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
                                      row_off, alist);
     if ((rc = launch_check("update thresholds"))) return rc;
     const int nk = cfg->coalesced ? cfg->n_classes : 1;
-    // the largest chunk (multiple of 32, at most 256 and the batch) whose
+    // the largest chunk (multiple of 32, at most UPD_BC_MAX and the batch) whose
     // event list fits 32 KB of shared memory (keeps several CTAs per SM)
     int BC = std::min(UPD_BC_MAX, ((B + 31) / 32) * 32);
     while (BC > 32 && update_smem(nk, BC) > 32 * 1024) BC -= 32;

@@ -215,6 +215,11 @@ class BaseTM:
         if len(set(hosts)) != 1 or self.world > 8:
             return None
         lib = _lib.load()
+        if ctx is not None:  # regrow: every rank is done with the old buffers once all are here
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self._pg)
+            _lib.check(lib.ytm_peer_ar_destroy(ctx), "ytm_peer_ar_destroy")
+            self._par = None
         n = max(n, 1 << 16)
         ctx = ct.c_void_p()
         h = (ct.c_uint8 * 64)()
@@ -228,6 +233,36 @@ class BaseTM:
         dist.barrier(group=self._pg)
         self._par, self._par_n = ctx, n
         return ctx
+
+    def _check_peer_status(self, ctx) -> None:
+        """Raise if a peer all-reduce since the last check gave up waiting for
+        a rank (its slices were then left partly summed, so the ranks' models
+        have diverged).  Synchronises the device once."""
+        import ctypes as ct
+        st = ct.c_int32(0)
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.load().ytm_peer_ar_status(ctx, ct.byref(st)), "ytm_peer_ar_status")
+        if st.value:
+            raise _lib.YTMError(f"peer all-reduce: rank {st.value - 1} did not arrive in time; "
+                                "the clause shards are no longer consistent")
+
+    def close(self) -> None:
+        """Release the multi-GPU resources (peer all-reduce buffers and their
+        IPC mappings, the NCCL communicator).  Call on every rank, before
+        destroy_process_group; the model stays usable on one process."""
+        lib = _lib.load() if (getattr(self, "_par", None) is not None or getattr(self, "_comm", None) is not None) \
+            else None
+        if lib is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self._pg)
+        if getattr(self, "_par", None) is not None:
+            _lib.check(lib.ytm_peer_ar_destroy(self._par), "ytm_peer_ar_destroy")
+            self._par = None
+        if getattr(self, "_comm", None) is not None:
+            _lib.check(lib.ytm_nccl_comm_destroy(self._comm), "ytm_nccl_comm_destroy")
+            self._comm = None
 
     def _allreduce(self, t: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
@@ -342,6 +377,8 @@ class BaseTM:
             self.last_class_sums = self.engine.train_fit_batches(lits, Y, batch_size, t, drop, self.rank == 0,
                                                                  None if par is not None else self._nccl(), par)
             self.sample_counter = t + N
+            if par is not None:
+                self._check_peer_status(par)
             return
         for i in range(0, N, batch_size):
             B = min(batch_size, N - i)
