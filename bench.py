@@ -1,15 +1,37 @@
 """Benchmark: Tsetlin Machine training (and inference) samples/s on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c5] [--impl ours|reference]
 
-Default workload: configuration 2 (coalesced TM, 10k shared clauses, 784
-features, 10 classes, T=1000, s=15, mini-batch 256) on seeded synthetic
-prototype data.  A step is one mini-batch: clause evaluation of the batch,
-class sums (all-reduced over ranks when N > 1: clauses are sharded), and the
-Type I/II feedback.  N > 1 runs under torchrun, one rank per GPU, NCCL.
+Default workload: configuration 5 (65,536 shared clauses, 16,384 boolean
+features, 100 classes, 4096 TA states = 13 bit planes, T=20000, s=20,
+mini-batch 1024) on seeded synthetic planted-rule data; it is the largest
+configuration and the one the multi-GPU scaling is quoted on.  A step is one
+mini-batch: clause evaluation of the batch, class sums (summed over ranks when
+N > 1: clauses are sharded), and the Type I/II feedback.  The timed steps are
+the batches W..W+K-1 of a fresh model (the early-training regime, where every
+(sample, class) pair is still active).  N > 1 runs under torchrun, one rank
+per GPU, NCCL.
+
+The JSON line also carries:
+  e2e        the same K batches through MultiClassTM.fit from the same model
+             state, pinned host inputs copied in every step, class sums read back;
+  roofline   the feedback kernel (the dominant one) against the measured INT
+             ceiling, from device counters of its work (ytm_train_update_counted);
+  infer      inference samples/s on the trained model (configuration 5:
+             2^20 samples, chunked as the reference's _score_batch does);
+  target_c1  configuration 1 (20,000 clauses, batch 1) on one GPU, device and
+             e2e, with the reference's own CPU path (pytm, baseline/_ref)
+             timed on this host beside it;
+  cpu_baseline  the CPU restatement (oracle/, OpenMP) on a bounded sample of
+             the default workload.
 
 --impl reference times the CPU restatement of the reference algorithm
-(oracle/, OpenMP over all host cores) on the same workload, rank 0 only.
+(oracle/, OpenMP over all host cores) on the same workload, rank 0 only: the
+reference has no CPU implementation of the cutm algorithm (its pytm package
+covers configuration 1 only and is timed inside target_c1).
+
+--profile all|converged|case  launch a chosen set of kernels inside a
+cudaProfilerStart/Stop range for ncu (no JSON line); see profile_run().
 """
 from __future__ import annotations
 
@@ -29,11 +51,11 @@ sys.path.insert(0, ROOT)
 
 METRIC = "train & infer samples/s (1/2/4/8 B200) + % of HBM/INT-pipe roofline vs CPU"
 L2_BYTES = 126 * 1024 * 1024
-# DRAM bytes (read + write) per launch of the dominant kernel in the regime
-# bench.py times it in (a converged model), from one ncu capture of
-# `python -m ytm_b200.profile_kernels --converged 100`; None where no capture
-# was made.
-TRAFFIC = {"c2": 11.8976e6}
+# DRAM bytes (read + write) of one feedback launch in the regime bench.py
+# times it in, from one ncu capture of a reduced-clause model of the same
+# workload, scaled by clauses (the feedback's traffic is per clause); None
+# where no capture was made.
+TRAFFIC_PER_CLAUSE = {}
 
 
 def load_peaks():
@@ -134,32 +156,48 @@ def count_launches(fn):
     return sum(1 for e in prof.events() if e.device_type == DeviceType.CUDA and pat.search(e.name))
 
 
-def lop3_peak(dev):
-    """Measured LOP3 throughput (ops/s) of this GPU: the ceiling of the
-    word-test (one LOP3 each) clause evaluation."""
+def _probe_lib():
     import ctypes as ct
+    from ytm_b200 import build
+    path = build.build_probe()
+    lib = ct.CDLL(path)
+    for name in ("bench_probe_lop3", "bench_probe_philox7"):
+        f = getattr(lib, name)
+        f.argtypes = [ct.c_int32, ct.c_int32, ct.c_void_p, ct.POINTER(ct.c_uint64), ct.c_void_p]
+        f.restype = ct.c_int
+    return lib
+
+
+def probe_peak(dev, name):
+    """Measured throughput (operations/s) of this GPU for one probe of
+    bench_probe.cu: LOP3 operations (the word-test instruction) or
+    Philox4x32-7 calls (the literal-mask draw); best of three long runs."""
+    import ctypes as ct
+
     import torch
-    from ytm_b200 import _lib
-    lib = _lib.load()
+    lib = _probe_lib()
+    fn = getattr(lib, name)
     out = torch.zeros(1, dtype=torch.int32, device=dev)
     ops = ct.c_uint64(0)
     stream = ct.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
     blocks = torch.cuda.get_device_properties(dev).multi_processor_count * 8
     best = 0.0
-    for it in (64, 4096, 4096, 4096):
+    long_iters = 4096 if name == "bench_probe_lop3" else 256
+    for it in (16, long_iters, long_iters, long_iters):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        _lib.check(lib.ytm_probe_lop3(blocks, it, ct.c_void_p(out.data_ptr()), ct.byref(ops), stream))
+        rc = fn(blocks, it, ct.c_void_p(out.data_ptr()), ct.byref(ops), stream)
         b.record()
         torch.cuda.synchronize(dev)
+        if rc != 0:
+            raise RuntimeError(f"{name} failed: CUDA error {rc}")
         best = max(best, ops.value / (a.elapsed_time(b) / 1000.0))
     return best
 
 
 def workload(name, n):
     from ytm_b200 import synthetic
-    X, y = synthetic.make(name, n)
-    return X, y
+    return synthetic.make(name, n)
 
 
 def oracle_kw(kw):
@@ -167,6 +205,21 @@ def oracle_kw(kw):
     kw = dict(kw)
     pytm = kw.pop("rules", "cutm") == "pytm"
     return dict(kw, one_negative=pytm, count_empty=pytm)
+
+
+def _cfgjson(kw):
+    return {k: (list(v) if isinstance(v, tuple) else v) for k, v in kw.items()}
+
+
+def config_of(name, world):
+    """The `config` object of both arms' JSON lines (identical for a workload)."""
+    from ytm_b200 import synthetic
+    kw = synthetic.MODELS[name]
+    B = synthetic.BATCH[name]
+    S = B if B > 1 else 256
+    return {"workload": name, "global_batch": B, "samples_per_step": S, "parallelism": f"clause-shard{world}",
+            "l2": "flushed between timed steps (2x L2 write)",
+            "regime": "batches W..W+K-1 of a fresh model (early training)", **_cfgjson(kw)}
 
 
 def cpu_sample(name, kw, B, budget_s=20.0, threads=None):
@@ -204,6 +257,55 @@ def cpu_sample(name, kw, B, budget_s=20.0, threads=None):
     return rate, done, el, O.get_threads(), note
 
 
+def pytm_baseline(budget_s=8.0):
+    """The reference's own CPU path: pytm.base.BaseTM.fit (src/pytm/base.py,
+    installed unmodified in baseline/_ref) on configuration-1 data, at
+    n_clause 2000 and 20000, each on a bounded number of samples.  pytm is a
+    numpy loop over samples (bool matmuls, no BLAS): one core."""
+    import contextlib
+    import io
+    refdir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(refdir, "pytm")):
+        return {"unavailable": "baseline/_ref has no pytm (run oracle/install_reference.py)"}
+    sys.path.insert(0, refdir)
+    try:
+        from pytm.base import BaseTM
+    finally:
+        sys.path.remove(refdir)
+    X, y = workload("c1", 1200)
+    Xb = X.astype(bool)
+    yi = y.astype(np.int64)
+    out = {"kind": "reference", "source": "pytm.base.BaseTM.fit (src/pytm/base.py:145-156), baseline/_ref",
+           "cores": 1, "cpu": _cpu_model(), "numpy": np.__version__, "host_threads": os.cpu_count()}
+    for n_clause in (2000, 20000):
+        tm = BaseTM(n_clause=n_clause, T=50, s=10.0, q=1.0, n_class=10, dim=(28, 28, 1), seed=1)
+        done, el, i = 0, 0.0, 0
+        with contextlib.redirect_stderr(io.StringIO()):  # pytm's tqdm bar
+            tm.fit(Xb[:2], yi[:2])  # warm-up
+            t0 = time.perf_counter()
+            while el < budget_s and done < 1000:
+                n = 50 if n_clause == 2000 else 5
+                tm.fit(Xb[i:i + n], yi[i:i + n])
+                done += n
+                i = (i + n) % 1000
+                el = time.perf_counter() - t0
+        out[f"n_clause_{n_clause}"] = {"value": done / el, "unit": "samples/s", "samples": done,
+                                       "seconds": round(el, 2)}
+    out["best"] = max(out["n_clause_2000"]["value"], out["n_clause_20000"]["value"])
+    return out
+
+
+def _cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
 def run_reference(args):
     """Reference arm: the CPU restatement of the reference algorithm (oracle/,
     OpenMP over all host threads) on the same workload, rank 0 only.  A step
@@ -213,8 +315,8 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from ytm_b200 import synthetic
     from oracle import oracle as O
+    from ytm_b200 import synthetic
     kw = synthetic.MODELS[args.workload]
     B = synthetic.BATCH[args.workload]
     O.build()
@@ -250,7 +352,7 @@ def run_reference(args):
     out = {"metric": METRIC, "impl": "reference", "value": v, "unit": "samples/s", "n_gpus": args.gpus,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * el / args.steps,
            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u32",
-           "data": "synthetic", "config": {"workload": args.workload, "global_batch": B, **_cfgjson(kw)},
+           "data": "synthetic", "config": config_of(args.workload, args.gpus),
            "cpu_baseline": {"value": v, "unit": "samples/s", "cores": O.get_threads(), "kind": "port",
                             "sample": f"{args.steps} steps of {S} samples (batch {b}) of {args.workload}{note}; "
                                       "oracle/ytm_oracle.c (CPU restatement of kernel.cu), OpenMP"},
@@ -258,24 +360,158 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
-def _cfgjson(kw):
-    return {k: (list(v) if isinstance(v, tuple) else v) for k, v in kw.items()}
+# ------------------------------------------------------------------ helpers of our arm
+
+class Snapshot:
+    """Device copy of a model's trainable state and sample counter, so that
+    several measurements start from the same state."""
+
+    def __init__(self, tm):
+        e = tm.engine
+        self.tm = tm
+        self.t = tm.sample_counter
+        self.bufs = [(x, x.clone()) for x in (e.state, e.weights, e.patch_w, e.bias)]
+
+    def restore(self):
+        for dst, src in self.bufs:
+            dst.copy_(src)
+        self.tm.sample_counter = self.t
+        self.tm._model_version += 1
+
+
+def max_over_ranks(v, world, dev):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def device_lits(name, tm, n, dev, seed=777):
+    """The engine input of n synthetic samples (literals [n, 1, W], or packed
+    bit images for convolutional models), generated and encoded in chunks
+    (configuration 5's 2^20 samples would be 64 GB as host u32)."""
+    import torch
+    from ytm_b200 import synthetic
+    shape = (n, tm.engine.cfg.image_words) if tm.number_of_patches > 1 else \
+        (n, tm.number_of_patches, tm.number_of_literal_chunks)
+    out = torch.empty(shape, dtype=torch.int32, device=dev)
+    chunk = 32768
+    for i in range(0, n, chunk):
+        m = min(chunk, n - i)
+        if name == "c5":
+            X = synthetic.rules_torch(m, seed + i, dev)
+        else:
+            X = torch.from_numpy(synthetic.make(name, m, seed=seed + i)[0].view(np.int32)).to(dev)
+        out[i:i + m] = tm._input_device(X)
+        del X
+    return out
+
+
+def run_target_c1(args, dev, flush, clk_rows=None):
+    """Configuration 1 (vanilla, 2000 clauses per class x 10, 784 features,
+    batch 1) on this GPU: a step is 256 samples through the fused batch-1
+    path (the one MultiClassTM.fit takes), device-timed from a fixed
+    warmed-up state; e2e the same samples through MultiClassTM.fit with pinned
+    host inputs and the class sums read back per step; beside it the
+    reference's pytm on this host."""
+    import torch
+    from ytm_b200 import synthetic
+    from ytm_b200.cutm import MultiClassTM
+    kw = synthetic.MODELS["c1"]
+    S, K, W = 256, max(args.steps, 10), 3
+    X, y = workload("c1", S * (K + W))
+    tm = MultiClassTM(seed=42, device=dev, **kw)
+    eng = tm.engine
+    lits = tm._encode_device(X)
+    Yd = torch.from_numpy(tm.encode_Y(y)).to(dev)
+    for i in range(W):
+        eng.train_fit_b1(lits[i * S:(i + 1) * S], Yd[i * S:(i + 1) * S], tm.sample_counter, None)
+        tm.sample_counter += S
+    torch.cuda.synchronize()
+    snap = Snapshot(tm)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    for j in range(K):
+        i = W + j
+        flush.zero_()
+        ev[j][0].record()
+        eng.train_fit_b1(lits[i * S:(i + 1) * S], Yd[i * S:(i + 1) * S], tm.sample_counter, None)
+        ev[j][1].record()
+        tm.sample_counter += S
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in ev)
+    value = K * S / (ms / 1000.0)
+    launches = count_launches(lambda: eng.train_fit_b1(lits[:S], Yd[:S], 0, None))
+    # e2e from the same state
+    snap.restore()
+    Xh = torch.from_numpy(X.view(np.int32)).pin_memory()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for j in range(K):
+        i = W + j
+        tm.fit(Xh[i * S:(i + 1) * S], y[i * S:(i + 1) * S], batch_size=1)
+        tm.last_class_sums.cpu()
+    b.record()
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b)
+    out = {"workload": "c1", "config": {"global_batch": 1, "samples_per_step": S, **_cfgjson(kw)},
+           "value": value, "unit": "samples/s", "steps": K, "warmup_steps": W,
+           "us_per_sample": 1e6 / value, "gpu_launches_per_step": launches,
+           "e2e": {"value": K * S / (e2e_ms / 1000.0), "unit": "samples/s",
+                   "h2d_bytes_per_step": int(S * 784 * 4 + S * kw["n_classes"] * 4),
+                   "d2h_bytes_per_step": int(kw["n_classes"] * 4)}}
+    if not args.no_cpu:
+        pb = pytm_baseline()
+        out["cpu_baseline"] = pb
+        if "best" in pb:
+            out["vs_pytm_best"] = out["e2e"]["value"] / pb["best"]
+            out["vs_pytm_20000"] = out["e2e"]["value"] / pb["n_clause_20000"]["value"]
+            out["target"] = ">= 50x the best pytm training samples/s (e2e)"
+    del tm, eng, lits
+    return out
+
+
+def counted_feedback(tm, lits, Yd, B, base, nb, dev):
+    """Run nb batches of the per-call path from the current state with the
+    feedback's device counters on; returns the summed counters and the batch
+    count."""
+    import torch
+    eng = tm.engine
+    ctr = torch.zeros(4, dtype=torch.int64, device=dev)
+    for r in range(nb):
+        j = (base + r) * B
+        t = tm.sample_counter
+        cs = eng.train_eval(lits[j:j + B], t, None, add_bias=tm.rank == 0)
+        cs = tm._allreduce(cs)
+        eng.train_update(cs, Yd[j:j + B], lits[j:j + B], t, None, counters=ctr)
+        tm.sample_counter += B
+    torch.cuda.synchronize()
+    return [int(v) for v in ctr.cpu().tolist()]
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "p1"])
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5", "p1"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline legs")
+    ap.add_argument("--no-target", action="store_true", help="skip the configuration-1 target object")
     ap.add_argument("--infer-samples", type=int, default=None)
+    ap.add_argument("--profile", choices=["all", "converged", "case"], default=None)
+    ap.add_argument("--profile-batches", type=int, default=2)
+    ap.add_argument("--profile-clauses", type=int, default=None)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile:
+        return profile_run(args)
 
     import torch
     import torch.distributed as dist
@@ -299,7 +535,7 @@ def main():
     X, y = workload(name, n_train)
     tm = MultiClassTM(seed=42, device=dev, **kw)
     eng = tm.engine
-    lits = tm._encode_device(X)
+    lits = tm._input_device(X)  # what MultiClassTM.fit feeds the engine (conv models: packed bit images)
     Yd = torch.from_numpy(tm.encode_Y(y)).to(dev)
     flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
 
@@ -310,90 +546,131 @@ def main():
 
     fused = B == 1 and world == 1 and tm._fused_b1_ok()
 
-    def step(i, ev=None):
+    def step(i):
         if fused:  # the path MultiClassTM.fit takes at batch 1: one fused launch per sample
-            if ev:
-                ev[0].record()
             eng.train_fit_b1(lits[i * S:(i + 1) * S], Yd[i * S:(i + 1) * S], tm.sample_counter, None)
-            if ev:
-                ev[1].record()
-            tm.sample_counter += S
-            return
-        if hasattr(eng, "train_fit_batches") and not ev:  # the path MultiClassTM.fit takes at batch > 1
+        else:  # the path MultiClassTM.fit takes at batch > 1: the C batch loop
             par = tm._peer_ar(B * kw["n_classes"])
             eng.train_fit_batches(lits[i * S:(i + 1) * S], Yd[i * S:(i + 1) * S], B, tm.sample_counter, None,
                                   rank == 0, None if par is not None else tm._nccl(), par)
-            tm.sample_counter += S
-            return
-        for j in range(i * S, (i + 1) * S, B):
-            lb, yb = lits[j:j + B], Yd[j:j + B]
-            t = tm.sample_counter
-            cs = eng.train_eval(lb, t, None, add_bias=rank == 0)
-            cs = tm._allreduce(cs)
-            if ev and j == i * S:
-                ev[0].record()
-            eng.train_update(cs, yb, lb, t, None)
-            if ev and j == i * S:
-                ev[1].record()
-            tm.sample_counter += B
+        tm.sample_counter += S
 
     for i in range(args.warmup):
         step(i)
     barrier()
+    snap = Snapshot(tm)
+    barrier()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    upd = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     with ClockSampler(dev) as clk:
         barrier()
         for j in range(args.steps):
             flush.zero_()  # L2 flush between timed steps (outside the step events)
             starts[j].record()
-            step(args.warmup + j, upd[j] if fused else None)
+            step(args.warmup + j)
             ends[j].record()
         barrier()
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    if fused:
-        upd_ms = [a.elapsed_time(b) for a, b in upd]
-    else:
-        # the dominant kernel's duration: three more batches through the
-        # per-call path with events around the feedback only (after the timed
-        # region, so the timed steps stay on the C loop)
-        upd = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(3)]
-        base = (args.warmup + args.steps) % max(1, n_train // S - 3)
-        for r in range(3):
-            step(base + r, upd[r])
-        barrier()
-        upd_ms = [a.elapsed_time(b) for a, b in upd]
-    total_ms = sum(step_ms)
-    if world > 1:
-        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
+    if getattr(tm, "_par", None) is not None:
+        tm._check_peer_status(tm._par)
+    total_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(starts, ends)), world, dev)
     value = args.steps * S / (total_ms / 1000.0)
+    launches = None
 
-    # roofline of the dominant kernel (feedback): the state's read-modify-write
+    # the dominant kernel (feedback) in the same regime: the first timed
+    # batches again from the snapshot, through the per-call path with events
+    # around the feedback, then once more with its device counters on
     cfg = eng.cfg
-    if fused:  # per sample: every clause's planes read + written once, literals read once
-        alg_bytes = S * (cfg.clause_count * cfg.planes * cfg.words * 4 * 2 + cfg.words * 4 * cfg.patches)
-        kernel = "k_fused_b1 (feedback of sample i + evaluation of sample i+1), per 256 launches"
+    nb = 3 if not fused else 1
+    if fused:
+        upd_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)][:3]
+        ctrs = None
     else:
-        # one read and one write of every clause's bit planes per launch (the
-        # kernel streams them once per chunk of samples; the roofline counts
-        # the minimum), plus the batch's literals
-        alg_bytes = cfg.clause_count * cfg.planes * cfg.words * 4 * 2 + B * cfg.words * 4 * cfg.patches
-        kernel = "k_update (feedback)"
-    # this library's kernels in one step, counted from the CUDA activity trace
-    launches = count_launches(lambda: step((args.warmup + args.steps) % max(1, n_train // S)))
+        snap.restore()
+        barrier()
+        upd_ms = []
+        for r in range(nb):
+            j = (args.warmup + r) * B
+            t = tm.sample_counter
+            cs = eng.train_eval(lits[j:j + B], t, None, add_bias=rank == 0)
+            cs = tm._allreduce(cs)
+            flush.zero_()
+            a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            eng.train_update(cs, Yd[j:j + B], lits[j:j + B], t, None)
+            b_.record()
+            tm.sample_counter += B
+            barrier()
+            upd_ms.append(a.elapsed_time(b_))
+        snap.restore()
+        barrier()
+        ctrs = counted_feedback(tm, lits, Yd, B, args.warmup, nb, dev)
+    snap.restore()
+    barrier()
+    launches = count_launches(lambda: step(args.warmup))
+    snap.restore()
+    barrier()
     upd_s = statistics.mean(upd_ms) / 1000.0
-    peak, peak_kind = load_peaks()
-    achieved = alg_bytes / upd_s / 1e9
+
+    lop3 = probe_peak(dev, "bench_probe_lop3")
+    philox = probe_peak(dev, "bench_probe_philox7")
+    hbm_peak, peak_kind = load_peaks()
+    NB, W = cfg.planes, cfg.words
+    if ctrs is not None:
+        units, calls, words, events = (v / nb for v in ctrs)
+        # INT work of one feedback launch in LOP3-equivalent operations:
+        # 4 * planes logic ops per (event, literal word) (a ripple add or
+        # borrow over the planes plus the comparator that selects its
+        # literals) and each literal-mask Philox4x32-7 call weighted by the
+        # measured LOP3 : Philox throughput ratio
+        ops = units * 4 * NB + calls * (lop3 / philox)
+        t_min = units * 4 * NB / lop3 + calls / philox
+        state_bytes = words * NB * 4 * 2
+        roofline = {"bound": "int", "achieved": ops / upd_s / 1e9, "peak": lop3 / 1e9, "unit": "G int-ops/s",
+                    "frac": ops / upd_s / lop3, "traffic": None, "kernel": "k_update (feedback)",
+                    "peak_kind": "measured on this GPU (bench_probe.cu LOP3 probe)",
+                    "launch_ms": upd_s * 1000.0, "launches_averaged": nb,
+                    "counters_per_launch": {"event_word_pairs": units, "philox7_calls": calls,
+                                            "state_words_streamed": words, "events": events},
+                    "philox7_peak_calls_per_s": philox, "lop3_peak_per_s": lop3,
+                    "op_model": "4*planes LOP3 per (event, word) + Philox7 calls x (LOP3 peak / Philox peak)",
+                    "t_min_ms": t_min * 1000.0,
+                    "hbm": {"algorithmic_bytes": state_bytes + B * W * 4 * cfg.patches,
+                            "achieved_gbs": (state_bytes + B * W * 4 * cfg.patches) / upd_s / 1e9,
+                            "peak_gbs": hbm_peak, "frac": (state_bytes + B * W * 4 * cfg.patches) / upd_s / 1e9
+                            / hbm_peak, "peak_kind": peak_kind}}
+        tpc = TRAFFIC_PER_CLAUSE.get(name)
+        if tpc is not None and world == 1:
+            roofline["traffic"] = tpc * cfg.clause_count
+    else:
+        alg_bytes = S * (cfg.clause_count * NB * W * 4 * 2 + W * 4 * cfg.patches)
+        roofline = {"bound": "hbm", "achieved": alg_bytes / upd_s / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                    "frac": alg_bytes / upd_s / 1e9 / hbm_peak, "traffic": None,
+                    "kernel": "k_fused_b1 (feedback of sample i + evaluation of sample i+1), per 256 launches",
+                    "peak_kind": peak_kind, "launch_ms": upd_s * 1000.0}
+
+    # end to end through the public API from the same state: pinned host
+    # inputs copied in every step, class sums of the step's last batch read back
+    Xh = torch.from_numpy(X.view(np.int32)).pin_memory()
+    barrier()
+    a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for j in range(args.steps):
+        i = args.warmup + j
+        tm.fit(Xh[i * S:(i + 1) * S], y[i * S:(i + 1) * S], batch_size=B)
+        tm.last_class_sums.cpu()
+    b_.record()
+    barrier()
+    e2e_ms = max_over_ranks(a.elapsed_time(b_), world, dev)
+    e2e = {"value": args.steps * S / (e2e_ms / 1000.0), "unit": "samples/s",
+           "h2d_bytes_per_step": int(S * X.shape[1] * 4 + S * kw["n_classes"] * 4),
+           "d2h_bytes_per_step": int(min(B, S) * kw["n_classes"] * 4)}
+    del Xh
 
     # inference samples/s on the trained state
-    ni = args.infer_samples or (65536 if name in ("c1", "c2") else 4096)
-    Xi, _ = workload(name, ni)
-    lits_i = tm._encode_device(Xi)
-    for _ in range(2):
-        tm._score_device(lits_i)
+    ni = args.infer_samples or (1 << 20 if name == "c5" else (65536 if name in ("c1", "c2") else 4096))
+    del lits
+    lits_i = device_lits(name, tm, ni, dev)
+    tm._score_device(lits_i[:min(ni, 4096)])
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     flush.zero_()
@@ -401,58 +678,27 @@ def main():
     tm._score_device(lits_i)
     e1.record()
     barrier()
-    infer_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([infer_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        infer_ms = float(t.item())
+    infer_ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
     infer_value = ni / (infer_ms / 1000.0)
-    word_tests = ni * cfg.clauses * cfg.patches * cfg.words
-    # conv models whose patch tile fits shared memory take the sparse match
-    # (compacted include words): the dense word-test rate is then only a
-    # dense-equivalent figure, not a fraction of the INT pipe
+    word_tests = ni * cfg.clauses * cfg.patches * cfg.words  # all clauses (every rank scores its sample slice)
     sparse = cfg.patches > 1 and cfg.words * 129 * 4 <= 220 * 1024
+    del lits_i
 
-    lop3 = lop3_peak(dev)
-
-    # end to end through the public API: pinned host inputs, H2D, encode, train,
-    # D2H of the batch's class sums
-    Xh = torch.from_numpy(X.view(np.int32)).pin_memory()
-    yh = y
-    for i in range(2):
-        tm.fit(Xh[i * S:(i + 1) * S], yh[i * S:(i + 1) * S], batch_size=B)
-    barrier()
-    a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for j in range(args.steps):
-        i = (args.warmup + j) % (n_train // S)
-        tm.fit(Xh[i * S:(i + 1) * S], yh[i * S:(i + 1) * S], batch_size=B)
-        tm.last_class_sums.cpu()
-    b_.record()
-    barrier()
-    e2e_ms = a.elapsed_time(b_)
-    if world > 1:
-        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e = {"value": args.steps * S / (e2e_ms / 1000.0), "unit": "samples/s",
-           "h2d_bytes_per_step": int(S * X.shape[1] * 4 + S * kw["n_classes"] * 4),
-           "d2h_bytes_per_step": int(B * kw["n_classes"] * 4)}
+    target = None
+    if rank == 0 and world == 1 and not args.no_target and name != "c1":
+        target = run_target_c1(args, dev, flush)
 
     if rank == 0:
         out = {
             "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "u32", "data": "synthetic",
-            "config": {"workload": name, "global_batch": B, "samples_per_step": S, "parallelism": f"clause-shard{world}",
-                       "l2": "flushed between timed steps (2x L2 write)", **_cfgjson(kw)},
+            "config": config_of(name, world),
             "e2e": e2e,
             "gpu_launches": launches * args.steps,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": TRAFFIC.get(name) if world == 1 else None, "kernel": kernel,
-                         "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg_bytes,
-                         "launch_ms": statistics.mean(upd_ms)},
+            "roofline": roofline,
             "infer": {"value": infer_value, "unit": "samples/s", "samples": ni,
+                      "chunking": "MultiClassTM._score_device chunks of at most 2^31 bytes of literals + fired bits",
                       "dense_word_tests_per_s": word_tests / (infer_ms / 1000.0),
                       "lop3_peak_per_s": lop3,
                       "int_pipe_frac": None if sparse else word_tests / (infer_ms / 1000.0) / lop3,
@@ -460,6 +706,8 @@ def main():
                                  else "k_match<0> (one LOP3 per word test)")},
             "clocks": clk.summary(),
         }
+        if target is not None:
+            out["target_c1"] = target
         if not args.no_cpu:
             v, done, el, thr, note = cpu_sample(name, kw, B)
             out["cpu_baseline"] = {"value": v, "unit": "samples/s", "cores": thr, "kind": "port",
@@ -467,8 +715,117 @@ def main():
                                              "OpenMP"}
         print(json.dumps(out), flush=True)
     if world > 1:
+        tm.close()
         dist.barrier()
         dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ profiling ranges
+
+def profile_run(args):
+    """Launch kernels inside one cudaProfilerStart/Stop range, for
+    `ncu --profile-from-start off` (no JSON line; prints "done").
+
+    all        warm-up outside the range (configuration-2 batches, batch-1
+               training of configurations 1 and 3, a thermometer encode); in
+               the range one configuration-2 training batch and 65,536-sample
+               inference, a transform, an encode, two fused batch-1 samples of
+               configurations 1 and 3, a patch-wise transform and a
+               thermometer encode.
+    converged  configuration 2 trained --profile-batches batches outside the
+               range, then one batch (evaluation, thresholds, feedback) in it.
+    case       --workload with --profile-clauses clauses per class (default:
+               the full model), --profile-batches warm-up batches outside the
+               range, then one training batch (batch-1 workloads: 2 samples
+               of the fused path) and inference of one batch in it."""
+    import torch
+
+    from ytm_b200 import synthetic
+    from ytm_b200.cutm import MultiClassTM
+    torch.cuda.set_device(0)
+    if args.profile == "converged":
+        nb = args.profile_batches
+        X, y = synthetic.make("c2", 256 * (nb + 1))
+        tm = MultiClassTM(seed=42, **synthetic.MODELS["c2"])
+        lits, Y, e = tm._encode_device(X), torch.from_numpy(tm.encode_Y(y)).cuda(), tm.engine
+        for i in range(nb + 1):
+            if i == nb:
+                torch.cuda.synchronize()
+                torch.cuda.profiler.start()
+            sl = slice(i * 256, (i + 1) * 256)
+            cs = e.train_eval(lits[sl], i * 256, None, True)
+            e.train_update(cs, Y[sl], lits[sl], i * 256, None)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print("done", flush=True)
+        return
+    if args.profile == "case":
+        name = args.workload
+        kw = dict(synthetic.MODELS[name])
+        if args.profile_clauses:
+            kw["number_of_clauses_per_class"] = args.profile_clauses
+        B = synthetic.BATCH[name]
+        nb = args.profile_batches
+        n = (B if B > 1 else 2) * (nb + 1)
+        X, y = synthetic.make(name, n)
+        tm = MultiClassTM(seed=42, **kw)
+        lits, Y, e = tm._input_device(X), torch.from_numpy(tm.encode_Y(y)).cuda(), tm.engine
+        step = B if B > 1 else 2
+        for i in range(nb + 1):
+            sl = slice(i * step, (i + 1) * step)
+            if i == nb:
+                torch.cuda.synchronize()
+                torch.cuda.profiler.start()
+            if B == 1 and tm._fused_b1_ok():
+                e.train_fit_b1(lits[sl], Y[sl], i * step, None)
+            else:
+                for j in range(sl.start, sl.stop, B):
+                    cs = e.train_eval(lits[j:j + B], j, None, True)
+                    e.train_update(cs, Y[j:j + B], lits[j:j + B], j, None)
+        e.infer(lits[-step:])
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print("done", flush=True)
+        return
+    X, y = synthetic.make("c2", 256 * 5)
+    tm = MultiClassTM(seed=42, **synthetic.MODELS["c2"])
+    lits, Y, e = tm._encode_device(X), torch.from_numpy(tm.encode_Y(y)).cuda(), tm.engine
+    for i in range(4):
+        sl = slice(i * 256, (i + 1) * 256)
+        cs = e.train_eval(lits[sl], i * 256, None, True)
+        e.train_update(cs, Y[sl], lits[sl], i * 256, None)
+    Xi, _ = synthetic.make("c2", 65536)
+    Xi_d = torch.from_numpy(Xi.view(np.int32)).cuda()
+    li = tm._encode_device(Xi)
+    X1, y1 = synthetic.make("c1", 600)
+    t1 = MultiClassTM(seed=1, **synthetic.MODELS["c1"])
+    l1, Y1 = t1._encode_device(X1), torch.from_numpy(t1.encode_Y(y1)).cuda()
+    t1.engine.train_fit_b1(l1[:500], Y1[:500], 0, None)
+    X3, y3 = synthetic.make("c3", 300)
+    t3 = MultiClassTM(seed=1, **synthetic.MODELS["c3"])
+    l3, Y3 = t3._input_device(X3), torch.from_numpy(t3.encode_Y(y3)).cuda()
+    t3.engine.train_fit_b1(l3[:200], Y3[:200], 0, None)
+    kw4 = dict(synthetic.MODELS["c4"])
+    kw4["number_of_clauses_per_class"] = 64
+    t4 = MultiClassTM(seed=1, **kw4)
+    img = torch.randint(0, 256, (2048, 32 * 32 * 3), dtype=torch.uint8, device="cuda")
+    t4.encode_thermometer(img, 8, on_device=True)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    i = 4
+    sl = slice(i * 256, (i + 1) * 256)
+    cs = e.train_eval(lits[sl], i * 256, None, True)
+    e.train_update(cs, Y[sl], lits[sl], i * 256, None)
+    e.infer(li)
+    e.transform(li[:4096])
+    e.encode(Xi_d)
+    t1.engine.train_fit_b1(l1[500:502], Y1[500:502], 500, None)
+    t3.engine.train_fit_b1(l3[200:202], Y3[200:202], 200, None)
+    t3.engine.transform_patchwise(l3[:16])
+    t4.encode_thermometer(img, 8, on_device=True)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    print("done", flush=True)
 
 
 if __name__ == "__main__":

@@ -76,8 +76,10 @@ typedef struct ytm_config {
     int32_t planes;            /* bits per counter                              */
     int32_t state_offset;      /* stored value = state + state_offset           */
     int32_t state_top;         /* largest representable state                  */
-    /* decision thresholds (fractions of 2^32 or 2^12) */
-    uint32_t s_threshold12;    /* literal mask Bernoulli(1/s) = thr / 4096      */
+    /* decision thresholds (fractions of 2^32) */
+    uint32_t s_count_cdf[32];  /* literal mask: number of set literals among 32,
+                                  Binomial(32, 1/s); entry n = floor(2^32 *
+                                  P(count <= n)), saturated at 2^32 - 1     */
     uint64_t q_threshold;      /* negative-class selection, thr / 2^32          */
     /* clause shard held by this process */
     int32_t clause_lo;         /* first global clause index                     */
@@ -89,6 +91,15 @@ typedef struct ytm_config {
                                   Q-selection (pytm/base.py:139-143)           */
     int32_t count_empty;       /* inference counts clauses without includes
                                   (pytm/base.py:59-67)                         */
+    /* input form of the data path (set after ytm_config_init) */
+    int32_t input_images;      /* 0: `lits` arguments are per-patch literal
+                                  words u32 [N][P][W] (ytm_encode); 1: they
+                                  are packed bit images u32 [N][image_words]
+                                  (ytm_pack_images) and the patch literal words
+                                  are formed on the fly where they are read
+                                  (models with several patches only)          */
+    int32_t image_words;       /* ceil(dim0*dim1*dim2 / 32) + 1 (one padding
+                                  word)                                        */
 } ytm_config;
 
 /* Fill *cfg.  Arguments mirror BaseTM.__init__ (base.py:42-92) and its defaults
@@ -132,6 +143,22 @@ ytm_status ytm_encode(const ytm_config *cfg, const uint32_t *X, int64_t N, uint3
  * binarised array.  workspace: ytm_workspace_bytes(cfg, YTM_OP_ENCODE_THERMO, N). */
 ytm_status ytm_encode_thermometer(const ytm_config *cfg, const uint8_t *img, int64_t N, int32_t levels,
                                   uint32_t *lits, void *workspace, void *stream);
+
+/* Pack raw inputs into one bit image per sample, the input form of
+ * cfg->input_images = 1: X u32 [N][dim0*dim1*dim2] (any nonzero value is a 1)
+ * -> img u32 [N][cfg->image_words] (bit j = input j; last word zero padding).
+ * With it, convolutional models never hold the reference's per-patch literal
+ * tensor (encode_batch, kernel.cu:76-152: P*W words per sample, 324 KB at
+ * 32x32x24 with 10x10 patches): the data-path kernels form each patch's
+ * literal words from the image where they read them.  No workspace. */
+ytm_status ytm_pack_images(const ytm_config *cfg, const uint32_t *X, int64_t N, uint32_t *img, void *stream);
+
+/* Same from raw 8-bit images, thermometer-binarised as in
+ * ytm_encode_thermometer (tm_utils/binarizer.py:5-21): img u8
+ * [N][dim0*dim1][ch], ch = dim2 / levels -> bits u32 [N][cfg->image_words].
+ * No workspace. */
+ytm_status ytm_pack_images_thermometer(const ytm_config *cfg, const uint8_t *img, int64_t N, int32_t levels,
+                                       uint32_t *bits, void *stream);
 
 /* Set every TA state of the shard to number_of_ta_states/2.
  * Replaces _reset_clauses (base.py:208-209). */
@@ -215,6 +242,18 @@ ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, int32_t *wei
                             const uint32_t *lits, int32_t B, uint64_t t0,
                             const int32_t *sel_override, int32_t *patch_w, void *workspace,
                             void *stream);
+
+/* ytm_train_update that also adds measurement counts of its feedback into
+ * counters u64[4] (device memory, accumulated, never cleared here):
+ * [0] (event, literal word) pairs applied, [1] Philox4x32-7 calls made for
+ * literal masks, [2] state words streamed (each a read and a write of every
+ * bit plane), [3] feedback events.  Measurement variant with no reference
+ * counterpart; counters == NULL gives ytm_train_update. */
+ytm_status ytm_train_update_counted(const ytm_config *cfg, uint32_t *state, int32_t *weights,
+                                    const int32_t *cs, const int32_t *Y, const uint32_t *drop,
+                                    const uint32_t *lits, int32_t B, uint64_t t0,
+                                    const int32_t *sel_override, int32_t *patch_w, void *workspace,
+                                    uint64_t *counters, void *stream);
 
 /* Train on samples 0..N-1 one at a time, in order: the reference's
  * per-sample loop (_fit, base.py:305-357: pack_clauses, fast_eval,

@@ -49,7 +49,7 @@ class OrcCfg(ct.Structure):
         ("seed", ct.c_uint64),
         ("banks", ct.c_int32), ("C", ct.c_int32), ("L", ct.c_int32), ("W", ct.c_int32), ("P", ct.c_int32),
         ("max_state", ct.c_int32), ("half_state", ct.c_int32), ("state_top", ct.c_int32),
-        ("s_thr12", ct.c_uint32), ("q_thr", ct.c_uint64),
+        ("s_cdf", ct.c_uint32 * 32), ("q_thr", ct.c_uint64),
         ("one_negative", ct.c_int32), ("count_empty", ct.c_int32),
     ]
 
@@ -71,6 +71,8 @@ def _declare(L):
     L.orc_philox4x32.argtypes = [_P, _P, ct.c_int, _P]
     L.orc_smask_word.argtypes = [ct.POINTER(OrcCfg), ct.c_uint32, _U64, ct.c_uint32, ct.c_uint32]
     L.orc_smask_word.restype = ct.c_uint32
+    L.orc_smask_count.argtypes = [ct.c_int]
+    L.orc_smask_count.restype = ct.c_uint64
     L.orc_update_threshold.argtypes = [_I32, _I32]
     L.orc_update_threshold.restype = _U64
     L.orc_encode.argtypes = [ct.POINTER(OrcCfg), _P, _I64, _P]
@@ -196,6 +198,12 @@ class Oracle:
 
     def smask_word(self, clause, t, k, w):
         return int(lib().orc_smask_word(self._cfg(), clause, t, k, w))
+
+    @staticmethod
+    def smask_count(on: bool) -> int:
+        """Start (on) or stop counting the Philox4x32-7 calls of the literal
+        masks; returns the count since the previous call and resets it."""
+        return int(lib().orc_smask_count(int(bool(on))))
 
     # -- training -----------------------------------------------------------
     def train_eval(self, lo, ta, w, lits, B, t0, drop=None, bias=None, add_bias=False, patch_w=None):

@@ -51,6 +51,8 @@ SHAPES = {
     # accuracy-parity shapes (configuration 1 / 2 rules, fewer clauses)
     "acc_vanilla": dict(number_of_clauses_per_class=50, T=15, s=3.9, dim=(28, 28, 1), n_classes=10, coalesced=False),
     "acc_coal": dict(number_of_clauses_per_class=400, T=100, s=5.0, dim=(28, 28, 1), n_classes=10),
+    # configuration 2's model (10k shared clauses, T=1000, s=15), batch 1 as the reference trains
+    "acc_c2": dict(number_of_clauses_per_class=10000, T=1000, s=15.0, dim=(28, 28, 1), n_classes=10),
     "tr_maxinc": dict(number_of_clauses_per_class=24, T=1, s=1.0, dim=(40, 1, 1), n_classes=4, q=3.0,
                       max_included_literals=3, negative_polarity=False),
 }

@@ -43,7 +43,7 @@ typedef struct orc_cfg {
     /* derived, base.py:94-121 */
     int32_t banks, C, L, W, P;
     int32_t max_state, half_state, state_top;
-    uint32_t s_thr12;
+    uint32_t s_cdf[32];
     uint64_t q_thr;
     /* rule variants of the reference's CPU TM, pytm/base.py (0 = cutm rules) */
     int32_t one_negative; /* one uniformly chosen negative class per sample, true class first (base.py:139-143) */
@@ -53,6 +53,29 @@ typedef struct orc_cfg {
 void orc_cfg_set_modes(orc_cfg *c, int32_t one_negative, int32_t count_empty) {
     c->one_negative = one_negative;
     c->count_empty = count_empty;
+}
+
+/* The literal mask's set-literal count among 32 is Binomial(32, p) with
+ * p = 1/s (the reference's S_INV, kernel.cu:31, used at 425-428, 457-460):
+ * cdf[n] = floor(2^32 * P(count <= n)), saturated at 2^32 - 1, from the pmf
+ * recurrence pmf(n+1) = pmf(n) * (32-n)/(n+1) * p/(1-p) in IEEE double. */
+static void count_cdf(double s, uint32_t cdf[32]) {
+    double p = 1.0 / s;
+    if (!(p > 0.0)) p = 0.0;
+    if (p > 1.0) p = 1.0;
+    const double q = 1.0 - p;
+    if (!(q > 0.0)) { /* p = 1: every literal is set */
+        for (int n = 0; n < 32; ++n) cdf[n] = 0u;
+        return;
+    }
+    double pmf = 1.0, acc = 0.0;
+    for (int i = 0; i < 32; ++i) pmf *= q;
+    for (int n = 0; n < 32; ++n) {
+        acc += pmf;
+        const double v = floor(acc * 4294967296.0);
+        cdf[n] = v >= 4294967295.0 ? 0xFFFFFFFFu : (uint32_t)v;
+        pmf = pmf * (double)(32 - n) / (double)(n + 1) * p / q;
+    }
 }
 
 /* ---------------------------------------------------------------- sizes */
@@ -93,12 +116,7 @@ int orc_cfg_init(orc_cfg *c, int32_t clauses_per_class, int32_t T, double s, int
         while (p < m || p < c->half_state + 1) p <<= 1;
         c->state_top = p + c->half_state;
     }
-    {
-        double t = floor(4096.0 / s + 0.5);
-        if (!(t > 0.0)) t = 0.0;
-        if (t > 4096.0) t = 4096.0;
-        c->s_thr12 = (uint32_t)t;
-    }
+    count_cdf(s, c->s_cdf);
     {
         double qp = c->q / (double)(K - 1 > 1 ? K - 1 : 1); /* kernel.cu:32 */
         if (qp >= 1.0) c->q_thr = 4294967296ull;
@@ -111,7 +129,7 @@ int orc_cfg_init(orc_cfg *c, int32_t clauses_per_class, int32_t T, double s, int
 
 void orc_cfg_sizes(const orc_cfg *c, int32_t *out) {
     out[0] = c->C; out[1] = c->K; out[2] = c->L; out[3] = c->W; out[4] = c->P;
-    out[5] = c->state_top; out[6] = (int32_t)c->s_thr12; out[7] = c->half_state;
+    out[5] = c->state_top; out[6] = (int32_t)c->s_cdf[0]; out[7] = c->half_state;
 }
 
 void orc_set_threads(int n) {
@@ -171,26 +189,61 @@ static inline void draw(const orc_cfg *c, uint32_t clause, uint64_t t, uint32_t 
     draw_r(c, clause, t, sub, tag, k, 10, out);
 }
 
-/* Bernoulli(s_thr12 / 4096) for the 32 literals of word w: literal j is set
- * iff the 12-bit number whose bit 11-i is bit j of random word i is below the
- * threshold (three Philox4x32-7 draws give the 12 random words).  Stands in
- * for `curand_uniform(rng) <= S_INV` (kernel.cu:425-428, 439, 457-460, 466). */
+/* Bernoulli(1/s) for the 32 literals of word w (stands in for the reference's
+ * per-literal `curand_uniform(rng) <= S_INV`, kernel.cu:425-428, 439,
+ * 457-460, 466), by count and placement: the first Philox4x32-7 word r0 of
+ * counter sub-index 4w gives the number n of set literals, the smallest n
+ * with r0 < cdf[n] (32 if none), i.e. Binomial(32, 1/s); then n distinct
+ * positions (or, when n > 16, the 32 - n unset ones) are drawn uniformly by
+ * rejection from 5-bit fields: bits 0-4, 5-9, ..., 25-29 of r1, r2, r3, then
+ * of all four words of further draws at sub-indices 4w+1, 4w+2, ...  Given n,
+ * every n-subset is equally likely, so the bits are independent
+ * Bernoulli(p) up to the 2^-32 resolution of the table. */
+static uint64_t g_smask_draws;
+static int g_smask_counting;
+
+/* Count the Philox4x32-7 calls of orc_smask_word from now on (on != 0) or
+ * stop; returns the count so far and resets it. */
+uint64_t orc_smask_count(int on) {
+    uint64_t v;
+#pragma omp atomic read
+    v = g_smask_draws;
+#pragma omp atomic write
+    g_smask_draws = 0;
+    g_smask_counting = on;
+    return v;
+}
+
 uint32_t orc_smask_word(const orc_cfg *c, uint32_t clause, uint64_t t, uint32_t k, uint32_t w) {
-    uint32_t thr = c->s_thr12;
-    if (thr >= 4096u) return 0xFFFFFFFFu;
-    if (thr == 0u) return 0u;
-    uint32_t R[12];
-    for (uint32_t j = 0; j < 3; ++j) draw_r(c, clause, t, w * 4u + j, TAG_SMASK, k, 7, &R[4 * j]);
-    uint32_t lt = 0u, eq = 0xFFFFFFFFu;
-    for (int i = 0; i < 12; ++i) {
-        if ((thr >> (11 - i)) & 1u) {
-            lt |= eq & ~R[i];
-            eq &= R[i];
-        } else {
-            eq &= ~R[i];
+    uint32_t R[4];
+    uint32_t sub = w * 4u, calls = 1;
+    draw_r(c, clause, t, sub, TAG_SMASK, k, 7, R);
+    uint32_t n = 0;
+    while (n < 32 && R[0] >= c->s_cdf[n]) ++n;
+    const int holes = n > 16;
+    uint32_t need = holes ? 32u - n : n, m = 0u;
+    int wi = 1, left = 6;
+    uint32_t cur = R[1];
+    while (need) {
+        if (left == 0) {
+            if (++wi == 4) {
+                draw_r(c, clause, t, ++sub, TAG_SMASK, k, 7, R);
+                ++calls;
+                wi = 0;
+            }
+            cur = R[wi];
+            left = 6;
         }
+        const uint32_t b = 1u << (cur & 31u);
+        cur >>= 5;
+        --left;
+        if (!(m & b)) { m |= b; --need; }
     }
-    return lt;
+    if (g_smask_counting) {
+#pragma omp atomic
+        g_smask_draws += calls;
+    }
+    return holes ? ~m : m;
 }
 
 /* floor(p * 2^32) for p = (y - v) / (2y), kernel.cu:508-529 (h and mod unused

@@ -37,7 +37,7 @@ def test_config_matches_oracle(name):
     assert (cfg.clauses, cfg.n_classes, cfg.literals, cfg.words, cfg.patches) == (d["C"], d["K"], d["L"], d["W"], d["P"])
     assert (cfg.clauses, cfg.literals, cfg.words, cfg.patches) == (o.C, o.L, o.W, o.P)
     assert cfg.state_top == o.state_top and cfg.half_state == o.half_state
-    assert cfg.s_threshold12 == o.cfg.s_thr12 and cfg.q_threshold == o.cfg.q_thr
+    assert list(cfg.s_count_cdf) == list(o.cfg.s_cdf) and cfg.q_threshold == o.cfg.q_thr
     # include iff state > half  <=>  stored value has the top plane set
     assert cfg.half_state + 1 + cfg.state_offset == 1 << (cfg.planes - 1)
     assert cfg.state_top + cfg.state_offset == (1 << cfg.planes) - 1

@@ -2,8 +2,14 @@
 reaches the test accuracy the reference's own training reaches (its CUDA
 kernels for the cutm rules, its numpy TM for the pytm rules) on the same data
 after the same epochs.  Fixtures: tests/golden/accuracy.json, made by
-tests/golden/make_accuracy.py.  The tolerance is on the mean over 5 seeds of a
-2000-sample test set; one run's sampling spread alone is about 0.7 pt."""
+tests/golden/make_accuracy.py.
+
+The models of configuration-1 and -2 rules with few clauses are compared on
+the mean over 48 seeds of a 10,000-sample test set: the standard error of each
+mean is about 0.15 point, so the +-0.5 point bound is about three standard
+errors of the difference.  Configuration 2's own model (10k shared clauses)
+is compared over 12 seeds, within 0.5 point or three standard errors of the
+difference of the means, whichever is larger."""
 import json
 import os
 
@@ -16,7 +22,14 @@ pytestmark = pytest.mark.gpu
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 GOLD = os.path.join(HERE, "golden", "accuracy.json")
-TOL = 0.015  # 1.5 points on the 5-seed mean
+TOL = 0.005  # 0.5 point on the seed mean
+
+
+def _tol(ours, ref):
+    """TOL, or three standard errors of the difference of the two seed means
+    when fewer seeds make that larger."""
+    se = np.sqrt(np.var(ours, ddof=1) / len(ours) + np.var(ref, ddof=1) / len(ref))
+    return max(TOL, 3 * se)
 
 
 def _gold():
@@ -32,21 +45,24 @@ def _data(g):
     return X[:n], y[:n], X[n:], y[n:]
 
 
-@pytest.mark.parametrize("name", ["acc_vanilla", "acc_coal"])
+@pytest.mark.parametrize("name", ["acc_vanilla", "acc_coal", "acc_c2"])
 def test_cutm_accuracy_matches_reference_kernels(name):
     from ytm_b200.cutm import MultiClassTM
     g = _gold()
-    if name not in g:
+    if name not in g or name not in g["models"]:
         pytest.skip("no reference-kernel accuracy recorded")
     Xtr, ytr, Xte, yte = _data(g)
     kw = {k: (tuple(v) if isinstance(v, list) else v) for k, v in g["models"][name].items()}
+    seeds = g["data"]["seeds_large"] if name == "acc_c2" else g["data"]["seeds"]
+    assert len(g[name]["accuracies"]) == len(seeds)
     accs = []
-    for seed in g["data"]["seeds"]:
+    for seed in seeds:
         tm = MultiClassTM(seed=seed, **kw)
         for _ in range(g["data"]["epochs"]):
-            tm.fit(Xtr, ytr)
+            tm.fit(Xtr, ytr)  # batch 1, as the reference trains
         accs.append((tm.predict(Xte)[0] == yte).mean())
-    assert abs(np.mean(accs) - g[name]["mean"]) <= TOL, (np.mean(accs), g[name])
+    tol = TOL if name != "acc_c2" else _tol(accs, g[name]["accuracies"])
+    assert abs(np.mean(accs) - g[name]["mean"]) <= tol, (np.mean(accs), g[name]["mean"], tol)
 
 
 def test_pytm_accuracy_matches_reference_pytm():
@@ -62,4 +78,4 @@ def test_pytm_accuracy_matches_reference_pytm():
         for _ in range(g["data"]["epochs"]):
             tm.fit(Xtr.astype(bool), ytr)
         accs.append((tm.predict(Xte.astype(bool)) == yte).mean())
-    assert abs(np.mean(accs) - g["pytm"]["mean"]) <= TOL, (np.mean(accs), g["pytm"])
+    assert abs(np.mean(accs) - g["pytm"]["mean"]) <= TOL, (np.mean(accs), g["pytm"]["mean"])

@@ -93,11 +93,75 @@ def test_batch_of_one_equals_per_sample_loop():
 
 
 def test_smask_rate():
-    """The literal mask is Bernoulli(round(4096/s)/4096)."""
+    """The literal mask is Bernoulli(1/s)."""
     o = O.Oracle(number_of_clauses_per_class=4, T=10, s=10.0, dim=(4, 1, 1), n_classes=2, seed=9)
     ones = sum(bin(o.smask_word(c, t, 0, 0)).count("1") for c in range(4) for t in range(500))
     rate = ones / (4 * 500 * 32)
-    assert abs(rate - 410 / 4096) < 0.01
+    assert abs(rate - 0.1) < 0.005
+
+
+def _smask_spec(o, clause, t, k, w):
+    """Count-and-place literal mask, restated from its definition with the
+    oracle's Philox4x32-7: count n = first index with r0 < cdf[n]; n distinct
+    positions (or 32-n holes when n > 16) from 5-bit fields of r1..r3, then of
+    further draws at sub-indices 4w+1, ..."""
+    seed = o.cfg.seed
+    key = [seed & 0xFFFFFFFF, ((seed >> 32) ^ (t >> 32)) & 0xFFFFFFFF]
+
+    def draw(sub):
+        return [int(v) for v in O.philox4x32([clause, t & 0xFFFFFFFF, sub, 2 | (k << 2)], key, 7)]
+
+    cdf = list(o.cfg.s_cdf)
+    r = draw(4 * w)
+    n = 0
+    while n < 32 and r[0] >= cdf[n]:
+        n += 1
+    holes = n > 16
+    need = 32 - n if holes else n
+    fields = []
+    for word in r[1:]:
+        fields += [(word >> (5 * i)) & 31 for i in range(6)]
+    sub, m = 4 * w, 0
+    while need:
+        if not fields:
+            sub += 1
+            for word in draw(sub):
+                fields += [(word >> (5 * i)) & 31 for i in range(6)]
+        b = 1 << fields.pop(0)
+        if not m & b:
+            m |= b
+            need -= 1
+    return (~m & 0xFFFFFFFF) if holes else m
+
+
+@pytest.mark.parametrize("s", [1.0, 1.3, 2.0, 10.0, 20.0])
+def test_smask_matches_its_definition(s):
+    o = O.Oracle(number_of_clauses_per_class=4, T=10, s=s, dim=(4, 1, 1), n_classes=3, seed=2**40 + 17)
+    for clause, t, k, w in [(0, 0, 0, 0), (3, 7, 2, 5), (1, 2**32 + 9, 1, 30), (2, 123456, 0, 1023)]:
+        assert o.smask_word(clause, t, k, w) == _smask_spec(o, clause, t, k, w)
+    if s == 1.0:
+        assert o.smask_word(0, 1, 0, 0) == 0xFFFFFFFF
+
+
+def test_smask_distribution():
+    """Count of set literals ~ Binomial(32, 1/s); every position equally
+    likely; about one Philox call per word (chi-square-free bounds at 20k
+    words)."""
+    from math import comb
+    s = 6.0
+    p = 1 / s
+    o = O.Oracle(number_of_clauses_per_class=4, T=10, s=s, dim=(4, 1, 1), n_classes=2, seed=5)
+    O.Oracle.smask_count(True)
+    words = [o.smask_word(c, t, 1, w) for c in range(4) for t in range(1000) for w in range(5)]
+    calls = O.Oracle.smask_count(False)
+    n = len(words)
+    counts = np.bincount([bin(x).count("1") for x in words], minlength=33)
+    for j in range(12):
+        want = comb(32, j) * p ** j * (1 - p) ** (32 - j) * n
+        assert abs(counts[j] - want) < 5 * np.sqrt(want) + 5
+    pos = np.array([[(x >> b) & 1 for b in range(32)] for x in words]).mean(0)
+    assert np.all(np.abs(pos - p) < 5 * np.sqrt(p * (1 - p) / n))
+    assert n <= calls < 1.01 * n
 
 
 def test_oracle_threads():

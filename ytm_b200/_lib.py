@@ -21,7 +21,8 @@ EXPORTS = (
     "ytm_state_from_u32", "ytm_state_to_u32", "ytm_include_mask", "ytm_weights_init", "ytm_infer",
     "ytm_transform", "ytm_transform_patchwise", "ytm_train_eval", "ytm_train_update",
     "ytm_train_selection", "ytm_last_error", "ytm_version", "ytm_infer_noalloc",
-    "ytm_train_fit_b1", "ytm_infer_include",
+    "ytm_train_fit_b1", "ytm_infer_include", "ytm_train_update_counted", "ytm_pack_images",
+    "ytm_pack_images_thermometer",
     "ytm_encode_thermometer", "ytm_nccl_unique_id", "ytm_nccl_comm_init", "ytm_nccl_comm_destroy",
     "ytm_train_fit_batches", "ytm_peer_ar_create", "ytm_peer_ar_open", "ytm_peer_allreduce_i32",
     "ytm_peer_ar_status", "ytm_peer_ar_destroy", "ytm_config_size",
@@ -46,9 +47,10 @@ class Config(ct.Structure):
         ("loc_literals", ct.c_int32),
         ("max_state", ct.c_int32), ("half_state", ct.c_int32), ("planes", ct.c_int32),
         ("state_offset", ct.c_int32), ("state_top", ct.c_int32),
-        ("s_threshold12", ct.c_uint32), ("q_threshold", ct.c_uint64),
+        ("s_count_cdf", ct.c_uint32 * 32), ("q_threshold", ct.c_uint64),
         ("clause_lo", ct.c_int32), ("clause_count", ct.c_int32),
         ("one_negative", ct.c_int32), ("count_empty", ct.c_int32),
+        ("input_images", ct.c_int32), ("image_words", ct.c_int32),
     ]
 
 
@@ -72,6 +74,9 @@ _SIGS = {
     "ytm_transform_patchwise": ([_CFG, _P, _P, _I64, _P, _P], ct.c_int),
     "ytm_train_eval": ([_CFG, _P, _P, _P, _P, _P, _I32, _U64, _I32, _P, _P, _P, _P], ct.c_int),
     "ytm_train_update": ([_CFG, _P, _P, _P, _P, _P, _P, _I32, _U64, _P, _P, _P, _P], ct.c_int),
+    "ytm_pack_images": ([_CFG, _P, _I64, _P, _P], ct.c_int),
+    "ytm_pack_images_thermometer": ([_CFG, _P, _I64, _I32, _P, _P], ct.c_int),
+    "ytm_train_update_counted": ([_CFG, _P, _P, _P, _P, _P, _P, _I32, _U64, _P, _P, _P, _P, _P], ct.c_int),
     "ytm_train_selection": ([_CFG, _I32, _P, _P, _P], ct.c_int),
     "ytm_train_fit_b1": ([_CFG, _P, _P, _P, _P, _P, _P, _I64, _U64, _P, _P, _P], ct.c_int),
     "ytm_infer_noalloc": ([_CFG, _P, _P, _P, _P, _I64, _P, _P], ct.c_int),

@@ -37,6 +37,12 @@ ytm_status check_cfg(const ytm_config *cfg) {
     if (cfg->clause_count <= 0 || cfg->clause_lo < 0 || cfg->clause_lo + cfg->clause_count > cfg->clauses)
         return fail(YTM_ERR_ARG, "config clause shard out of range");
     if (cfg->planes < 2 || cfg->planes > 16) return fail(YTM_ERR_UNSUPPORTED, "unsupported plane count");
+    if (cfg->input_images) {
+        if (cfg->patches <= 1)
+            return fail(YTM_ERR_UNSUPPORTED, "bit-image input is for models with several patches (use ytm_encode)");
+        if (cfg->image_words != (int32_t)cdiv((uint64_t)cfg->dim0 * cfg->dim1 * cfg->dim2, 32) + 1)
+            return fail(YTM_ERR_ARG, "config image_words does not match its dims");
+    }
     return YTM_OK;
 }
 
@@ -118,6 +124,8 @@ ytm_status ytm_config_init(ytm_config *cfg, int32_t clauses_per_class, int32_t T
     cfg->half_literals = (int32_t)half;
     cfg->words = (int32_t)((L - 1) / 32 + 1);
     cfg->patches = (dim0 - patch_dim0 + 1) * (dim1 - patch_dim1 + 1);
+    cfg->input_images = 0;
+    cfg->image_words = (int32_t)(((int64_t)dim0 * dim1 * dim2 + 31) / 32 + 1);
     cfg->max_included_literals = max_included_literals < 0 ? (int32_t)L : max_included_literals;
     // The reference sets its location thermometer bits even without
     // encode_loc (kernel.cu:101-121); they must land inside the literal vector.
@@ -141,11 +149,26 @@ ytm_status ytm_config_init(ytm_config *cfg, int32_t clauses_per_class, int32_t T
         cfg->state_top = (int32_t)(p + cfg->half_state);
         if (nb > 16) return fail(YTM_ERR_UNSUPPORTED, "number_of_ta_states needs more than 16 bit planes");
     }
+    // literal-mask count table: Binomial(32, p), p = 1/s (S_INV, kernel.cu:31);
+    // cdf[n] = floor(2^32 * P(count <= n)) saturated at 2^32 - 1, from the pmf
+    // recurrence pmf(n+1) = pmf(n) * (32-n)/(n+1) * p/(1-p) in IEEE double
     {
-        double t = floor(4096.0 / s + 0.5);
-        if (!(t > 0.0)) t = 0.0;
-        if (t > 4096.0) t = 4096.0;
-        cfg->s_threshold12 = (uint32_t)t;
+        double p = 1.0 / s;
+        if (!(p > 0.0)) p = 0.0;
+        if (p > 1.0) p = 1.0;
+        const double qq = 1.0 - p;
+        if (!(qq > 0.0)) {
+            for (int n = 0; n < 32; ++n) cfg->s_count_cdf[n] = 0u;
+        } else {
+            double pmf = 1.0, acc = 0.0;
+            for (int i = 0; i < 32; ++i) pmf *= qq;
+            for (int n = 0; n < 32; ++n) {
+                acc += pmf;
+                const double v = floor(acc * 4294967296.0);
+                cfg->s_count_cdf[n] = v >= 4294967295.0 ? 0xFFFFFFFFu : (uint32_t)v;
+                pmf = pmf * (double)(32 - n) / (double)(n + 1) * p / qq;
+            }
+        }
     }
     {
         double qp = cfg->q / (double)(n_classes - 1 > 1 ? n_classes - 1 : 1);  // kernel.cu:32

@@ -113,48 +113,59 @@ __device__ __forceinline__ u32x4 draw_rk(const RoundKeys &rk, uint32_t clause, u
     return philox_rk<R>(clause, (uint32_t)t, sub, tag | (k << 2), rk);
 }
 
-// Bernoulli(thr/4096) bits for the 32 literals of word w of clause g in the
-// feedback for class k of sample t: literal j is set iff the 12-bit number
-// whose bit 11-i is bit j of random word i is below thr; three Philox4x32-7
-// draws give the 12 words.  (Stands in for the reference's per-literal
-// `curand_uniform(rng) <= S_INV`.)  Only the literals in `cand` are wanted:
-// the comparison runs most significant bit first, so once every candidate
-// literal is decided the remaining draws cannot change the result and are
-// skipped.  Returns the bits within cand.
-// One Philox draw j of the comparison: planes 11-4j .. 8-4j of the 12-bit
-// values against the same bits of thr (branch-free: thr is uniform).
-__device__ __forceinline__ void smask_planes(uint32_t thr, int j, const u32x4 &r, uint32_t &lt, uint32_t &eq) {
-    const uint32_t R[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t tb = 0u - ((thr >> (11 - (4 * j + i))) & 1u);
-        lt |= eq & ~R[i] & tb;
-        eq &= ~(R[i] ^ tb);
-    }
-}
-
+// Bernoulli(1/s) bits for the 32 literals of word w of clause g in the
+// feedback for class k of sample t (stands in for the reference's per-literal
+// `curand_uniform(rng) <= S_INV`, kernel.cu:425-428, 457-460), by count and
+// placement, so that a word costs one Philox4x32-7 call in all but rare
+// cases: the first random word r0 of counter sub-index 4w gives the number n
+// of set literals, the smallest n with r0 < cdf[n] (32 if none), which is
+// Binomial(32, 1/s); then n distinct positions (when n > 16: the 32 - n unset
+// ones) are drawn uniformly by rejection from 5-bit fields (bits 0-4, ...,
+// 25-29) of r1, r2, r3 and, if those run out, of all four words of further
+// calls at sub-indices 4w+1, 4w+2, ...  Given n every n-subset is equally
+// likely, so the 32 bits are independent Bernoulli(1/s) (to the table's 2^-32
+// resolution).  `calls` is increased by the number of Philox calls made.
+// The count scan's index is the same in every lane still scanning, so the
+// table reads are uniform (kernel-parameter space).
 template <typename DrawFn>
-__device__ __forceinline__ uint32_t smask_compare(uint32_t thr, uint32_t cand, DrawFn drawj) {
-    if (thr >= 4096u) return cand;
-    if (thr == 0u) return 0u;
-    uint32_t lt = 0u, eq = cand;
-#pragma unroll
-    for (int j = 0; j < 3; ++j) {
-        if (eq == 0u) break;
-        smask_planes(thr, j, drawj((uint32_t)j), lt, eq);
+__device__ __forceinline__ uint32_t smask_place(const ytm_config &cfg, DrawFn drawj, uint32_t &calls) {
+    u32x4 r = drawj(0u);
+    uint32_t n = 0;
+    while (n < 32u && r.x >= cfg.s_count_cdf[n]) ++n;
+    const bool holes = n > 16u;
+    uint32_t need = holes ? 32u - n : n, m = 0u, cur = r.y, sub = 0;
+    int wi = 1, left = 6;
+    ++calls;
+    while (need) {
+        if (left == 0) {
+            if (++wi == 4) {
+                r = drawj(++sub);
+                ++calls;
+                wi = 0;
+            }
+            cur = wi == 0 ? r.x : (wi == 1 ? r.y : (wi == 2 ? r.z : r.w));
+            left = 6;
+        }
+        const uint32_t b = 1u << (cur & 31u);
+        cur >>= 5;
+        --left;
+        if (!(m & b)) {
+            m |= b;
+            --need;
+        }
     }
-    return lt;
+    return holes ? ~m : m;
 }
 
-__device__ __forceinline__ uint32_t smask_word(uint64_t seed, uint32_t thr, uint32_t cand, uint32_t g, uint64_t t,
-                                               uint32_t k, uint32_t w) {
-    return smask_compare(thr, cand, [&](uint32_t j) { return draw<7>(seed, g, t, w * 4u + j, TAG_SMASK, k); });
+__device__ __forceinline__ uint32_t smask_word(const ytm_config &cfg, uint32_t g, uint64_t t, uint32_t k, uint32_t w,
+                                               uint32_t &calls) {
+    return smask_place(cfg, [&](uint32_t j) { return draw<7>(cfg.seed, g, t, w * 4u + j, TAG_SMASK, k); }, calls);
 }
 
 // smask_word with precomputed round keys.
-__device__ __forceinline__ uint32_t smask_word_rk(const RoundKeys &rk, uint32_t thr, uint32_t cand, uint32_t g,
-                                                  uint64_t t, uint32_t k, uint32_t w) {
-    return smask_compare(thr, cand, [&](uint32_t j) { return draw_rk<7>(rk, g, t, w * 4u + j, TAG_SMASK, k); });
+__device__ __forceinline__ uint32_t smask_word_rk(const ytm_config &cfg, const RoundKeys &rk, uint32_t g, uint64_t t,
+                                                  uint32_t k, uint32_t w, uint32_t &calls) {
+    return smask_place(cfg, [&](uint32_t j) { return draw_rk<7>(rk, g, t, w * 4u + j, TAG_SMASK, k); }, calls);
 }
 
 // pytm's per-sample pick (pytm/base.py:139-141): the true class (the first
@@ -254,6 +265,112 @@ __host__ __device__ __forceinline__ uint32_t valid_mask(int w, int W, int L) {
     return r ? ((1u << r) - 1u) : 0xFFFFFFFFu;
 }
 
+// ------------------------------------------- patch literals from bit images
+// With cfg->input_images set, the `lits` arguments of the data path hold one
+// packed bit image per sample, u32 [N][image_words] (bit j = input j of the
+// D0*D1*D2 inputs, any nonzero value a 1; one zero word of padding at the
+// end), and the literal words of a patch are formed where they are used,
+// exactly as encode_batch (kernel.cu:76-152) lays them out: for patch (py, px)
+// bits [0, py) and [D1-P1, D1-P1+px) are the location thermometers (set even
+// without encode_loc, as the reference does), bit loc + ry*P0*D2 + rx*D2 + z
+// is pixel (py+ry, px+rx, z), and bit L/2 + j is NOT literal j.
+struct PatchGeom {
+    int D2, dx, seg, loc, npix, Lh, thx, W, L, neg;
+    int64_t rowbits;
+    __host__ __device__ explicit PatchGeom(const ytm_config &c)
+        : D2(c.dim2), dx(c.dim0 - c.patch_dim0 + 1), seg(c.patch_dim0 * c.dim2),
+          loc(c.encode_loc ? c.loc_literals : 0), npix(c.patch_dim0 * c.patch_dim1 * c.dim2), Lh(c.half_literals),
+          thx(c.dim1 - c.patch_dim1), W(c.words), L(c.literals), neg(c.append_negated),
+          rowbits((int64_t)c.dim0 * c.dim2) {}
+};
+
+// nbits (1..32) bits of a packed image starting at bit q (the image's padding
+// word keeps the second read inside it).
+__device__ __forceinline__ uint32_t img_bits(const uint32_t *__restrict__ img, int64_t q, int nbits) {
+    const uint32_t lo = img[q >> 5], hi = img[(q >> 5) + 1];
+    const uint32_t v = __funnelshift_r(lo, hi, (uint32_t)(q & 31));
+    return nbits >= 32 ? v : (v & ((1u << nbits) - 1u));
+}
+
+// Bits [a, a+32) of patch (py, px)'s positive literal vector (zero outside
+// [0, L/2)); a may be negative.
+__device__ __forceinline__ uint32_t pos_window(const uint32_t *__restrict__ img, const PatchGeom &g, int py, int px,
+                                               int a) {
+    if (a <= -32 || a >= g.Lh) return 0u;
+    uint32_t v = 0u;
+    // location thermometers
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int s0 = r ? g.thx : 0, s1 = r ? g.thx + px : py;
+        const int l0 = max(s0, a), l1 = min(s1, a + 32);
+        if (l0 < l1) {
+            const int n = l1 - l0;
+            v |= (n >= 32 ? 0xFFFFFFFFu : ((1u << n) - 1u)) << (l0 - a);
+        }
+    }
+    // pixels: segments of one patch row (P0 * D2 bits) each
+    int lo = max(a, g.loc);
+    const int hi = min(a + 32, g.loc + g.npix);
+    if (lo < hi) {
+        const int rel = lo - g.loc;
+        int ry = rel / g.seg, o = rel - ry * g.seg;
+        int64_t q = (int64_t)(py + ry) * g.rowbits + (int64_t)px * g.D2 + o;
+        while (lo < hi) {
+            const int n = min(hi - lo, g.seg - o);
+            v |= img_bits(img, q, n) << (lo - a);
+            lo += n;
+            q += g.rowbits - o;  // next patch row, from its first bit
+            o = 0;
+        }
+    }
+    const int keep = g.Lh - a;
+    return keep >= 32 ? v : (v & ((1u << keep) - 1u));
+}
+
+// Literal word w of patch `patch` of the sample whose bit image is img.
+__device__ __forceinline__ uint32_t patch_word(const uint32_t *__restrict__ img, const PatchGeom &g, int patch,
+                                               int w) {
+    const int py = patch / g.dx, px = patch - py * g.dx;
+    const int a = w * 32;
+    uint32_t v = pos_window(img, g, py, px, a);
+    const int rem = g.L - a;
+    const uint32_t vm = rem >= 32 ? 0xFFFFFFFFu : ((1u << rem) - 1u);
+    if (g.neg && a + 32 > g.Lh) {
+        const int k = g.Lh - a;  // bits of this word in the positive half
+        const uint32_t mpos = k >= 32 ? 0xFFFFFFFFu : (k <= 0 ? 0u : ((1u << k) - 1u));
+        v = (v & mpos) | (~pos_window(img, g, py, px, a - g.Lh) & ~mpos & vm);
+    } else {
+        v &= vm;
+    }
+    return v;
+}
+
+// The literal input of a data-path call: per-patch literal words
+// u32 [N][P][W], or packed bit images u32 [N][iws] (cfg->input_images).
+struct LitSrc {
+    const uint32_t *p;
+    PatchGeom g;
+    int P, img;
+    int64_t iws;
+    // literal word w of patch `patch` of sample n
+    __device__ __forceinline__ uint32_t word(int64_t n, int patch, int w) const {
+        if (img) return patch_word(p + n * iws, g, patch, w);
+        return __ldg(&p[(n * P + patch) * (int64_t)g.W + w]);
+    }
+    // the same source starting at sample n0
+    __host__ __device__ LitSrc from(int64_t n0) const {
+        LitSrc s = *this;
+        s.p += n0 * (img ? iws : (int64_t)P * g.W);
+        return s;
+    }
+};
+
+__host__ __device__ inline LitSrc lit_src_dev(const ytm_config &cfg, const uint32_t *lits) {
+    LitSrc s{lits, PatchGeom(cfg), cfg.patches, cfg.input_images ? 1 : 0, cfg.image_words};
+    return s;
+}
+inline LitSrc lit_src(const ytm_config *cfg, const uint32_t *lits) { return lit_src_dev(*cfg, lits); }
+
 // Dispatch a templated launcher on the plane count.
 #define YTM_DISPATCH_PLANES(NBVAR, ...)                      \
     switch (NBVAR) {                                         \
@@ -292,7 +409,7 @@ struct InferWs {
 };
 InferWs infer_ws_layout(const ytm_config *cfg, int64_t N);
 struct B1Ws {
-    uint64_t cs, fired, ninc, total;
+    uint64_t cs, fired, ninc, ring, total;
 };
 B1Ws b1_ws_layout(const ytm_config *cfg);
 uint64_t cs_planes_bytes(const ytm_config *cfg);  // class-sum weight planes scratch (eval.cu)

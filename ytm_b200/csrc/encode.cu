@@ -114,7 +114,9 @@ __global__ void k_literals(ytm_config cfg, const uint32_t *__restrict__ img, int
 // Thermometer binarisation fused into the bit packing: img u8 [N][pixels][ch]
 // -> bit image [N][IWS] with bit (pixel * ch + c) * levels + j set iff
 // img >= thr[j] (thr[j] = ceil((j+1) * 255 / (levels+1)), the integer form of
-// ThermometerBinarizer's float thresholds, tm_utils/binarizer.py:11-21).
+// ThermometerBinarizer's float thresholds, tm_utils/binarizer.py:11-21; thr =
+// NULL computes them as ((j+1) * 255 + levels) / (levels+1), the same exact
+// ceiling).
 __global__ void k_thermo_bitpack(const uint8_t *__restrict__ img, int64_t N, int64_t pixels, int ch, int levels,
                                  const uint32_t *__restrict__ thr, int64_t IWS, uint32_t *__restrict__ out) {
     const int64_t D = pixels * ch * levels;
@@ -126,7 +128,9 @@ __global__ void k_thermo_bitpack(const uint8_t *__restrict__ img, int64_t N, int
         if (q < D) {
             const int64_t pc = q / levels;  // pixel * ch + c
             const int j = (int)(q % levels);
-            v = img[n * pixels * ch + pc] >= thr[j];
+            // thr == NULL: the same thresholds in exact integer form
+            const uint32_t t = thr ? thr[j] : (uint32_t)(((j + 1) * 255 + levels) / (levels + 1));
+            v = img[n * pixels * ch + pc] >= t;
         }
         const uint32_t b = __ballot_sync(0xFFFFFFFFu, v);
         if ((threadIdx.x & 31) == 0) out[n * IWS + q / 32] = b;
@@ -172,6 +176,41 @@ extern "C" ytm_status ytm_encode_thermometer(const ytm_config *cfg, const uint8_
     int64_t blocks = std::min<int64_t>(cdiv(N * cfg->patches, wpb), (int64_t)sms * 32);
     k_literals<<<(unsigned)blocks, wpb * 32, smem, st>>>(*cfg, bits, IWS, N, lits);
     return launch_check("encode literals");
+}
+
+extern "C" ytm_status ytm_pack_images(const ytm_config *cfg, const uint32_t *X, int64_t N, uint32_t *img,
+                                      void *stream) {
+    ytm_status rc = check_cfg(cfg);
+    if (rc) return rc;
+    if (N < 0) return fail(YTM_ERR_ARG, "N < 0");
+    if (N == 0) return YTM_OK;
+    if (!X || !img) return fail(YTM_ERR_ARG, "null pointer");
+    const int64_t D = (int64_t)cfg->dim0 * cfg->dim1 * cfg->dim2;
+    const int64_t IWS = cfg->image_words;
+    if (IWS != (int64_t)cdiv(D, 32) + 1) return fail(YTM_ERR_ARG, "config image_words does not match its dims");
+    int64_t blocks = std::min<int64_t>(cdiv(N * IWS * 32, 256), (int64_t)sm_count() * 16);
+    k_bitpack<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(X, N, D, IWS, img);
+    return launch_check("image bitpack");
+}
+
+extern "C" ytm_status ytm_pack_images_thermometer(const ytm_config *cfg, const uint8_t *img, int64_t N,
+                                                  int32_t levels, uint32_t *bits, void *stream) {
+    ytm_status rc = check_cfg(cfg);
+    if (rc) return rc;
+    if (N < 0 || levels <= 0 || levels > 255) return fail(YTM_ERR_ARG, "bad N or levels");
+    if (cfg->dim2 % levels) return fail(YTM_ERR_ARG, "dim2 must be channels * levels");
+    if (N == 0) return YTM_OK;
+    if (!img || !bits) return fail(YTM_ERR_ARG, "null pointer");
+    const int ch = cfg->dim2 / levels;
+    const int64_t pixels = (int64_t)cfg->dim0 * cfg->dim1;
+    const int64_t IWS = cfg->image_words;
+    if (IWS != (int64_t)cdiv(pixels * cfg->dim2, 32) + 1)
+        return fail(YTM_ERR_ARG, "config image_words does not match its dims");
+    cudaStream_t st = as_stream(stream);
+    int64_t blocks = std::min<int64_t>(cdiv(N * IWS * 32, 256), (int64_t)sm_count() * 16);
+    // thresholds computed in the kernel (thr = NULL): no scratch memory
+    k_thermo_bitpack<<<(unsigned)blocks, 256, 0, st>>>(img, N, pixels, ch, levels, nullptr, IWS, bits);
+    return launch_check("thermometer image bitpack");
 }
 
 extern "C" ytm_status ytm_encode(const ytm_config *cfg, const uint32_t *X, int64_t N, uint32_t *lits,

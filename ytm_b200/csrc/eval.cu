@@ -26,7 +26,7 @@ constexpr int RT = 64, CT = 64, KW = 32, XS = RT + 4;
 // Violations v[i][j] = OR_w (inc & ~x) of the 4 rows x 4 clauses a thread
 // owns in the 64 x 64 tile at (row0, c0); 32-word chunks staged in shared
 // memory, no work on words past W.
-__device__ __forceinline__ void tile_violations(const uint32_t *__restrict__ inc, const uint32_t *__restrict__ lits,
+__device__ __forceinline__ void tile_violations(const uint32_t *__restrict__ inc, const LitSrc &src,
                                                 int64_t R, int C, int W, int64_t row0, int c0,
                                                 uint32_t (*xs)[XS], uint32_t (*is)[XS], uint32_t (&v)[4][4]) {
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -43,7 +43,16 @@ __device__ __forceinline__ void tile_violations(const uint32_t *__restrict__ inc
             int w = w0 + kw;
             int64_t row = row0 + r;
             int c = c0 + r;
-            xs[kw][r] = (row < R && w < W) ? __ldg(&lits[row * W + w]) : 0xFFFFFFFFu;
+            uint32_t x = 0xFFFFFFFFu;
+            if (row < R && w < W) {
+                if (src.img) {  // row = sample * P + patch
+                    const int64_t n = row / src.P;
+                    x = src.word(n, (int)(row - n * src.P), w);
+                } else {
+                    x = __ldg(&src.p[row * W + w]);
+                }
+            }
+            xs[kw][r] = x;
             is[kw][r] = (c < C && w < W) ? __ldg(&inc[(int64_t)c * W + w]) : 0u;
         }
         __syncthreads();
@@ -63,7 +72,7 @@ __device__ __forceinline__ void tile_violations(const uint32_t *__restrict__ inc
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(256) k_match(const uint32_t *__restrict__ inc, const uint32_t *__restrict__ lits,
+__global__ void __launch_bounds__(256) k_match(const uint32_t *__restrict__ inc, const LitSrc src,
                                                int64_t R, int C, int W, int P, uint32_t *__restrict__ out) {
     __shared__ __align__(16) uint32_t xs[KW][XS];
     __shared__ __align__(16) uint32_t is[KW][XS];
@@ -71,7 +80,7 @@ __global__ void __launch_bounds__(256) k_match(const uint32_t *__restrict__ inc,
     const int64_t row0 = (int64_t)blockIdx.x * RT;
     const int c0 = blockIdx.y * CT;
     uint32_t v[4][4];
-    tile_violations(inc, lits, R, C, W, row0, c0, xs, is, v);
+    tile_violations(inc, src, R, C, W, row0, c0, xs, is, v);
 
     const int cb = c0 + tx * 4;
 #pragma unroll
@@ -104,12 +113,12 @@ __global__ void __launch_bounds__(256) k_match(const uint32_t *__restrict__ inc,
 }
 
 template <int MODE>
-static ytm_status launch_match(const uint32_t *inc, const uint32_t *lits, int64_t R, int C, int W, int P,
+static ytm_status launch_match(const uint32_t *inc, const LitSrc &src, int64_t R, int C, int W, int P,
                                uint32_t *out, cudaStream_t st) {
     if (R <= 0) return YTM_OK;
     int64_t gx = (int64_t)cdiv(R, RT), gy = (int64_t)cdiv(C, CT);
     if (gx > 0x7FFFFFFFll || gy > 65535) return fail(YTM_ERR_UNSUPPORTED, "match grid too large; split the batch");
-    k_match<MODE><<<dim3((unsigned)gx, (unsigned)gy), 256, 0, st>>>(inc, lits, R, C, W, P, out);
+    k_match<MODE><<<dim3((unsigned)gx, (unsigned)gy), 256, 0, st>>>(inc, src, R, C, W, P, out);
     return launch_check("clause match");
 }
 
@@ -125,8 +134,9 @@ static unsigned grid1(int64_t threads);
 
 constexpr int SP_PT = 128, SP_STRIDE = SP_PT + 1, SP_WARPS = 32;
 
-inline size_t sparse_smem_bytes(int W) { return (size_t)W * SP_STRIDE * 4; }
-inline bool sparse_match_fits(int W) { return sparse_smem_bytes(W) <= 220 * 1024; }
+// the patch tile, plus the sample's bit image when the input is bit images
+inline size_t sparse_smem_bytes(int W, int64_t img_words = 0) { return ((size_t)W * SP_STRIDE + img_words) * 4; }
+inline bool sparse_match_fits(int W, int64_t img_words = 0) { return sparse_smem_bytes(W, img_words) <= 220 * 1024; }
 
 // One warp per clause: cnt[c] = non-zero include words, ent[c][0..cnt) =
 // (word index, include word) in word order.
@@ -155,19 +165,32 @@ __global__ void k_compact(const uint32_t *__restrict__ inc, int C, int W, int32_
 // (out cleared beforehand).  Grid: x = 128-patch tiles, y = clause blocks of
 // cpb clauses, z = samples.
 template <int MODE>
-__global__ void __launch_bounds__(SP_WARPS * 32, 2) k_match_sparse(const uint32_t *__restrict__ lits,
+__global__ void __launch_bounds__(SP_WARPS * 32, 2) k_match_sparse(const LitSrc src,
                                                                 const int32_t *__restrict__ cnt,
                                                                 const uint2 *__restrict__ ent, int C, int W, int P,
                                                                 int cpb, uint32_t *__restrict__ out) {
-    extern __shared__ uint32_t sl[];  // [W][SP_STRIDE]
+    extern __shared__ uint32_t sl[];  // [W][SP_STRIDE], then (bit images) the sample's image
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t n = blockIdx.z;
     const int p0 = blockIdx.x * SP_PT;
     const int np = min(SP_PT, P - p0);
-    const uint32_t *src = lits + ((int64_t)n * P + p0) * W;
-    for (int idx = tid; idx < SP_PT * W; idx += SP_WARPS * 32) {
-        const int p = idx / W, w = idx - p * W;
-        sl[w * SP_STRIDE + p] = p < np ? __ldg(&src[idx]) : 0u;
+    if (src.img) {
+        // the tile's patch words formed from the sample's bit image, staged
+        // in shared memory first (sliding-window patches of one image)
+        uint32_t *im = sl + W * SP_STRIDE;
+        const uint32_t *gi = src.p + n * src.iws;
+        for (int i = tid; i < src.iws; i += SP_WARPS * 32) im[i] = __ldg(&gi[i]);
+        __syncthreads();
+        for (int idx = tid; idx < SP_PT * W; idx += SP_WARPS * 32) {
+            const int p = idx / W, w = idx - p * W;
+            sl[w * SP_STRIDE + p] = p < np ? patch_word(im, src.g, p0 + p, w) : 0u;
+        }
+    } else {
+        const uint32_t *gp = src.p + ((int64_t)n * P + p0) * W;
+        for (int idx = tid; idx < SP_PT * W; idx += SP_WARPS * 32) {
+            const int p = idx / W, w = idx - p * W;
+            sl[w * SP_STRIDE + p] = p < np ? __ldg(&gp[idx]) : 0u;
+        }
     }
     __syncthreads();
     const int PW = (P + 31) / 32;
@@ -236,18 +259,20 @@ uint64_t sparse_ws_bytes(const ytm_config *cfg) {
     return align_up(C * 4, 256) + align_up(C * (uint64_t)cfg->words * 8, 256);
 }
 
-inline bool use_sparse_match(const ytm_config *cfg) { return cfg->patches > 1 && sparse_match_fits(cfg->words); }
+inline bool use_sparse_match(const ytm_config *cfg) {
+    return cfg->patches > 1 && sparse_match_fits(cfg->words, cfg->input_images ? cfg->image_words : 0);
+}
 
-// Samples [0, N) of lits; out as k_match_sparse<MODE> describes.
+// Samples [0, N) of src; out as k_match_sparse<MODE> describes.
 template <int MODE>
-static ytm_status launch_match_sparse(const uint32_t *inc, const uint32_t *lits, int64_t N, int C, int W, int P,
+static ytm_status launch_match_sparse(const uint32_t *inc, const LitSrc &src, int64_t N, int C, int W, int P,
                                       void *scratch, uint32_t *out, cudaStream_t st) {
     int32_t *cnt = (int32_t *)scratch;
     uint2 *ent = (uint2 *)((char *)scratch + align_up((uint64_t)C * 4, 256));
     k_compact<<<grid1((int64_t)C * 32), 256, 0, st>>>(inc, C, W, cnt, ent);
     ytm_status rc = launch_check("include compaction");
     if (rc) return rc;
-    const size_t smem = sparse_smem_bytes(W);
+    const size_t smem = sparse_smem_bytes(W, src.img ? src.iws : 0);
     if (smem > 48 * 1024 &&
         (rc = cuda_check(cudaFuncSetAttribute(k_match_sparse<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               (int)smem),
@@ -264,7 +289,7 @@ static ytm_status launch_match_sparse(const uint32_t *inc, const uint32_t *lits,
         cb = cdiv(C, cpb);
         uint32_t *o = out + n0 * (MODE == MODE_PBITS ? (int64_t)C * PW : CW);
         k_match_sparse<MODE><<<dim3((unsigned)tiles, (unsigned)cb, (unsigned)nb), SP_WARPS * 32, smem, st>>>(
-            lits + n0 * P * W, cnt, ent, C, W, P, cpb, o);
+            src.from(n0), cnt, ent, C, W, P, cpb, o);
         if ((rc = launch_check("sparse match"))) return rc;
     }
     return YTM_OK;
@@ -274,9 +299,10 @@ static ytm_status launch_match_sparse(const uint32_t *inc, const uint32_t *lits,
 static ytm_status launch_match_any(const ytm_config *cfg, const uint32_t *inc, const uint32_t *lits, int64_t N,
                                    void *sparse_scratch, uint32_t *fired, cudaStream_t st) {
     const int C = cfg->clause_count, W = cfg->words, P = cfg->patches;
+    const LitSrc src = lit_src(cfg, lits);
     if (sparse_scratch && use_sparse_match(cfg))
-        return launch_match_sparse<MODE_ANY>(inc, lits, N, C, W, P, sparse_scratch, fired, st);
-    return launch_match<MODE_ANY>(inc, lits, N * P, C, W, P, fired, st);
+        return launch_match_sparse<MODE_ANY>(inc, src, N, C, W, P, sparse_scratch, fired, st);
+    return launch_match<MODE_ANY>(inc, src, N * P, C, W, P, fired, st);
 }
 
 // Training evaluation of single-patch models in one kernel: the tile's
@@ -308,7 +334,7 @@ __global__ void __launch_bounds__(256) k_train_eval1(ytm_config cfg, const uint3
         w_s[q] = v;
     }
     uint32_t v[4][4];
-    tile_violations(inc, lits, B, C, W, row0, c0, xs, is, v);  // its syncs also publish w_s
+    tile_violations(inc, lit_src_dev(cfg, lits), B, C, W, row0, c0, xs, is, v);  // its syncs also publish w_s
     const int cb = c0 + tx * 4;
     uint32_t keep = 0u;  // clauses of this thread that exist and are not dropped
 #pragma unroll
@@ -464,8 +490,10 @@ __global__ void k_wmax(const int32_t *__restrict__ w, int C, int K, int own_clas
 
 __device__ __forceinline__ int planes_for(int wmax) { return 33 - __clz(wmax | 1) > 32 ? 32 : 33 - __clz(wmax | 1); }
 
-// One warp per (clause word, class): lane = clause.  planes [CW][K][32];
-// keep [CW] = clauses that count (non-empty when ninc is given).
+// One warp per (clause word, class): lane = clause.  planes [K][32][CW]
+// (class-major, clause words innermost, so that lanes walking consecutive
+// clause words read consecutive plane words); keep [CW] = clauses that count
+// (non-empty when ninc is given).
 __global__ void k_wplanes(const int32_t *__restrict__ w, const int32_t *__restrict__ ninc, int C, int K,
                           int own_class, int clause_lo, int cpc, const int32_t *__restrict__ wmax,
                           uint32_t *__restrict__ planes, uint32_t *__restrict__ keep) {
@@ -481,10 +509,10 @@ __global__ void k_wplanes(const int32_t *__restrict__ w, const int32_t *__restri
         int32_t v = 0;
         if (c < C && !(own_class && k != (clause_lo + c) / cpc)) v = w[(int64_t)c * K + k];
         const uint32_t x = (uint32_t)v + off;
-        uint32_t *pl = planes + ((int64_t)wd * K + k) * 32;
+        uint32_t *pl = planes + (int64_t)k * 32 * CWn + wd;
         for (int b = 0; b < npl; ++b) {
             const uint32_t m = __ballot_sync(0xFFFFFFFFu, (x >> b) & 1u);
-            if (lane == 0) pl[b] = m;
+            if (lane == 0) pl[(int64_t)b * CWn] = m;
         }
         if (k == 0) {
             const uint32_t m = __ballot_sync(0xFFFFFFFFu, c < C && (!ninc || ninc[c] > 0));
@@ -494,10 +522,10 @@ __global__ void k_wplanes(const int32_t *__restrict__ w, const int32_t *__restri
 }
 
 // WARP: one warp per (sample, 16 classes, segment of seg_words clause words),
-// lanes striding over the segment's words (few samples: training batches);
-// with more than one segment (gridDim.y) the partial sums are added
+// lanes striding over the segment's words (coalesced fired-bit and plane
+// reads); with more than one segment (gridDim.y) the partial sums are added
 // atomically onto cs, which then holds the bias already.  Else one thread per
-// (sample, 16 classes) walking all words (many samples: inference).
+// (sample, 16 classes) walking all words (models with few clause words).
 template <bool WARP>
 __global__ void __launch_bounds__(256) k_cs_planes(const uint32_t *__restrict__ fired,
                                                    const uint32_t *__restrict__ keep,
@@ -530,12 +558,12 @@ __global__ void __launch_bounds__(256) k_cs_planes(const uint32_t *__restrict__ 
             const uint32_t f = fr[wd] & keep[wd];
             if (!f) continue;
             nf += (uint32_t)__popc(f);
-            const uint32_t *pl = planes + ((int64_t)wd * K + k0) * 32;
+            const uint32_t *pl = planes + (int64_t)k0 * 32 * CWn + wd;
 #pragma unroll
             for (int j = 0; j < CSP_KCH; ++j) {
                 if (j < kn) {
                     uint32_t a = 0u;
-                    for (int b = 0; b < npl; ++b) a += (uint32_t)__popc(f & pl[j * 32 + b]) << b;
+                    for (int b = 0; b < npl; ++b) a += (uint32_t)__popc(f & pl[((int64_t)j * 32 + b) * CWn]) << b;
                     acc[j] += a;
                 }
             }
@@ -581,7 +609,7 @@ static ytm_status launch_cs_planes(const uint32_t *fired, const int32_t *ninc, c
     if ((rc = launch_check("weight planes"))) return rc;
     const int64_t units = N * (int64_t)cdiv(K, CSP_KCH);
     const int sms = sm_count();
-    if (units < (int64_t)sms * 32) {
+    if (units < (int64_t)sms * 32 || CW >= 64) {
         // split the clause words so that about 16 warps per SM run; a segment
         // keeps at least one word per lane
         int64_t segs = std::max<int64_t>(1, (int64_t)sms * 16 / units);
@@ -733,7 +761,7 @@ ytm_status ytm_transform_patchwise(const ytm_config *cfg, const uint32_t *state,
     if (!state || !lits || !out) return fail(YTM_ERR_ARG, "null pointer");
     const int C = cfg->clause_count, W = cfg->words, P = cfg->patches;
     const uint32_t *inc = state + (int64_t)(cfg->planes - 1) * C * W;
-    return launch_match<MODE_PATCHWISE>(inc, lits, N * P, C, W, P, out, as_stream(stream));
+    return launch_match<MODE_PATCHWISE>(inc, lit_src(cfg, lits), N * P, C, W, P, out, as_stream(stream));
 }
 
 ytm_status ytm_train_eval(const ytm_config *cfg, const uint32_t *state, const int32_t *weights, const int32_t *bias,
@@ -773,11 +801,12 @@ ytm_status ytm_train_eval(const ytm_config *cfg, const uint32_t *state, const in
     // training semantics: an empty clause matches every patch (kernel.cu:273-276)
     if (use_sparse_match(cfg)) {
         if ((rc = cuda_check(cudaMemsetAsync(fired, 0, l.sel - l.fired, st), "memset"))) return rc;
-        if ((rc = launch_match_sparse<MODE_PBITS>(inc, lits, B, C, W, P, ws + l.sparse, mbits, st))) return rc;
+        if ((rc = launch_match_sparse<MODE_PBITS>(inc, lit_src(cfg, lits), B, C, W, P, ws + l.sparse, mbits, st)))
+            return rc;
     } else {
         // match bits and fired bits are adjacent in the workspace: one clear
         if ((rc = cuda_check(cudaMemsetAsync(mbits, 0, l.sel - l.mbits, st), "memset"))) return rc;
-        if ((rc = launch_match<MODE_PBITS>(inc, lits, (int64_t)B * P, C, W, P, mbits, st))) return rc;
+        if ((rc = launch_match<MODE_PBITS>(inc, lit_src(cfg, lits), (int64_t)B * P, C, W, P, mbits, st))) return rc;
     }
     int32_t *wmax = (int32_t *)(ws + l.total);  // the class-sum planes scratch starts with the weight range
     k_pick<<<grid1((int64_t)B * C), 256, 0, st>>>(*cfg, mbits, drop, B, t0, sel, fired, patch_w, wmax);
@@ -875,7 +904,7 @@ extern "C" ytm_status ytm_infer_noalloc(const ytm_config *cfg, const uint32_t *s
     const uint32_t *inc = state + (int64_t)(cfg->planes - 1) * C * W;
     if ((rc = launch_ninc(cfg, state, ninc, st))) return rc;
     if ((rc = cuda_check(cudaMemsetAsync(fired, 0, (size_t)N * cdiv(C, 32) * 4, st), "memset"))) return rc;
-    if ((rc = launch_match<MODE_ANY>(inc, lits, N * P, C, W, P, fired, st))) return rc;
+    if ((rc = launch_match<MODE_ANY>(inc, lit_src(cfg, lits), N * P, C, W, P, fired, st))) return rc;
     k_cs_init<<<grid1(N * cfg->n_classes), 256, 0, st>>>(cs, bias, N, cfg->n_classes);
     if ((rc = launch_check("cs init"))) return rc;
     return launch_class_sums(fired, cfg->count_empty ? nullptr : ninc, weights, cfg, N, 0, cs, st);

@@ -34,8 +34,21 @@ B1Ws b1_ws_layout(const ytm_config *cfg) {
     l.cs = o;    o = align_up(o + 3 * K * 4, 256);
     l.fired = o; o = align_up(o + 2 * C * 4, 256);
     l.ninc = o;  o = align_up(o + C * 4, 256);
+    // bit-image input: the patch literal words of three samples (ring)
+    l.ring = o;
+    if (cfg->input_images) o = align_up(o + 3ull * cfg->patches * cfg->words * 4, 256);
     l.total = o;
     return l;
+}
+
+// Patch literal words u32 [P][W] of sample n of the bit images into out.
+__global__ void k_patch_words(const LitSrc src, int64_t n, uint32_t *__restrict__ out) {
+    const int64_t total = (int64_t)src.P * src.g.W;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        const int p = (int)(idx / src.g.W);
+        out[idx] = src.word(n, p, (int)(idx - (int64_t)p * src.g.W));
+    }
 }
 
 // Block = 8 warps owning CPB clauses.  Thresholds of sample i
@@ -48,7 +61,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     ytm_config cfg, uint32_t *__restrict__ state, int32_t *__restrict__ weights, const int32_t *__restrict__ bias,
     const uint32_t *__restrict__ drop, const uint32_t *__restrict__ lits, const int32_t *__restrict__ Y, int64_t i,
     int64_t N, uint64_t t0, int do_update, int32_t *__restrict__ cs_ring, int32_t *__restrict__ sel_pp,
-    int32_t *__restrict__ ninc_ws, int32_t *__restrict__ patch_w, const RoundKeys rk) {
+    int32_t *__restrict__ ninc_ws, int32_t *__restrict__ patch_w, const RoundKeys rk, uint32_t *__restrict__ ring) {
     extern __shared__ __align__(16) unsigned char smraw[];
     // Programmatic dependent launch: let launch i+1 be scheduled now, and
     // wait here until launch i-1 has completed and its writes are visible.
@@ -56,6 +69,27 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int C = cfg.clause_count, W = cfg.words, K = cfg.n_classes, L = cfg.literals;
+    // Bit-image input (convolutional models): the patch literal words of a
+    // sample are formed two launches ahead into a ring of three samples
+    // (slot = sample % 3); this launch forms sample e_next + 1's words, which
+    // no launch reads before this one has completed.
+    const int64_t PWW = (int64_t)cfg.patches * W;
+    const uint32_t *lits_of = lits;  // base of the per-sample [P][W] words (lits or the ring)
+    int64_t lits_stride = PWW;
+    if (ring) {
+        const int64_t e_nx = do_update ? i + 1 : 0;
+        if (e_nx + 1 < N) {
+            const LitSrc src = lit_src_dev(cfg, lits);
+            uint32_t *dst = ring + ((e_nx + 1) % 3) * PWW;
+            for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < PWW;
+                 idx += (int64_t)gridDim.x * blockDim.x) {
+                const int p = (int)(idx / W);
+                dst[idx] = src.word(e_nx + 1, p, (int)(idx - (int64_t)p * W));
+            }
+        }
+        lits_of = ring;
+        lits_stride = 0;  // slot chosen per sample below
+    }
     const int nk = cfg.coalesced ? K : 1;
     const int KB = (nk + 31) >> 5;                       // 32-class chunks per clause
     uint64_t *thr_s = (uint64_t *)smraw;                 // [K]  threshold | target bit
@@ -144,7 +178,9 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     const uint32_t max_s = (uint32_t)(cfg.max_state + cfg.state_offset);
     const uint32_t zero_s = (uint32_t)cfg.state_offset;
     const bool top2 = NB >= 2 && (uint32_t)cfg.state_offset + 1u == (1u << (NB >= 2 ? NB - 2 : 0));
-    const uint32_t *x_next = lits + e_next * P * W;  // patch 0 of sample i+1 (single-patch eval)
+    // [P][W] literal words of a sample
+    auto words_of = [&](int64_t smp) { return lits_of + (ring ? (smp % 3) * PWW : smp * lits_stride); };
+    const uint32_t *x_next = words_of(e_next);  // patch 0 of sample i+1 (single-patch eval)
     constexpr int CPW = CPB / FB_WARPS;  // clauses per warp
     bool has_ev[CPW];
 #pragma unroll
@@ -176,6 +212,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
         }
     }
     // 2b. clauses with events: feedback of sample i, then the evaluation
+    uint32_t n_calls = 0;  // literal-mask Philox calls (not reported by this kernel)
 #pragma unroll 1
     for (int q = 0; q < CPW; ++q) {
         if (!has_ev[q]) continue;
@@ -185,7 +222,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
         const int k0 = cfg.coalesced ? 0 : (int)(g / (uint32_t)cfg.clauses_per_class);
         const uint32_t *ev = ev_s + j * KB * 3;
         const int32_t sc = sel_cur[c];
-        const uint32_t *x_cur = lits + (i * P + (sc > 0 ? sc : 0)) * W;  // the picked patch of sample i
+        const uint32_t *x_cur = words_of(i) + (int64_t)(sc > 0 ? sc : 0) * W;  // the picked patch of sample i
         uint32_t vq = 0u;
         int cq = 0;
         for (int w = lane; w < W; w += 32) {
@@ -214,8 +251,8 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
                             cand = vm & ctr.nonzero(zero_s, top2);
                         }
                         if (cand)
-                            ctr.dec(smask_word_rk(rk, cfg.s_threshold12, cand, g, t,
-                                                  (uint32_t)(k0 + kb * 32 + b), (uint32_t)w));
+                            ctr.dec(cand & smask_word_rk(cfg, rk, g, t, (uint32_t)(k0 + kb * 32 + b), (uint32_t)w,
+                                                         n_calls));
                     }
                 }
             }
@@ -257,7 +294,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     //     pick one matching patch uniformly (select_active, kernel.cu:285-316)
     if (do_eval && P > 1) {
         uint32_t *lw = lw_s + wib * W, *li = li_s + wib * W, *mb = mb_s + wib * PW;
-        const uint32_t *xs = lits + e_next * P * W;
+        const uint32_t *xs = words_of(e_next);
         const uint64_t t_next = t0 + (uint64_t)e_next;
 #pragma unroll 1
         for (int q = 0; q < CPW; ++q) {
@@ -336,8 +373,14 @@ using namespace ytm;
 template <int NB, int CPB>
 static ytm_status launch_b1(const ytm_config *cfg, uint32_t *state, int32_t *weights, const int32_t *bias,
                             const uint32_t *drop, const uint32_t *lits, const int32_t *Y, int64_t N, uint64_t t0,
-                            int32_t *cs_ring, int32_t *sel, int32_t *ninc, int32_t *patch_w, cudaStream_t st) {
+                            int32_t *cs_ring, int32_t *sel, int32_t *ninc, int32_t *patch_w, uint32_t *ring,
+                            cudaStream_t st) {
     ytm_status rc;
+    if (ring) {  // sample 0's patch words; each launch forms the next one's
+        k_patch_words<<<(unsigned)std::min<int64_t>(cdiv((int64_t)cfg->patches * cfg->words, 256), 1024), 256, 0,
+                        st>>>(lit_src(cfg, lits), 0, ring);
+        if ((rc = launch_check("patch words"))) return rc;
+    }
     const int C = cfg->clause_count;
     const int blocks = (int)cdiv(C, CPB);
     const int nk = cfg->coalesced ? cfg->n_classes : 1;
@@ -364,7 +407,7 @@ static ytm_status launch_b1(const ytm_config *cfg, uint32_t *state, int32_t *wei
         const int upd = i < 0 ? 0 : 1;
         const RoundKeys rk = round_keys(c.seed, (uint32_t)((t0 + (uint64_t)ii) >> 32));  // keys of sample ii
         if ((rc = cuda_check(cudaLaunchKernelEx(&lc, k_fused_b1<NB, CPB>, c, state, weights, bias, drop, lits, Y, ii,
-                                                N, t0, upd, cs_ring, sel, ninc, patch_w, rk),
+                                                N, t0, upd, cs_ring, sel, ninc, patch_w, rk, ring),
                              "fused b1 launch")))
             return rc;
     }
@@ -388,13 +431,14 @@ extern "C" ytm_status ytm_train_fit_b1(const ytm_config *cfg, uint32_t *state, i
     int32_t *cs_ring = (int32_t *)(ws + l.cs);
     int32_t *sel = (int32_t *)(ws + l.fired);
     int32_t *ninc = (int32_t *)(ws + l.ninc);
+    uint32_t *ring = cfg->input_images ? (uint32_t *)(ws + l.ring) : nullptr;
     if ((rc = cuda_check(cudaMemsetAsync(cs_ring, 0, 3 * (size_t)cfg->n_classes * 4, st), "memset"))) return rc;
     const int cpb = cfg->patches > 1 ? 16 : 64;
     YTM_DISPATCH_PLANES(cfg->planes, {
         rc = cpb == 16 ? launch_b1<NB, 16>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel, ninc,
-                                           patch_w, st)
+                                           patch_w, ring, st)
                        : launch_b1<NB, 64>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel, ninc,
-                                           patch_w, st);
+                                           patch_w, ring, st);
         if (rc) return rc;
     });
     return launch_check("fused b1");

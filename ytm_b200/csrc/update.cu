@@ -195,16 +195,17 @@ template <int NB, bool WPC>
 __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, uint32_t *__restrict__ state,
                                                 int32_t *__restrict__ weights, const uint64_t *__restrict__ thr,
                                                 const uint32_t *__restrict__ drop,
-                                                const uint32_t *__restrict__ lits, int B, uint64_t t0,
+                                                const LitSrc src, int B, uint64_t t0,
                                                 const int32_t *__restrict__ sel, int32_t *__restrict__ patch_w,
                                                 int BC, const RoundKeys rk, int rk_ok,
                                                 int count_patch, const int32_t *__restrict__ pair,
                                                 const uint32_t *__restrict__ amask, const uint32_t *__restrict__ colm,
                                                 const int32_t *__restrict__ row_off,
                                                 const uint32_t *__restrict__ alist,
-                                                const uint32_t *__restrict__ fcm) {
+                                                const uint32_t *__restrict__ fcm,
+                                                unsigned long long *__restrict__ counters) {
     extern __shared__ __align__(16) unsigned char small[];
-    const int C = cfg.clause_count, W = cfg.words, K = cfg.n_classes, P = cfg.patches;
+    const int C = cfg.clause_count, W = cfg.words, K = cfg.n_classes;
     const int c = WPC ? (int)(blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) : (int)blockIdx.x;
     if (c >= C) return;
     const uint32_t g = (uint32_t)(cfg.clause_lo + c);
@@ -242,6 +243,9 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
         }
     }
     int fired_count = 0;  // single-patch models: patch 0 picks of this clause (select_active, kernel.cu:305)
+    // measurement counters: (event, word) pairs applied, Philox4x32-7 calls
+    // of the literal masks, state words streamed, events
+    uint32_t n_units = 0, n_calls = 0, n_words = 0, n_events = 0;
     const uint32_t max_s = (uint32_t)(cfg.max_state + cfg.state_offset);
     const uint32_t zero_s = (uint32_t)cfg.state_offset;
     const bool top2 = NB >= 2 && (uint32_t)cfg.state_offset + 1u == (1u << (NB >= 2 ? NB - 2 : 0));
@@ -380,7 +384,10 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
         const int nev = cnt[0];
         // 3. stream the literal words
         if (nev > 0) {
+            if (counters && tid == 0) n_events += (uint32_t)nev;
             for (int w = tid; w < W; w += nt) {
+                n_units += (uint32_t)nev;
+                ++n_words;
                 Counter<NB> ctr;
 #pragma unroll
                 for (int i = 0; i < NB; ++i) ctr.p[i] = state[((int64_t)i * C + c) * W + w];
@@ -393,21 +400,20 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                     const int b = b0 + bl;
                     const uint64_t t = t0 + (uint64_t)b;
                     if (ev == EV_T2) {  // type2_fb, kernel.cu:481-506
-                        const uint32_t x = lits[((int64_t)b * P + sel_s[bl]) * W + w];
+                        const uint32_t x = src.word(b, sel_s[bl], w);
                         ctr.inc(~x & vm & ctr.below_top());
                     } else {
                         uint32_t cand;
                         if (ev == EV_T1A) {  // type1a_fb, kernel.cu:410-443
-                            const uint32_t x = lits[((int64_t)b * P + sel_s[bl]) * W + w];
+                            const uint32_t x = src.word(b, sel_s[bl], w);
                             ctr.inc(x & vm & ctr.lt(max_s));
                             cand = ~x & vm & ctr.nonzero(zero_s, top2);
                         } else {  // type1b_fb, kernel.cu:453-470
                             cand = vm & ctr.nonzero(zero_s, top2);
                         }
                         if (cand)
-                            ctr.dec(rk_ok ? smask_word_rk(rk, cfg.s_threshold12, cand, g, t, (uint32_t)k, (uint32_t)w)
-                                          : smask_word(cfg.seed, cfg.s_threshold12, cand, g, t, (uint32_t)k,
-                                                       (uint32_t)w));
+                            ctr.dec(cand & (rk_ok ? smask_word_rk(cfg, rk, g, t, (uint32_t)k, (uint32_t)w, n_calls)
+                                                  : smask_word(cfg, g, t, (uint32_t)k, (uint32_t)w, n_calls)));
                     }
                 }
 #pragma unroll
@@ -417,6 +423,14 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
         block_sync<WPC>();
     }
     for (int kk = tid; kk < nk; kk += nt) weights[(int64_t)c * K + k0 + kk] = wk[kk];
+    if (counters) {
+        unsigned long long v[4] = {n_units, n_calls, n_words, n_events};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            for (int o = 16; o; o >>= 1) v[i] += __shfl_xor_sync(0xFFFFFFFFu, v[i], o);
+            if ((tid & 31) == 0 && v[i]) atomicAdd(&counters[i], v[i]);
+        }
+    }
     if (count_patch) {
         for (int o = 16; o; o >>= 1) fired_count += __shfl_xor_sync(0xFFFFFFFFu, fired_count, o);
         if ((tid & 31) == 0 && fired_count) atomicAdd(&patch_w[c], fired_count);
@@ -427,10 +441,12 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
 
 using namespace ytm;
 
-extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, int32_t *weights, const int32_t *cs,
-                                       const int32_t *Y, const uint32_t *drop, const uint32_t *lits, int32_t B,
-                                       uint64_t t0, const int32_t *sel_override, int32_t *patch_w, void *workspace,
-                                       void *stream) {
+extern "C" ytm_status ytm_train_update_counted(const ytm_config *cfg, uint32_t *state, int32_t *weights,
+                                               const int32_t *cs, const int32_t *Y, const uint32_t *drop,
+                                               const uint32_t *lits, int32_t B, uint64_t t0,
+                                               const int32_t *sel_override, int32_t *patch_w, void *workspace,
+                                               uint64_t *counters, void *stream) {
+    unsigned long long *ctrs = reinterpret_cast<unsigned long long *>(counters);
     ytm_status rc = check_cfg(cfg);
     if (rc) return rc;
     if (B <= 0) return fail(YTM_ERR_ARG, "batch must be positive");
@@ -475,8 +491,9 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
     if (B <= 32 && smem_wpc <= 48 * 1024) {
         YTM_DISPATCH_PLANES(cfg->planes, {
             k_update<NB, true><<<(unsigned)cdiv(cfg->clause_count, 8), 256, smem_wpc, st>>>(
-                *cfg, state, weights, thr, drop, lits, B, t0, sel, patch_w, 32, rk, rk_ok, count_patch, pair, amask, colm, row_off,
-                alist, fcm);
+                *cfg, state, weights, thr, drop, lit_src(cfg, lits), B, t0, sel, patch_w, 32, rk, rk_ok, count_patch, pair, amask,
+                colm, row_off,
+                alist, fcm, ctrs);
         });
         return launch_check("feedback");
     }
@@ -488,9 +505,18 @@ extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, i
                                  "update smem")))
                 return rc;
         }
-        k_update<NB, false><<<cfg->clause_count, tpb, smem, st>>>(*cfg, state, weights, thr, drop, lits, B, t0, sel,
+        k_update<NB, false><<<cfg->clause_count, tpb, smem, st>>>(*cfg, state, weights, thr, drop, lit_src(cfg, lits), B,
+                                                                  t0, sel,
                                                                   patch_w, BC, rk, rk_ok, count_patch, pair,
-                                                                  amask, colm, row_off, alist, fcm);
+                                                                  amask, colm, row_off, alist, fcm, ctrs);
     });
     return launch_check("feedback");
+}
+
+extern "C" ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, int32_t *weights, const int32_t *cs,
+                                       const int32_t *Y, const uint32_t *drop, const uint32_t *lits, int32_t B,
+                                       uint64_t t0, const int32_t *sel_override, int32_t *patch_w, void *workspace,
+                                       void *stream) {
+    return ytm_train_update_counted(cfg, state, weights, cs, Y, drop, lits, B, t0, sel_override, patch_w, workspace,
+                                    nullptr, stream);
 }

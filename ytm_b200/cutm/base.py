@@ -316,6 +316,23 @@ class BaseTM:
         assert Xd.shape[1] == self.dim[0] * self.dim[1] * self.dim[2], "X has the wrong number of features."
         return self.engine.encode(Xd)
 
+    def _input_device(self, X) -> torch.Tensor:
+        """Raw inputs -> the engine's input for training and inference:
+        packed bit images [N, image_words] for convolutional models (patch
+        literal words are then formed on the fly, never stored: P*W words per
+        sample), per-patch literal words [N, 1, W] for single-patch models."""
+        if self.number_of_patches == 1:
+            return self._encode_device(X)
+        if isinstance(X, torch.Tensor):
+            Xd = X.to(self.device).to(torch.int32).contiguous()
+            assert Xd.dim() == 2, "X must be a 2D array (samples, dim0 * dim1 * dim2)."
+        else:
+            assert X.ndim == 2, "X must be a 2D array (samples, dim0 * dim1 * dim2)."
+            assert X.dtype == np.uint32, "X must be of type np.uint32."
+            Xd = self._to_device(X)
+        assert Xd.shape[1] == self.dim[0] * self.dim[1] * self.dim[2], "X has the wrong number of features."
+        return self.engine.pack_images(Xd)
+
     def encode(self, X, block_size: int | None = None) -> np.ndarray:
         """Raw u32 inputs [N, D0*D1*D2] -> encoded literals u32 [N, P, W] (host)."""
         return self._encode_device(X).cpu().numpy().view(np.uint32)
@@ -340,7 +357,7 @@ class BaseTM:
 
     def _literals_device(self, X, is_X_encoded: bool) -> torch.Tensor:
         if not is_X_encoded:
-            return self._encode_device(X)
+            return self._input_device(X)
         lits = self._to_device(X)
         return lits.reshape(-1, self.number_of_patches, self.number_of_literal_chunks)
 
@@ -354,7 +371,8 @@ class BaseTM:
             raise ValueError("batch_size must be >= 1")
         lits = encoded_X if isinstance(encoded_X, torch.Tensor) and encoded_X.device == self.device \
             else self._literals_device(encoded_X, True)
-        lits = lits.reshape(-1, self.number_of_patches, self.number_of_literal_chunks)
+        if not self._is_images(lits):
+            lits = lits.reshape(-1, self.number_of_patches, self.number_of_literal_chunks)
         Y = self._to_device(encoded_Y, np.int32).reshape(-1, self.number_of_outputs)
         N = lits.shape[0]
         if clause_drop_p > 0.0:  # base.py:288-293: one mask per fit call, from the host RNG
@@ -389,6 +407,10 @@ class BaseTM:
             t += B
             self.last_class_sums = cs
         self.sample_counter = t
+
+    def _is_images(self, lits: torch.Tensor) -> bool:
+        """Packed bit images (2-D) rather than per-patch literal words (3-D)."""
+        return lits.dim() == 2 and self.number_of_patches > 1
 
     def _fused_b1_ok(self) -> bool:
         """Batch-1 training runs as one fused launch per sample unless the
@@ -430,7 +452,8 @@ class BaseTM:
         if self.world > 1 and self.inference_sharding == "samples":
             return self._score_samples_sharded(lits)
         if chunk is None:
-            per = max(1, self.number_of_patches * self.number_of_literal_chunks * 4
+            per = max(1, (lits.shape[1] if self._is_images(lits) else
+                          self.number_of_patches * self.number_of_literal_chunks) * 4
                       + ((self.clause_count + 31) // 32) * 4)
             chunk = max(1, min(N, (1 << 31) // per))
         outs = []

@@ -50,11 +50,26 @@ class CudaEngine:
     def _cfg(self):
         return ct.byref(self.cfg)
 
+    @property
+    def cfg_img(self) -> _lib.Config:
+        """A copy of cfg for packed bit-image input (input_images = 1)."""
+        c = _lib.Config.from_buffer_copy(self.cfg)
+        c.input_images = 1 if self.P > 1 else 0
+        return c
+
+    def _cfg_for(self, lits: torch.Tensor | None):
+        """The config matching the input form of `lits`: 2-D [N, image_words]
+        tensors are packed bit images (convolutional models: input_images = 1),
+        3-D [N, P, W] tensors per-patch literal words."""
+        if lits is not None and lits.dim() == 2 and self.P > 1:
+            return ct.byref(self.cfg_img)
+        return self._cfg
+
     def _stream(self):
         return ct.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
 
-    def workspace(self, op: int, n: int) -> torch.Tensor:
-        need = int(self.lib.ytm_workspace_bytes(self._cfg, op, int(n)))
+    def workspace(self, op: int, n: int, cfg=None) -> torch.Tensor:
+        need = int(self.lib.ytm_workspace_bytes(cfg if cfg is not None else self._cfg, op, int(n)))
         ws = self._ws.get(op)
         if ws is None or ws.numel() < need:
             ws = torch.empty(max(need, 256), dtype=torch.uint8, device=self.device)
@@ -108,6 +123,31 @@ class CudaEngine:
             check(self.lib.ytm_encode(self._cfg, _p(X), N, _p(lits), _p(ws), self._stream()), "ytm_encode")
         return lits
 
+    def pack_images(self, X: torch.Tensor) -> torch.Tensor:
+        """X int32/uint32 [N, D] on this device -> packed bit images int32
+        [N, image_words], the input form that forms patch literal words on the
+        fly (models with several patches)."""
+        X = X.contiguous()
+        N = X.shape[0]
+        out = torch.empty((N, self.cfg.image_words), dtype=torch.int32, device=self.device)
+        if N:
+            with torch.cuda.device(self.device):
+                check(self.lib.ytm_pack_images(ct.byref(self.cfg_img), _p(X), N, _p(out), self._stream()),
+                      "ytm_pack_images")
+        return out
+
+    def pack_images_thermometer(self, img: torch.Tensor, levels: int) -> torch.Tensor:
+        """Raw uint8 images [N, dim0*dim1*channels] -> thermometer-binarised
+        packed bit images int32 [N, image_words]."""
+        img = img.contiguous()
+        N = img.shape[0]
+        out = torch.empty((N, self.cfg.image_words), dtype=torch.int32, device=self.device)
+        if N:
+            with torch.cuda.device(self.device):
+                check(self.lib.ytm_pack_images_thermometer(ct.byref(self.cfg_img), _p(img), N, int(levels), _p(out),
+                                                           self._stream()), "ytm_pack_images_thermometer")
+        return out
+
     def encode_thermometer(self, img: torch.Tensor, levels: int) -> torch.Tensor:
         """Raw uint8 images [N, dim0*dim1*channels] on this device ->
         literals int32 [N, P, W] (thermometer binarisation on the device)."""
@@ -123,13 +163,14 @@ class CudaEngine:
         return lits
 
     def infer(self, lits: torch.Tensor, add_bias: bool = True) -> torch.Tensor:
+        c = self._cfg_for(lits)
         N = lits.shape[0]
         cs = torch.empty((N, self.K), dtype=torch.int32, device=self.device)
         if N == 0:
             return cs
-        ws = self.workspace(_lib.YTM_OP_INFER, N)
+        ws = self.workspace(_lib.YTM_OP_INFER, N, c)
         with torch.cuda.device(self.device):
-            check(self.lib.ytm_infer(self._cfg, _p(self.state), _p(self.weights), _p(self.bias) if add_bias else None,
+            check(self.lib.ytm_infer(c, _p(self.state), _p(self.weights), _p(self.bias) if add_bias else None,
                                      _p(lits), N, _p(cs), _p(ws), self._stream()), "ytm_infer")
         return cs
 
@@ -141,6 +182,9 @@ class CudaEngine:
         cs = torch.empty((N, self.K), dtype=torch.int32, device=self.device)
         if N == 0:
             return cs
+        if lits.dim() == 2 and cfg_full.patches > 1:  # bit images
+            cfg_full = _lib.Config.from_buffer_copy(cfg_full)
+            cfg_full.input_images = 1
         need = int(self.lib.ytm_workspace_bytes(ct.byref(cfg_full), _lib.YTM_OP_INFER, N))
         ws = torch.empty(max(need, 256), dtype=torch.uint8, device=self.device)
         with torch.cuda.device(self.device):
@@ -149,55 +193,69 @@ class CudaEngine:
         return cs
 
     def transform(self, lits: torch.Tensor) -> torch.Tensor:
+        c = self._cfg_for(lits)
         N = lits.shape[0]
         out = torch.empty((N, self.C), dtype=torch.int32, device=self.device)
         if N == 0:
             return out
-        ws = self.workspace(_lib.YTM_OP_TRANSFORM, N)
+        ws = self.workspace(_lib.YTM_OP_TRANSFORM, N, c)
         with torch.cuda.device(self.device):
-            check(self.lib.ytm_transform(self._cfg, _p(self.state), _p(lits), N, _p(out), _p(ws), self._stream()),
+            check(self.lib.ytm_transform(c, _p(self.state), _p(lits), N, _p(out), _p(ws), self._stream()),
                   "ytm_transform")
         return out
 
     def transform_patchwise(self, lits: torch.Tensor) -> torch.Tensor:
+        c = self._cfg_for(lits)
         N = lits.shape[0]
         out = torch.empty((N, self.C, self.P), dtype=torch.int32, device=self.device)
         if N == 0:
             return out
         with torch.cuda.device(self.device):
-            check(self.lib.ytm_transform_patchwise(self._cfg, _p(self.state), _p(lits), N, _p(out), self._stream()),
+            check(self.lib.ytm_transform_patchwise(c, _p(self.state), _p(lits), N, _p(out), self._stream()),
                   "ytm_transform_patchwise")
         return out
 
     def train_eval(self, lits_b: torch.Tensor, t0: int, drop: torch.Tensor | None, add_bias: bool) -> torch.Tensor:
+        c = self._cfg_for(lits_b)
         B = lits_b.shape[0]
         cs = torch.empty((B, self.K), dtype=torch.int32, device=self.device)
-        ws = self.workspace(_lib.YTM_OP_TRAIN, B)
+        ws = self.workspace(_lib.YTM_OP_TRAIN, B, c)
         with torch.cuda.device(self.device):
-            check(self.lib.ytm_train_eval(self._cfg, _p(self.state), _p(self.weights), _p(self.bias), _p(drop),
+            check(self.lib.ytm_train_eval(c, _p(self.state), _p(self.weights), _p(self.bias), _p(drop),
                                           _p(lits_b), B, int(t0), int(bool(add_bias)), _p(cs), _p(self.patch_w),
                                           _p(ws), self._stream()), "ytm_train_eval")
         return cs
 
     def train_update(self, cs: torch.Tensor, Y_b: torch.Tensor, lits_b: torch.Tensor, t0: int,
-                     drop: torch.Tensor | None, sel_override: torch.Tensor | None = None) -> None:
+                     drop: torch.Tensor | None, sel_override: torch.Tensor | None = None,
+                     counters: torch.Tensor | None = None) -> None:
+        """Feedback of the batch.  counters: optional int64 [4] device tensor
+        that accumulates the measurement counts of ytm_train_update_counted."""
+        c = self._cfg_for(lits_b)
         B = lits_b.shape[0]
-        ws = self.workspace(_lib.YTM_OP_TRAIN, B)
+        ws = self.workspace(_lib.YTM_OP_TRAIN, B, c)
         with torch.cuda.device(self.device):
-            check(self.lib.ytm_train_update(self._cfg, _p(self.state), _p(self.weights), _p(cs), _p(Y_b), _p(drop),
-                                            _p(lits_b), B, int(t0), _p(sel_override), _p(self.patch_w), _p(ws),
-                                            self._stream()),
-                  "ytm_train_update")
+            if counters is None:
+                check(self.lib.ytm_train_update(c, _p(self.state), _p(self.weights), _p(cs), _p(Y_b),
+                                                _p(drop), _p(lits_b), B, int(t0), _p(sel_override), _p(self.patch_w),
+                                                _p(ws), self._stream()),
+                      "ytm_train_update")
+            else:
+                check(self.lib.ytm_train_update_counted(c, _p(self.state), _p(self.weights), _p(cs), _p(Y_b),
+                                                        _p(drop), _p(lits_b), B, int(t0), _p(sel_override),
+                                                        _p(self.patch_w), _p(ws), _p(counters), self._stream()),
+                      "ytm_train_update_counted")
 
     def train_fit_b1(self, lits: torch.Tensor, Y: torch.Tensor, t0: int, drop: torch.Tensor | None) -> None:
         """Batch-1 training over all samples of lits in order (single
         process): one fused launch per sample."""
+        c = self._cfg_for(lits)
         N = lits.shape[0]
         if N == 0:
             return
-        ws = self.workspace(_lib.YTM_OP_TRAIN_B1, 0)
+        ws = self.workspace(_lib.YTM_OP_TRAIN_B1, 0, c)
         with torch.cuda.device(self.device):
-            check(self.lib.ytm_train_fit_b1(self._cfg, _p(self.state), _p(self.weights), _p(self.bias), _p(drop),
+            check(self.lib.ytm_train_fit_b1(c, _p(self.state), _p(self.weights), _p(self.bias), _p(drop),
                                             _p(lits), _p(Y), N, int(t0), _p(self.patch_w), _p(ws), self._stream()),
                   "ytm_train_fit_b1")
 
@@ -206,13 +264,14 @@ class CudaEngine:
         """Mini-batch training over all samples of lits in order, queued from C
         (eval, NCCL all-reduce of the class sums on `comm` if given, feedback
         per batch).  Returns the class sums [b, K] of the last batch."""
+        c = self._cfg_for(lits)
         N = lits.shape[0]
         if N == 0:
             return torch.empty((0, self.K), dtype=torch.int32, device=self.device)
         B = int(min(B, N))
-        ws = self.workspace(_lib.YTM_OP_TRAIN_LOOP, B)
+        ws = self.workspace(_lib.YTM_OP_TRAIN_LOOP, B, c)
         with torch.cuda.device(self.device):
-            check(self.lib.ytm_train_fit_batches(self._cfg, _p(self.state), _p(self.weights), _p(self.bias), _p(drop),
+            check(self.lib.ytm_train_fit_batches(c, _p(self.state), _p(self.weights), _p(self.bias), _p(drop),
                                                  _p(lits), _p(Y), N, B, int(t0), int(bool(add_bias)),
                                                  _p(self.patch_w), comm, peer_ar, _p(ws), self._stream()),
                   "ytm_train_fit_batches")

@@ -101,6 +101,26 @@ def rules(N, seed=1005, n_classes=100, n_features=16384, density=0.01, rules_per
     return X.astype(np.uint32), y.astype(np.uint32)
 
 
+def rules_torch(N, seed, device, n_classes=100, n_features=16384, density=0.01, rules_per_class=10, rule_len=8,
+                rule_seed=1005):
+    """Config 5 generated on the GPU (for the 2^20-sample inference run, 64 GB
+    as host u32): the same planted rules as rules(rule_seed) (the rule table is
+    drawn with numpy), Bernoulli(density) background and labels from a torch
+    generator seeded with `seed`.  Returns int32 [N, n_features] 0/1 on device."""
+    import torch
+    rng = np.random.default_rng(rule_seed)
+    feat = torch.from_numpy(rng.integers(0, n_features, (n_classes, rules_per_class, rule_len))).to(device)
+    pol = torch.from_numpy(rng.random((n_classes, rules_per_class, rule_len)) < 0.5).to(device)
+    g = torch.Generator(device=device)
+    g.manual_seed(int(seed))
+    y = torch.randint(0, n_classes, (N,), generator=g, device=device)
+    r = torch.randint(0, rules_per_class, (N,), generator=g, device=device)
+    X = (torch.rand((N, n_features), generator=g, device=device) < density).to(torch.int32)
+    rows = torch.arange(N, device=device).repeat_interleave(rule_len)
+    X[rows, feat[y, r].reshape(-1)] = pol[y, r].reshape(-1).to(torch.int32)
+    return X
+
+
 def make(name, N, seed=None):
     seed = SEEDS[name] if seed is None else seed
     if name in ("c1", "c2", "p1"):
