@@ -64,7 +64,8 @@ TrainWs train_ws_layout(const ytm_config *cfg, int64_t B) {
     l.row_off = o; o = align_up(o + ((uint64_t)B + 1) * 4, 256);
     l.alist = o; o = align_up(o + (uint64_t)B * K * 4, 256);
     l.pair = o;  o = align_up(o + (uint64_t)B * 2 * 4, 256);
-    l.sparse = o; o += sparse_ws_bytes(cfg);  // compacted include words (sparse patch match)
+    l.sparse = o; o = align_up(o + sparse_ws_bytes(cfg), 256);  // compacted include words (sparse patch match)
+    l.pwords = o; o += batch_words_bytes(cfg, B);  // bit-image input: the batch's patch literal words
     l.total = o;
     return l;
 }

@@ -127,15 +127,30 @@ __device__ __forceinline__ u32x4 draw_rk(const RoundKeys &rk, uint32_t clause, u
 // resolution).  `calls` is increased by the number of Philox calls made.
 // The count scan's index is the same in every lane still scanning, so the
 // table reads are uniform (kernel-parameter space).
+// The count and the first six placements run branch-free (the same
+// sequential rejection, unrolled), so that the lanes of a warp stay together;
+// only counts of 8 or more and words whose first six fields did not finish
+// the placement continue in the loops.
 template <typename DrawFn>
 __device__ __forceinline__ uint32_t smask_place(const ytm_config &cfg, DrawFn drawj, uint32_t &calls) {
     u32x4 r = drawj(0u);
     uint32_t n = 0;
-    while (n < 32u && r.x >= cfg.s_count_cdf[n]) ++n;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) n += r.x >= cfg.s_count_cdf[j] ? 1u : 0u;
+    if (n == 8u)
+        while (n < 32u && r.x >= cfg.s_count_cdf[n]) ++n;
     const bool holes = n > 16u;
-    uint32_t need = holes ? 32u - n : n, m = 0u, cur = r.y, sub = 0;
-    int wi = 1, left = 6;
+    uint32_t need = holes ? 32u - n : n, m = 0u;
     ++calls;
+#pragma unroll
+    for (int f = 0; f < 6; ++f) {  // fields 0-5: bits 0-29 of r.y
+        const uint32_t b = 1u << ((r.y >> (5 * f)) & 31u);
+        const bool take = need != 0u && !(m & b);
+        m |= take ? b : 0u;
+        need -= take ? 1u : 0u;
+    }
+    uint32_t cur = r.z, sub = 0;
+    int wi = 2, left = 6;
     while (need) {
         if (left == 0) {
             if (++wi == 4) {
@@ -240,6 +255,21 @@ struct Counter {
             }
         }
         return l;
+    }
+    // lt(v) for v = 2^(NB-1) + 2^(NB-2) - 1, the stored maximum state when
+    // the state count is a power of two (offset + 1 = 2^(NB-2)): a value is
+    // >= v iff its top plane is set and either the next plane or all lower
+    // planes are
+    __device__ __forceinline__ uint32_t lt_max_pow2() const {
+        uint32_t low = 0xFFFFFFFFu;
+#pragma unroll
+        for (int i = 0; i + 2 < NB; ++i) low &= p[i];
+        return ~(p[NB - 1] & (p[NB - 2] | low));
+    }
+    // lt(max_s) with the shortcut above when it applies (pow2 is uniform)
+    __device__ __forceinline__ uint32_t lt_max(uint32_t max_s, bool pow2) const {
+        if (NB >= 3 && pow2) return lt_max_pow2();
+        return lt(max_s);
     }
     // literals whose stored value is not all ones (below the top)
     // literals whose stored value is not v (= the stored zero state, offset):
@@ -352,9 +382,12 @@ struct LitSrc {
     PatchGeom g;
     int P, img;
     int64_t iws;
-    // literal word w of patch `patch` of sample n
+    // literal word w of patch `patch` of sample n; kernels instantiate IMG =
+    // img so that the per-patch-word instantiation carries no image code
+    // (its register count would otherwise grow)
+    template <bool IMG>
     __device__ __forceinline__ uint32_t word(int64_t n, int patch, int w) const {
-        if (img) return patch_word(p + n * iws, g, patch, w);
+        if (IMG) return patch_word(p + n * iws, g, patch, w);
         return __ldg(&p[(n * P + patch) * (int64_t)g.W + w]);
     }
     // the same source starting at sample n0
@@ -401,9 +434,16 @@ ytm_status check_cfg(const ytm_config *cfg);
 
 // Workspace carve-up (offsets in bytes, 256-aligned).
 struct TrainWs {
-    uint64_t ninc, mbits, sel, fired, fcm, thr, amask, colm, row_off, alist, pair, sparse, total;
+    uint64_t ninc, mbits, sel, fired, fcm, thr, amask, colm, row_off, alist, pair, sparse, pwords, total;
 };
 TrainWs train_ws_layout(const ytm_config *cfg, int64_t B);
+// Bit-image input: the feedback reads the batch's patch literal words from a
+// transient [B][P][W] buffer in the training workspace, formed from the
+// images by one kernel per batch (the per-sample arrays of the batch, such
+// as the patch match bits [B][C][P/32], are larger still).
+inline uint64_t batch_words_bytes(const ytm_config *cfg, int64_t B) {
+    return cfg->input_images ? (uint64_t)B * cfg->patches * cfg->words * 4 : 0;
+}
 struct InferWs {
     uint64_t ninc, fired, total;
 };

@@ -26,6 +26,7 @@ constexpr int RT = 64, CT = 64, KW = 32, XS = RT + 4;
 // Violations v[i][j] = OR_w (inc & ~x) of the 4 rows x 4 clauses a thread
 // owns in the 64 x 64 tile at (row0, c0); 32-word chunks staged in shared
 // memory, no work on words past W.
+template <bool IMG>
 __device__ __forceinline__ void tile_violations(const uint32_t *__restrict__ inc, const LitSrc &src,
                                                 int64_t R, int C, int W, int64_t row0, int c0,
                                                 uint32_t (*xs)[XS], uint32_t (*is)[XS], uint32_t (&v)[4][4]) {
@@ -45,9 +46,9 @@ __device__ __forceinline__ void tile_violations(const uint32_t *__restrict__ inc
             int c = c0 + r;
             uint32_t x = 0xFFFFFFFFu;
             if (row < R && w < W) {
-                if (src.img) {  // row = sample * P + patch
+                if (IMG) {  // row = sample * P + patch
                     const int64_t n = row / src.P;
-                    x = src.word(n, (int)(row - n * src.P), w);
+                    x = src.word<true>(n, (int)(row - n * src.P), w);
                 } else {
                     x = __ldg(&src.p[row * W + w]);
                 }
@@ -71,7 +72,7 @@ __device__ __forceinline__ void tile_violations(const uint32_t *__restrict__ inc
     }
 }
 
-template <int MODE>
+template <int MODE, bool IMG>
 __global__ void __launch_bounds__(256) k_match(const uint32_t *__restrict__ inc, const LitSrc src,
                                                int64_t R, int C, int W, int P, uint32_t *__restrict__ out) {
     __shared__ __align__(16) uint32_t xs[KW][XS];
@@ -80,7 +81,7 @@ __global__ void __launch_bounds__(256) k_match(const uint32_t *__restrict__ inc,
     const int64_t row0 = (int64_t)blockIdx.x * RT;
     const int c0 = blockIdx.y * CT;
     uint32_t v[4][4];
-    tile_violations(inc, src, R, C, W, row0, c0, xs, is, v);
+    tile_violations<IMG>(inc, src, R, C, W, row0, c0, xs, is, v);
 
     const int cb = c0 + tx * 4;
 #pragma unroll
@@ -118,7 +119,10 @@ static ytm_status launch_match(const uint32_t *inc, const LitSrc &src, int64_t R
     if (R <= 0) return YTM_OK;
     int64_t gx = (int64_t)cdiv(R, RT), gy = (int64_t)cdiv(C, CT);
     if (gx > 0x7FFFFFFFll || gy > 65535) return fail(YTM_ERR_UNSUPPORTED, "match grid too large; split the batch");
-    k_match<MODE><<<dim3((unsigned)gx, (unsigned)gy), 256, 0, st>>>(inc, src, R, C, W, P, out);
+    if (src.img)
+        k_match<MODE, true><<<dim3((unsigned)gx, (unsigned)gy), 256, 0, st>>>(inc, src, R, C, W, P, out);
+    else
+        k_match<MODE, false><<<dim3((unsigned)gx, (unsigned)gy), 256, 0, st>>>(inc, src, R, C, W, P, out);
     return launch_check("clause match");
 }
 
@@ -164,7 +168,7 @@ __global__ void k_compact(const uint32_t *__restrict__ inc, int C, int W, int32_
 // MODE_ANY: bit c of out[n][CW] is set when clause c matches some patch
 // (out cleared beforehand).  Grid: x = 128-patch tiles, y = clause blocks of
 // cpb clauses, z = samples.
-template <int MODE>
+template <int MODE, bool IMG>
 __global__ void __launch_bounds__(SP_WARPS * 32, 2) k_match_sparse(const LitSrc src,
                                                                 const int32_t *__restrict__ cnt,
                                                                 const uint2 *__restrict__ ent, int C, int W, int P,
@@ -174,7 +178,7 @@ __global__ void __launch_bounds__(SP_WARPS * 32, 2) k_match_sparse(const LitSrc 
     const int64_t n = blockIdx.z;
     const int p0 = blockIdx.x * SP_PT;
     const int np = min(SP_PT, P - p0);
-    if (src.img) {
+    if (IMG) {
         // the tile's patch words formed from the sample's bit image, staged
         // in shared memory first (sliding-window patches of one image)
         uint32_t *im = sl + W * SP_STRIDE;
@@ -274,8 +278,8 @@ static ytm_status launch_match_sparse(const uint32_t *inc, const LitSrc &src, in
     if (rc) return rc;
     const size_t smem = sparse_smem_bytes(W, src.img ? src.iws : 0);
     if (smem > 48 * 1024 &&
-        (rc = cuda_check(cudaFuncSetAttribute(k_match_sparse<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)smem),
+        (rc = cuda_check(cudaFuncSetAttribute(src.img ? k_match_sparse<MODE, true> : k_match_sparse<MODE, false>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                          "sparse match smem")))
         return rc;
     const int tiles = (int)cdiv(P, SP_PT);
@@ -288,8 +292,11 @@ static ytm_status launch_match_sparse(const uint32_t *inc, const LitSrc &src, in
         const int cpb = (int)cdiv(C, cb);
         cb = cdiv(C, cpb);
         uint32_t *o = out + n0 * (MODE == MODE_PBITS ? (int64_t)C * PW : CW);
-        k_match_sparse<MODE><<<dim3((unsigned)tiles, (unsigned)cb, (unsigned)nb), SP_WARPS * 32, smem, st>>>(
-            src.from(n0), cnt, ent, C, W, P, cpb, o);
+        const dim3 grid((unsigned)tiles, (unsigned)cb, (unsigned)nb);
+        if (src.img)
+            k_match_sparse<MODE, true><<<grid, SP_WARPS * 32, smem, st>>>(src.from(n0), cnt, ent, C, W, P, cpb, o);
+        else
+            k_match_sparse<MODE, false><<<grid, SP_WARPS * 32, smem, st>>>(src.from(n0), cnt, ent, C, W, P, cpb, o);
         if ((rc = launch_check("sparse match"))) return rc;
     }
     return YTM_OK;
@@ -334,7 +341,7 @@ __global__ void __launch_bounds__(256) k_train_eval1(ytm_config cfg, const uint3
         w_s[q] = v;
     }
     uint32_t v[4][4];
-    tile_violations(inc, lit_src_dev(cfg, lits), B, C, W, row0, c0, xs, is, v);  // its syncs also publish w_s
+    tile_violations<false>(inc, lit_src_dev(cfg, lits), B, C, W, row0, c0, xs, is, v);  // its syncs also publish w_s
     const int cb = c0 + tx * 4;
     uint32_t keep = 0u;  // clauses of this thread that exist and are not dropped
 #pragma unroll

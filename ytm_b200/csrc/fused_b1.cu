@@ -47,7 +47,7 @@ __global__ void k_patch_words(const LitSrc src, int64_t n, uint32_t *__restrict_
     for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
          idx += (int64_t)gridDim.x * blockDim.x) {
         const int p = (int)(idx / src.g.W);
-        out[idx] = src.word(n, p, (int)(idx - (int64_t)p * src.g.W));
+        out[idx] = src.word<true>(n, p, (int)(idx - (int64_t)p * src.g.W));
     }
 }
 
@@ -56,7 +56,7 @@ __global__ void k_patch_words(const LitSrc src, int64_t n, uint32_t *__restrict_
 // Philox class draws of 32 clauses share each warp instruction); then each
 // warp streams the words of its clauses (8 per warp), applying the events and
 // evaluating sample i+1.
-template <int NB, int CPB>
+template <int NB, int CPB, bool IMG>
 __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     ytm_config cfg, uint32_t *__restrict__ state, int32_t *__restrict__ weights, const int32_t *__restrict__ bias,
     const uint32_t *__restrict__ drop, const uint32_t *__restrict__ lits, const int32_t *__restrict__ Y, int64_t i,
@@ -76,7 +76,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     const int64_t PWW = (int64_t)cfg.patches * W;
     const uint32_t *lits_of = lits;  // base of the per-sample [P][W] words (lits or the ring)
     int64_t lits_stride = PWW;
-    if (ring) {
+    if (IMG) {
         const int64_t e_nx = do_update ? i + 1 : 0;
         if (e_nx + 1 < N) {
             const LitSrc src = lit_src_dev(cfg, lits);
@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
             for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < PWW;
                  idx += (int64_t)gridDim.x * blockDim.x) {
                 const int p = (int)(idx / W);
-                dst[idx] = src.word(e_nx + 1, p, (int)(idx - (int64_t)p * W));
+                dst[idx] = src.word<true>(e_nx + 1, p, (int)(idx - (int64_t)p * W));
             }
         }
         lits_of = ring;
@@ -178,8 +178,10 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     const uint32_t max_s = (uint32_t)(cfg.max_state + cfg.state_offset);
     const uint32_t zero_s = (uint32_t)cfg.state_offset;
     const bool top2 = NB >= 2 && (uint32_t)cfg.state_offset + 1u == (1u << (NB >= 2 ? NB - 2 : 0));
+    // the stored maximum is 2^(NB-1) + 2^(NB-2) - 1 (power-of-two state counts)
+    const bool max_pow2 = NB >= 3 && max_s == (1u << (NB - 1)) + (1u << (NB >= 2 ? NB - 2 : 0)) - 1u;
     // [P][W] literal words of a sample
-    auto words_of = [&](int64_t smp) { return lits_of + (ring ? (smp % 3) * PWW : smp * lits_stride); };
+    auto words_of = [&](int64_t smp) { return lits_of + (IMG ? (smp % 3) * PWW : smp * lits_stride); };
     const uint32_t *x_next = words_of(e_next);  // patch 0 of sample i+1 (single-patch eval)
     constexpr int CPW = CPB / FB_WARPS;  // clauses per warp
     bool has_ev[CPW];
@@ -245,7 +247,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
                     } else {
                         uint32_t cand;
                         if ((m1a >> b) & 1u) {  // type1a_fb, kernel.cu:410-443
-                            ctr.inc(x & vm & ctr.lt(max_s));
+                            ctr.inc(x & vm & ctr.lt_max(max_s, max_pow2));
                             cand = ~x & vm & ctr.nonzero(zero_s, top2);
                         } else {  // type1b_fb, kernel.cu:453-470
                             cand = vm & ctr.nonzero(zero_s, top2);
@@ -370,7 +372,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
 
 using namespace ytm;
 
-template <int NB, int CPB>
+template <int NB, int CPB, bool IMG>
 static ytm_status launch_b1(const ytm_config *cfg, uint32_t *state, int32_t *weights, const int32_t *bias,
                             const uint32_t *drop, const uint32_t *lits, const int32_t *Y, int64_t N, uint64_t t0,
                             int32_t *cs_ring, int32_t *sel, int32_t *ninc, int32_t *patch_w, uint32_t *ring,
@@ -388,7 +390,7 @@ static ytm_status launch_b1(const ytm_config *cfg, uint32_t *state, int32_t *wei
     if (cfg->patches > 1) smem += (size_t)FB_WARPS * (2 * cfg->words + (cfg->patches + 31) / 32) * 4;
     if (smem > 200 * 1024) return fail(YTM_ERR_UNSUPPORTED, "ytm_train_fit_b1: literal vector too long");
     if (smem > 48 * 1024 &&
-        (rc = cuda_check(cudaFuncSetAttribute(k_fused_b1<NB, CPB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        (rc = cuda_check(cudaFuncSetAttribute(k_fused_b1<NB, CPB, IMG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               (int)smem), "fused b1 smem")))
         return rc;
     cudaLaunchConfig_t lc = {};
@@ -406,7 +408,7 @@ static ytm_status launch_b1(const ytm_config *cfg, uint32_t *state, int32_t *wei
         const int64_t ii = i < 0 ? 0 : i;
         const int upd = i < 0 ? 0 : 1;
         const RoundKeys rk = round_keys(c.seed, (uint32_t)((t0 + (uint64_t)ii) >> 32));  // keys of sample ii
-        if ((rc = cuda_check(cudaLaunchKernelEx(&lc, k_fused_b1<NB, CPB>, c, state, weights, bias, drop, lits, Y, ii,
+        if ((rc = cuda_check(cudaLaunchKernelEx(&lc, k_fused_b1<NB, CPB, IMG>, c, state, weights, bias, drop, lits, Y, ii,
                                                 N, t0, upd, cs_ring, sel, ninc, patch_w, rk, ring),
                              "fused b1 launch")))
             return rc;
@@ -435,10 +437,13 @@ extern "C" ytm_status ytm_train_fit_b1(const ytm_config *cfg, uint32_t *state, i
     if ((rc = cuda_check(cudaMemsetAsync(cs_ring, 0, 3 * (size_t)cfg->n_classes * 4, st), "memset"))) return rc;
     const int cpb = cfg->patches > 1 ? 16 : 64;
     YTM_DISPATCH_PLANES(cfg->planes, {
-        rc = cpb == 16 ? launch_b1<NB, 16>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel, ninc,
-                                           patch_w, ring, st)
-                       : launch_b1<NB, 64>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel, ninc,
-                                           patch_w, ring, st);
+        // bit images only come with several patches (16 clauses per block)
+        rc = ring ? launch_b1<NB, 16, true>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel, ninc,
+                                            patch_w, ring, st)
+             : cpb == 16 ? launch_b1<NB, 16, false>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel,
+                                                    ninc, patch_w, ring, st)
+                         : launch_b1<NB, 64, false>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel,
+                                                    ninc, patch_w, ring, st);
         if (rc) return rc;
     });
     return launch_check("fused b1");

@@ -50,7 +50,8 @@ ytm_status ytm_train_fit_batches(const ytm_config *cfg, uint32_t *state, int32_t
     if (N < 0 || B <= 0) return fail(YTM_ERR_ARG, "bad N or batch size");
     if (N == 0) return YTM_OK;
     if (!lits || !Y || !workspace) return fail(YTM_ERR_ARG, "null pointer");
-    const int64_t PW = (int64_t)cfg->patches * cfg->words;
+    // words per sample of the input: per-patch literal words, or a bit image
+    const int64_t PW = cfg->input_images ? (int64_t)cfg->image_words : (int64_t)cfg->patches * cfg->words;
     const int K = cfg->n_classes;
     char *ws = (char *)workspace;
     int32_t *cs = (int32_t *)ws;  // [B][K] class sums

@@ -140,6 +140,18 @@ __global__ void __launch_bounds__(1024) k_thresholds(const int32_t *__restrict__
     if (threadIdx.x == 0) row_off[B] = base_s;
 }
 
+// Patch literal words u32 [B][P][W] of samples 0..B-1 of the bit images.
+__global__ void k_batch_words(const LitSrc src, int64_t B, uint32_t *__restrict__ out) {
+    const int64_t PW = (int64_t)src.P * src.g.W, total = B * PW;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t n = idx / PW;
+        const int64_t r = idx - n * PW;
+        const int p = (int)(r / src.g.W);
+        out[idx] = src.word<true>(n, p, (int)(r - (int64_t)p * src.g.W));
+    }
+}
+
 template <bool WPC>
 __device__ __forceinline__ void block_sync() {
     if (WPC)
@@ -249,6 +261,8 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
     const uint32_t max_s = (uint32_t)(cfg.max_state + cfg.state_offset);
     const uint32_t zero_s = (uint32_t)cfg.state_offset;
     const bool top2 = NB >= 2 && (uint32_t)cfg.state_offset + 1u == (1u << (NB >= 2 ? NB - 2 : 0));
+    // the stored maximum is 2^(NB-1) + 2^(NB-2) - 1 (power-of-two state counts)
+    const bool max_pow2 = NB >= 3 && max_s == (1u << (NB - 1)) + (1u << (NB >= 2 ? NB - 2 : 0)) - 1u;
     const uint32_t *mycol = colm + (int64_t)k0 * BW;  // non-coalesced: the active samples of the bank's class
 
     for (int kk = tid; kk < nk; kk += nt) wk[kk] = weights[(int64_t)c * K + k0 + kk];
@@ -400,13 +414,13 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                     const int b = b0 + bl;
                     const uint64_t t = t0 + (uint64_t)b;
                     if (ev == EV_T2) {  // type2_fb, kernel.cu:481-506
-                        const uint32_t x = src.word(b, sel_s[bl], w);
+                        const uint32_t x = src.word<false>(b, sel_s[bl], w);
                         ctr.inc(~x & vm & ctr.below_top());
                     } else {
                         uint32_t cand;
                         if (ev == EV_T1A) {  // type1a_fb, kernel.cu:410-443
-                            const uint32_t x = src.word(b, sel_s[bl], w);
-                            ctr.inc(x & vm & ctr.lt(max_s));
+                            const uint32_t x = src.word<false>(b, sel_s[bl], w);
+                            ctr.inc(x & vm & ctr.lt_max(max_s, max_pow2));
                             cand = ~x & vm & ctr.nonzero(zero_s, top2);
                         } else {  // type1b_fb, kernel.cu:453-470
                             cand = vm & ctr.nonzero(zero_s, top2);
@@ -483,6 +497,18 @@ extern "C" ytm_status ytm_train_update_counted(const ytm_config *cfg, uint32_t *
     const size_t smem = update_smem_total(nk, BC);
     if (smem > 227 * 1024) return fail(YTM_ERR_UNSUPPORTED, "too many classes for the feedback kernel");
     // round keys for the batch's samples when they share the counter's high word
+    // the literal source of the feedback: the batch's patch literal words;
+    // from bit images they are formed once into the workspace when they fit
+    LitSrc src = lit_src(cfg, lits);
+    if (cfg->input_images) {
+        uint32_t *pw = (uint32_t *)(ws + l.pwords);
+        const int64_t total = (int64_t)B * cfg->patches * cfg->words;
+        k_batch_words<<<(unsigned)std::min<int64_t>(cdiv(total, 256), (int64_t)sm_count() * 16), 256, 0, st>>>(
+            src, B, pw);
+        if ((rc = launch_check("batch patch words"))) return rc;
+        src.p = pw;
+        src.img = 0;
+    }
     const RoundKeys rk = round_keys(cfg->seed, (uint32_t)(t0 >> 32));
     const int rk_ok = (t0 >> 32) == ((t0 + (uint64_t)B - 1) >> 32);
     const int W = cfg->words;
@@ -491,7 +517,7 @@ extern "C" ytm_status ytm_train_update_counted(const ytm_config *cfg, uint32_t *
     if (B <= 32 && smem_wpc <= 48 * 1024) {
         YTM_DISPATCH_PLANES(cfg->planes, {
             k_update<NB, true><<<(unsigned)cdiv(cfg->clause_count, 8), 256, smem_wpc, st>>>(
-                *cfg, state, weights, thr, drop, lit_src(cfg, lits), B, t0, sel, patch_w, 32, rk, rk_ok, count_patch, pair, amask,
+                *cfg, state, weights, thr, drop, src, B, t0, sel, patch_w, 32, rk, rk_ok, count_patch, pair, amask,
                 colm, row_off,
                 alist, fcm, ctrs);
         });
@@ -505,7 +531,7 @@ extern "C" ytm_status ytm_train_update_counted(const ytm_config *cfg, uint32_t *
                                  "update smem")))
                 return rc;
         }
-        k_update<NB, false><<<cfg->clause_count, tpb, smem, st>>>(*cfg, state, weights, thr, drop, lit_src(cfg, lits), B,
+        k_update<NB, false><<<cfg->clause_count, tpb, smem, st>>>(*cfg, state, weights, thr, drop, src, B,
                                                                   t0, sel,
                                                                   patch_w, BC, rk, rk_ok, count_patch, pair,
                                                                   amask, colm, row_off, alist, fcm, ctrs);
