@@ -618,9 +618,10 @@ def main():
     if ctrs is not None:
         units, calls, words, events = (v / nb for v in ctrs)
         # INT work of one feedback launch in LOP3-equivalent operations:
-        # 4 * planes logic ops per (event, literal word) (a ripple add or
-        # borrow over the planes plus the comparator that selects its
-        # literals) and each literal-mask Philox4x32-7 call weighted by the
+        # 4 * planes logic ops per literal-word operation (a single event, or
+        # a Type Ib run piece: a ripple add, borrow or saturating subtraction
+        # over the planes plus the comparator that selects its literals) and
+        # each Philox4x32-7 call (literal masks, run counts) weighted by the
         # measured LOP3 : Philox throughput ratio
         ops = units * 4 * NB + calls * (lop3 / philox)
         t_min = units * 4 * NB / lop3 + calls / philox
@@ -629,10 +630,10 @@ def main():
                     "frac": ops / upd_s / lop3, "traffic": None, "kernel": "k_update (feedback)",
                     "peak_kind": "measured on this GPU (bench_probe.cu LOP3 probe)",
                     "launch_ms": upd_s * 1000.0, "launches_averaged": nb,
-                    "counters_per_launch": {"event_word_pairs": units, "philox7_calls": calls,
+                    "counters_per_launch": {"literal_word_ops": units, "philox7_calls": calls,
                                             "state_words_streamed": words, "events": events},
                     "philox7_peak_calls_per_s": philox, "lop3_peak_per_s": lop3,
-                    "op_model": "4*planes LOP3 per (event, word) + Philox7 calls x (LOP3 peak / Philox peak)",
+                    "op_model": "4*planes LOP3 per literal-word operation + Philox7 calls x (LOP3 peak / Philox peak)",
                     "t_min_ms": t_min * 1000.0,
                     "hbm": {"algorithmic_bytes": state_bytes + B * W * 4 * cfg.patches,
                             "achieved_gbs": (state_bytes + B * W * 4 * cfg.patches) / upd_s / 1e9,

@@ -81,6 +81,10 @@ typedef struct ytm_config {
                                   Binomial(32, 1/s); entry n = floor(2^32 *
                                   P(count <= n)), saturated at 2^32 - 1     */
     uint64_t q_threshold;      /* negative-class selection, thr / 2^32          */
+    uint32_t run_cdf16[3][33]; /* Type Ib runs of m = 8, 16, 32 events: per
+                                  literal decrement count Binomial(m, 1/s);
+                                  entry d = floor(65536 * P(count <= d)),
+                                  65536 from d = m on                        */
     /* clause shard held by this process */
     int32_t clause_lo;         /* first global clause index                     */
     int32_t clause_count;      /* clauses held (C above)                        */
@@ -245,9 +249,10 @@ ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, int32_t *wei
 
 /* ytm_train_update that also adds measurement counts of its feedback into
  * counters u64[4] (device memory, accumulated, never cleared here):
- * [0] (event, literal word) pairs applied, [1] Philox4x32-7 calls made for
- * literal masks, [2] state words streamed (each a read and a write of every
- * bit plane), [3] feedback events.  Measurement variant with no reference
+ * [0] literal-word operations applied (one per word for each single event
+ * and for each piece of a Type Ib run), [1] Philox4x32-7 calls made for
+ * literal masks and run counts, [2] state words streamed (each a read and a
+ * write of every bit plane), [3] feedback events.  Measurement variant with no reference
  * counterpart; counters == NULL gives ytm_train_update. */
 ytm_status ytm_train_update_counted(const ytm_config *cfg, uint32_t *state, int32_t *weights,
                                     const int32_t *cs, const int32_t *Y, const uint32_t *drop,

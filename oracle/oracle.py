@@ -49,7 +49,7 @@ class OrcCfg(ct.Structure):
         ("seed", ct.c_uint64),
         ("banks", ct.c_int32), ("C", ct.c_int32), ("L", ct.c_int32), ("W", ct.c_int32), ("P", ct.c_int32),
         ("max_state", ct.c_int32), ("half_state", ct.c_int32), ("state_top", ct.c_int32),
-        ("s_cdf", ct.c_uint32 * 32), ("q_thr", ct.c_uint64),
+        ("s_cdf", ct.c_uint32 * 32), ("q_thr", ct.c_uint64), ("run_cdf16", (ct.c_uint32 * 33) * 3),
         ("one_negative", ct.c_int32), ("count_empty", ct.c_int32),
     ]
 
@@ -71,6 +71,7 @@ def _declare(L):
     L.orc_philox4x32.argtypes = [_P, _P, ct.c_int, _P]
     L.orc_smask_word.argtypes = [ct.POINTER(OrcCfg), ct.c_uint32, _U64, ct.c_uint32, ct.c_uint32]
     L.orc_smask_word.restype = ct.c_uint32
+    L.orc_run_counts.argtypes = [ct.POINTER(OrcCfg), ct.c_uint32, _U64, ct.c_uint32, ct.c_uint32, ct.c_int, _P]
     L.orc_smask_count.argtypes = [ct.c_int]
     L.orc_smask_count.restype = ct.c_uint64
     L.orc_update_threshold.argtypes = [_I32, _I32]
@@ -198,6 +199,13 @@ class Oracle:
 
     def smask_word(self, clause, t, k, w):
         return int(lib().orc_smask_word(self._cfg(), clause, t, k, w))
+
+    def run_counts(self, clause, t, k, w, mi):
+        """Per-literal decrement counts of a Type Ib run piece of 8 << mi
+        events for word w (u32 [32])."""
+        out = np.zeros(32, np.uint32)
+        lib().orc_run_counts(self._cfg(), clause, t, k, w, int(mi), _ptr(out))
+        return out
 
     @staticmethod
     def smask_count(on: bool) -> int:

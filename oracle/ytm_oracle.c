@@ -45,6 +45,7 @@ typedef struct orc_cfg {
     int32_t max_state, half_state, state_top;
     uint32_t s_cdf[32];
     uint64_t q_thr;
+    uint32_t run_cdf16[3][33];
     /* rule variants of the reference's CPU TM, pytm/base.py (0 = cutm rules) */
     int32_t one_negative; /* one uniformly chosen negative class per sample, true class first (base.py:139-143) */
     int32_t count_empty;  /* inference counts clauses without includes (base.py:59-67) */
@@ -75,6 +76,35 @@ static void count_cdf(double s, uint32_t cdf[32]) {
         const double v = floor(acc * 4294967296.0);
         cdf[n] = v >= 4294967295.0 ? 0xFFFFFFFFu : (uint32_t)v;
         pmf = pmf * (double)(32 - n) / (double)(n + 1) * p / q;
+    }
+}
+
+/* Type Ib runs (see orc_train_update): for m = 8, 16, 32 events the number
+ * of decrements of one literal is Binomial(m, p), p = 1/s; entry d of row mi
+ * is floor(65536 * P(count <= d)), 65536 from d = m on; the same pmf
+ * recurrence in IEEE double. */
+static const int RUN_SIZES[3] = {8, 16, 32};
+
+static void run_cdf(double s, uint32_t out[3][33]) {
+    double p = 1.0 / s;
+    if (!(p > 0.0)) p = 0.0;
+    if (p > 1.0) p = 1.0;
+    const double q = 1.0 - p;
+    for (int mi = 0; mi < 3; ++mi) {
+        const int m = RUN_SIZES[mi];
+        for (int d = 0; d < 33; ++d) out[mi][d] = 65536u;
+        if (!(q > 0.0)) { /* p = 1: every event decrements */
+            for (int d = 0; d < m; ++d) out[mi][d] = 0u;
+            continue;
+        }
+        double pmf = 1.0, acc = 0.0;
+        for (int i = 0; i < m; ++i) pmf *= q;
+        for (int d = 0; d < m; ++d) {
+            acc += pmf;
+            const double v = floor(acc * 65536.0);
+            out[mi][d] = v >= 65536.0 ? 65536u : (uint32_t)v;
+            pmf = pmf * (double)(m - d) / (double)(d + 1) * p / q;
+        }
     }
 }
 
@@ -117,6 +147,7 @@ int orc_cfg_init(orc_cfg *c, int32_t clauses_per_class, int32_t T, double s, int
         c->state_top = p + c->half_state;
     }
     count_cdf(s, c->s_cdf);
+    run_cdf(s, c->run_cdf16);
     {
         double qp = c->q / (double)(K - 1 > 1 ? K - 1 : 1); /* kernel.cu:32 */
         if (qp >= 1.0) c->q_thr = 4294967296ull;
@@ -512,6 +543,44 @@ static void type1b(const orc_cfg *c, uint32_t *st, uint32_t g, uint64_t t, uint3
     }
 }
 
+/* A run of m (8, 16 or 32) consecutive Type Ib events of one clause, which
+ * the reference applies one by one (type1b_fb, kernel.cu:453-470: each
+ * decrements every literal with st > 0 with probability 1/s).  Decrements
+ * with a floor at 0 commute, so the run leaves st - d clamped at 0, d the
+ * literal's number of successes, Binomial(m, 1/s): drawn per literal by
+ * inverse CDF from a 16-bit uniform.  The uniforms of word w are the 16-bit
+ * halves of four Philox4x32-7 calls at sub-indices 0x40000000 | 4w | i keyed
+ * on the run's first event (t, k): literal j of the word takes half j & 1 of
+ * word (j >> 1) & 3 of call j >> 3. */
+static void type1b_run(const orc_cfg *c, uint32_t *st, uint32_t g, uint64_t t, uint32_t k, int mi) {
+    const int L = c->L, m = RUN_SIZES[mi];
+    for (int w = 0; w * 32 < L; ++w) {
+        uint32_t R[4][4];
+        for (uint32_t i = 0; i < 4; ++i)
+            draw_r(c, g, t, 0x40000000u | ((uint32_t)w << 2) | i, TAG_SMASK, k, 7, R[i]);
+        for (int j = 0; j < 32 && w * 32 + j < L; ++j) {
+            const uint32_t u = (R[j >> 3][(j >> 1) & 3] >> (16 * (j & 1))) & 0xFFFFu;
+            int d = 0;
+            while (d < m && u >= c->run_cdf16[mi][d]) ++d;
+            uint32_t *x = &st[w * 32 + j];
+            *x = *x > (uint32_t)d ? *x - (uint32_t)d : 0u;
+        }
+    }
+}
+
+/* The per-literal decrement counts type1b_run draws for word w (test hook). */
+void orc_run_counts(const orc_cfg *c, uint32_t g, uint64_t t, uint32_t k, uint32_t w, int mi, uint32_t out[32]) {
+    const int m = RUN_SIZES[mi];
+    uint32_t R[4][4];
+    for (uint32_t i = 0; i < 4; ++i) draw_r(c, g, t, 0x40000000u | (w << 2) | i, TAG_SMASK, k, 7, R[i]);
+    for (int j = 0; j < 32; ++j) {
+        const uint32_t u = (R[j >> 3][(j >> 1) & 3] >> (16 * (j & 1))) & 0xFFFFu;
+        int d = 0;
+        while (d < m && u >= c->run_cdf16[mi][d]) ++d;
+        out[j] = (uint32_t)d;
+    }
+}
+
 /* type2_fb, kernel.cu:481-506.  The reference has no upper check; state_top
  * lies above every value one sample can reach, so the cap only bounds
  * mini-batches. */
@@ -545,58 +614,96 @@ static void orc_pair(const orc_cfg *c, const int32_t *Yrow, uint64_t t, int *kt,
 /* Part 2 of a batch: clause_update, kernel.cu:531-613, for every clause of the
  * shard and every sample of the batch in order.  cs [B][K] are the summed class
  * sums, Y [B][K] the +-T targets, sel [B][nc] and ninc [nc] from part 1. */
+/* Feedback of a batch (clause_update, kernel.cu:531-613, per sample in
+ * order).  Per clause, the events of each 32-sample window of the batch are
+ * decided first (the decisions read only the batch-start fired bits and
+ * include counts, and the weights, which they update), then applied in
+ * feedback order; maximal runs of consecutive Type Ib events inside a window
+ * are applied in pieces of 32, 16 and 8 events (greedy, from the run's start)
+ * with type1b_run, the rest one by one. */
+enum { EV_T1A = 1, EV_T1B = 2, EV_T2 = 3 };
+typedef struct { int32_t b, k, type; } orc_event;
+
 void orc_train_update(const orc_cfg *c, int32_t lo, int32_t nc, uint32_t *ta, int32_t *w,
                       const int32_t *cs, const int32_t *Y, const uint32_t *drop, const uint32_t *lits,
                       int32_t B, uint64_t t0, const int32_t *sel, const int32_t *ninc) {
     const int K = c->K, L = c->L, W = c->W, P = c->P;
-#pragma omp parallel for schedule(dynamic, 4)
+#pragma omp parallel
+    {
+    orc_event *ev = (orc_event *)malloc(sizeof(orc_event) * 32 * (size_t)(K > 2 ? K : 2));
+#pragma omp for schedule(dynamic, 4)
     for (int32_t i = 0; i < nc; ++i) {
         if (drop && drop[i] == 1) continue; /* kernel.cu:555 */
         uint32_t g = (uint32_t)(lo + i);
         uint32_t *st = ta + (int64_t)i * L;
-        for (int32_t b = 0; b < B; ++b) {
-            uint64_t t = t0 + (uint64_t)b;
-            int32_t sp = sel[(int64_t)b * nc + i];
-            int fired = sp > -1; /* kernel.cu:558 */
-            const uint32_t *x = fired ? lits + ((int64_t)b * P + sp) * W : NULL;
-            int k0 = c->coalesced ? 0 : clause_class(c, (int32_t)g);
-            int k1 = c->coalesced ? K : k0 + 1;
-            int seq[2], nseq = 0;
-            if (c->one_negative) { /* the true class, then one other class */
-                int kt, ko;
-                orc_pair(c, Y + (int64_t)b * K, t, &kt, &ko);
-                if (kt >= k0 && kt < k1) seq[nseq++] = kt;
-                if (ko >= k0 && ko < k1) seq[nseq++] = ko;
-            }
-            int nk = c->one_negative ? nseq : k1 - k0;
-            for (int kq = 0; kq < nk; ++kq) { /* kernel.cu:563-568 */
-                const int k = c->one_negative ? seq[kq] : k0 + kq;
-                int32_t v = clip_cs(c, cs[(int64_t)b * K + k]);
-                int32_t y = Y[(int64_t)b * K + k];
-                int target = 1 - 2 * (v > y); /* kernel.cu:571 */
-                uint32_t r[4];
-                draw(c, g, t, 0, TAG_CLASS, (uint32_t)k, r);
-                if (!c->one_negative && target == -1 && !((uint64_t)r[0] < c->q_thr)) continue; /* kernel.cu:573 */
-                int upd = (uint64_t)r[1] < orc_update_threshold(y, v);   /* kernel.cu:582 */
-                int32_t *lw = &w[(int64_t)i * K + k];
-                int sign = (*lw >= 0) - (*lw < 0);
-                int ok = fired && ninc[i] <= c->max_included;
-                int t1a = target * sign > 0 && ok;
-                int t1b = target * sign > 0 && !ok;
-                int t2 = target * sign < 0 && fired;
-                if (!upd) continue;
-                if (t1a) {
-                    *lw += sign;
-                    type1a(c, st, x, g, t, (uint32_t)k);
-                } else if (t1b) {
-                    type1b(c, st, g, t, (uint32_t)k);
-                } else if (t2) {
-                    *lw -= sign;
-                    if (!c->negative_polarity && *lw < 1) *lw = 1; /* kernel.cu:603-606 */
-                    type2(c, st, x);
+        for (int32_t b0 = 0; b0 < B; b0 += 32) {
+            int nev = 0;
+            for (int32_t b = b0; b < B && b < b0 + 32; ++b) {
+                uint64_t t = t0 + (uint64_t)b;
+                int32_t sp = sel[(int64_t)b * nc + i];
+                int fired = sp > -1; /* kernel.cu:558 */
+                int k0 = c->coalesced ? 0 : clause_class(c, (int32_t)g);
+                int k1 = c->coalesced ? K : k0 + 1;
+                int seq[2], nseq = 0;
+                if (c->one_negative) { /* the true class, then one other class */
+                    int kt, ko;
+                    orc_pair(c, Y + (int64_t)b * K, t, &kt, &ko);
+                    if (kt >= k0 && kt < k1) seq[nseq++] = kt;
+                    if (ko >= k0 && ko < k1) seq[nseq++] = ko;
+                }
+                int nk = c->one_negative ? nseq : k1 - k0;
+                for (int kq = 0; kq < nk; ++kq) { /* kernel.cu:563-568 */
+                    const int k = c->one_negative ? seq[kq] : k0 + kq;
+                    int32_t v = clip_cs(c, cs[(int64_t)b * K + k]);
+                    int32_t y = Y[(int64_t)b * K + k];
+                    int target = 1 - 2 * (v > y); /* kernel.cu:571 */
+                    uint32_t r[4];
+                    draw(c, g, t, 0, TAG_CLASS, (uint32_t)k, r);
+                    if (!c->one_negative && target == -1 && !((uint64_t)r[0] < c->q_thr)) continue; /* kernel.cu:573 */
+                    int upd = (uint64_t)r[1] < orc_update_threshold(y, v);   /* kernel.cu:582 */
+                    int32_t *lw = &w[(int64_t)i * K + k];
+                    int sign = (*lw >= 0) - (*lw < 0);
+                    int ok = fired && ninc[i] <= c->max_included;
+                    int t1a = target * sign > 0 && ok;
+                    int t1b = target * sign > 0 && !ok;
+                    int t2 = target * sign < 0 && fired;
+                    if (!upd) continue;
+                    if (t1a) {
+                        *lw += sign;
+                        ev[nev++] = (orc_event){b, k, EV_T1A};
+                    } else if (t1b) {
+                        ev[nev++] = (orc_event){b, k, EV_T1B};
+                    } else if (t2) {
+                        *lw -= sign;
+                        if (!c->negative_polarity && *lw < 1) *lw = 1; /* kernel.cu:603-606 */
+                        ev[nev++] = (orc_event){b, k, EV_T2};
+                    }
                 }
             }
+            for (int e = 0; e < nev;) {
+                const orc_event *E = &ev[e];
+                const uint64_t t = t0 + (uint64_t)E->b;
+                if (E->type == EV_T1B) {
+                    int run = 0;
+                    while (e + run < nev && run < 32 && ev[e + run].type == EV_T1B) ++run;
+                    const int mi = run >= 32 ? 2 : (run >= 16 ? 1 : (run >= 8 ? 0 : -1));
+                    if (mi >= 0) {
+                        type1b_run(c, st, g, t, (uint32_t)E->k, mi);
+                        e += RUN_SIZES[mi];
+                        continue;
+                    }
+                    type1b(c, st, g, t, (uint32_t)E->k);
+                } else {
+                    const int32_t sp = sel[(int64_t)E->b * nc + i];
+                    const uint32_t *x = lits + ((int64_t)E->b * P + sp) * W;
+                    if (E->type == EV_T1A) type1a(c, st, x, g, t, (uint32_t)E->k);
+                    else type2(c, st, x);
+                }
+                ++e;
+            }
         }
+    }
+    free(ev);
     }
 }
 

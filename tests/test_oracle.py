@@ -167,3 +167,43 @@ def test_smask_distribution():
 def test_oracle_threads():
     O.set_threads(2)
     assert O.get_threads() == 2
+
+
+def _run_spec(o, clause, t, k, w, mi):
+    """Type Ib run counts restated from their definition: literal j's 16-bit
+    uniform is half j & 1 of word (j >> 1) & 3 of the Philox4x32-7 call
+    j >> 3 at sub-index 0x40000000 | 4w | (j >> 3); its count is the first d
+    with u < cdf[d]."""
+    seed = o.cfg.seed
+    key = [seed & 0xFFFFFFFF, ((seed >> 32) ^ (t >> 32)) & 0xFFFFFFFF]
+    calls = [[int(v) for v in O.philox4x32([clause, t & 0xFFFFFFFF, 0x40000000 | (w << 2) | i, 2 | (k << 2)],
+                                            key, 7)] for i in range(4)]
+    cdf = list(o.cfg.run_cdf16[mi])
+    m = 8 << mi
+    out = []
+    for j in range(32):
+        u = (calls[j >> 3][(j >> 1) & 3] >> (16 * (j & 1))) & 0xFFFF
+        d = 0
+        while d < m and u >= cdf[d]:
+            d += 1
+        out.append(d)
+    return out
+
+
+@pytest.mark.parametrize("s", [1.0, 3.0, 10.0, 20.0])
+def test_type1b_run_counts(s):
+    """Definition, and the count distribution Binomial(m, 1/s) of each run size."""
+    from math import comb
+    o = O.Oracle(number_of_clauses_per_class=4, T=10, s=s, dim=(4, 1, 1), n_classes=3, seed=3 + 2**36)
+    for mi in range(3):
+        m = 8 << mi
+        assert list(o.run_counts(2, 2**32 + 5, 1, 7, mi)) == _run_spec(o, 2, 2**32 + 5, 1, 7, mi)
+        d = np.concatenate([o.run_counts(c, t, 2, w, mi) for c in range(3) for t in range(60) for w in range(4)])
+        if s == 1.0:
+            assert (d == m).all()
+            continue
+        p = 1 / s
+        hist = np.bincount(d, minlength=m + 1)
+        for j in range(min(m, 12) + 1):
+            want = comb(m, j) * p ** j * (1 - p) ** (m - j) * len(d)
+            assert abs(hist[j] - want) < 5 * np.sqrt(want) + 6, (mi, j, hist[j], want)

@@ -171,6 +171,31 @@ ytm_status ytm_config_init(ytm_config *cfg, int32_t clauses_per_class, int32_t T
             }
         }
     }
+    // Type Ib run tables: per literal Binomial(m, p) decrement counts for runs
+    // of m = 8, 16, 32 events; entry d = floor(65536 * P(count <= d)),
+    // 65536 from d = m on, from the same pmf recurrence
+    {
+        double p = 1.0 / s;
+        if (!(p > 0.0)) p = 0.0;
+        if (p > 1.0) p = 1.0;
+        const double qq = 1.0 - p;
+        for (int mi = 0; mi < 3; ++mi) {
+            const int m = 8 << mi;
+            for (int d = 0; d < 33; ++d) cfg->run_cdf16[mi][d] = 65536u;
+            if (!(qq > 0.0)) {
+                for (int d = 0; d < m; ++d) cfg->run_cdf16[mi][d] = 0u;
+                continue;
+            }
+            double pmf = 1.0, acc = 0.0;
+            for (int i = 0; i < m; ++i) pmf *= qq;
+            for (int d = 0; d < m; ++d) {
+                acc += pmf;
+                const double v = floor(acc * 65536.0);
+                cfg->run_cdf16[mi][d] = v >= 65536.0 ? 65536u : (uint32_t)v;
+                pmf = pmf * (double)(m - d) / (double)(d + 1) * p / qq;
+            }
+        }
+    }
     {
         double qp = cfg->q / (double)(n_classes - 1 > 1 ? n_classes - 1 : 1);  // kernel.cu:32
         if (qp >= 1.0) cfg->q_threshold = 4294967296ull;

@@ -183,6 +183,41 @@ __device__ __forceinline__ uint32_t smask_word_rk(const ytm_config &cfg, const R
     return smask_place(cfg, [&](uint32_t j) { return draw_rk<7>(rk, g, t, w * 4u + j, TAG_SMASK, k); }, calls);
 }
 
+// A run of m = 8 << mi consecutive Type Ib events of one clause (type1b_fb,
+// kernel.cu:453-470, applied by the reference one event at a time: each
+// decrements every literal with a positive state with probability 1/s).
+// Decrements with a floor at 0 commute, so the run leaves state - d clamped
+// at 0, with d the literal's number of successes, Binomial(m, 1/s), drawn by
+// inverse CDF from a 16-bit uniform: literal j of word w takes half j & 1 of
+// word (j >> 1) & 3 of the Philox4x32-7 call j >> 3, at sub-index
+// 0x40000000 | 4w | (j >> 3), keyed on the run's first event.  D receives
+// the counts as bit planes (d <= 32 needs 6).  The first six comparisons are
+// branch-free; only counts of 6 or more continue in the loop.
+template <typename DrawFn>
+__device__ __forceinline__ void run_counts(const ytm_config &cfg, int mi, DrawFn drawi, uint32_t (&D)[6],
+                                           uint32_t &calls) {
+#pragma unroll
+    for (int b = 0; b < 6; ++b) D[b] = 0u;
+    const int m = 8 << mi;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const u32x4 r = drawi((uint32_t)i);
+        ++calls;
+        const uint32_t R[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const uint32_t u = (R[q >> 1] >> (16 * (q & 1))) & 0xFFFFu;
+            uint32_t d = 0;
+#pragma unroll
+            for (int e = 0; e < 6; ++e) d += u >= cfg.run_cdf16[mi][e] ? 1u : 0u;
+            if (d == 6u)
+                while ((int)d < m && u >= cfg.run_cdf16[mi][d]) ++d;
+#pragma unroll
+            for (int b = 0; b < 6; ++b) D[b] |= ((d >> b) & 1u) << (i * 8 + q);
+        }
+    }
+}
+
 // pytm's per-sample pick (pytm/base.py:139-141): the true class (the first
 // with a positive target, -1 if none) and one other class drawn uniformly
 // among the rest from the counter (clause 0xFFFFFFFF, t, 1, CLASS).
@@ -279,6 +314,39 @@ struct Counter {
     __device__ __forceinline__ uint32_t nonzero(uint32_t v, bool top2) const {
         if (NB >= 2 && top2) return p[NB - 1] | p[NB - 2];
         return ne(v);
+    }
+    // stored value := max(z, value - D) for the literals of D (bit planes,
+    // six of them): a run of Type Ib decrements with the floor at state 0
+    // (stored value z = offset).  top2: z + 1 = 2^(NB-2), so a value is at
+    // most z exactly when its two top planes are clear.
+    __device__ __forceinline__ void sub_floor(const uint32_t (&D)[6], uint32_t z, bool top2) {
+        uint32_t q[NB], br = 0u;
+#pragma unroll
+        for (int i = 0; i < NB; ++i) {
+            const uint32_t d = i < 6 ? D[i] : 0u;
+            q[i] = p[i] ^ d ^ br;
+            br = (~p[i] & (d | br)) | (d & br);
+        }
+        uint32_t low;  // literals whose difference is below z + 1 (or negative)
+        if (NB >= 3 && top2) {
+            low = ~(q[NB - 1] | q[NB - 2]);
+        } else {
+            uint32_t l = 0u, e = 0xFFFFFFFFu;
+            const uint32_t v = z + 1u;
+#pragma unroll
+            for (int i = NB - 1; i >= 0; --i) {
+                if ((v >> i) & 1u) {
+                    l |= e & ~q[i];
+                    e &= q[i];
+                } else {
+                    e &= ~q[i];
+                }
+            }
+            low = l;
+        }
+        low |= br;
+#pragma unroll
+        for (int i = 0; i < NB; ++i) p[i] = (q[i] & ~low) | (((z >> i) & 1u) ? low : 0u);
     }
     __device__ __forceinline__ uint32_t below_top() const {
         uint32_t a = 0xFFFFFFFFu;

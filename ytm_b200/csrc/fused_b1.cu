@@ -233,6 +233,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
 #pragma unroll
             for (int b = 0; b < NB; ++b) ctr.p[b] = state[((int64_t)b * C + c) * W + w];
             const uint32_t x = sc >= 0 ? x_cur[w] : 0u;
+            int skip = 0;  // events of a Type Ib run piece already applied
             for (int kb = 0; kb < KB; ++kb) {
                 uint32_t m = ev[kb * 3];
                 const uint32_t m1a = ev[kb * 3 + 1], m2 = ev[kb * 3 + 2];
@@ -242,6 +243,38 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
                     int b = __ffs(m) - 1;
                     if (first >= 0 && first < 32 && ((m >> first) & 1u)) b = first;
                     m &= ~(1u << b);
+                    if (skip) {
+                        --skip;
+                        continue;
+                    }
+                    if (!cfg.one_negative && !(((m1a | m2) >> b) & 1u)) {
+                        // Type Ib: the run of consecutive Type Ib events from
+                        // here (classes in order; one sample is one window)
+                        int run = 1;
+                        {
+                            uint32_t rem = m;
+                            uint32_t stop = (m1a | m2) & rem;
+                            for (int kb2 = kb;;) {
+                                run += __popc(stop ? (rem & ((stop & (0u - stop)) - 1u)) : rem);
+                                if (stop || run >= 32 || ++kb2 >= KB) break;
+                                rem = ev[kb2 * 3];
+                                stop = (ev[kb2 * 3 + 1] | ev[kb2 * 3 + 2]) & rem;
+                            }
+                        }
+                        if (run >= 8) {
+                            const int mi = run >= 32 ? 2 : (run >= 16 ? 1 : 0);
+                            const uint32_t kk = (uint32_t)(k0 + kb * 32 + b);
+                            uint32_t D[6];
+                            run_counts(cfg, mi, [&](uint32_t ii) {
+                                return draw_rk<7>(rk, g, t, 0x40000000u | ((uint32_t)w << 2) | ii, TAG_SMASK, kk);
+                            }, D, n_calls);
+#pragma unroll
+                            for (int ii = 0; ii < 6; ++ii) D[ii] &= vm;
+                            ctr.sub_floor(D, zero_s, top2);
+                            skip = (8 << mi) - 1;
+                            continue;
+                        }
+                    }
                     if ((m2 >> b) & 1u) {  // type2_fb, kernel.cu:481-506
                         ctr.inc(~x & vm & ctr.below_top());
                     } else {

@@ -400,7 +400,6 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
         if (nev > 0) {
             if (counters && tid == 0) n_events += (uint32_t)nev;
             for (int w = tid; w < W; w += nt) {
-                n_units += (uint32_t)nev;
                 ++n_words;
                 Counter<NB> ctr;
 #pragma unroll
@@ -413,6 +412,31 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                     const int k = k0 + (int)(ent & 0x3FFFFFu);
                     const int b = b0 + bl;
                     const uint64_t t = t0 + (uint64_t)b;
+                    ++n_units;
+                    if (ev == EV_T1B) {
+                        // a run of consecutive Type Ib events inside this
+                        // 32-sample window: pieces of 32, 16, 8 from its start
+                        int run = 1;
+                        while (run < 32 && e + run < nev) {
+                            const uint32_t en = list[e + run];
+                            if (((en >> 22) & 3u) != EV_T1B || ((en >> 24) >> 5) != ((uint32_t)bl >> 5)) break;
+                            ++run;
+                        }
+                        if (run >= 8) {
+                            const int mi = run >= 32 ? 2 : (run >= 16 ? 1 : 0);
+                            uint32_t D[6];
+                            run_counts(cfg, mi, [&](uint32_t i) {
+                                const uint32_t sub = 0x40000000u | ((uint32_t)w << 2) | i;
+                                return rk_ok ? draw_rk<7>(rk, g, t, sub, TAG_SMASK, (uint32_t)k)
+                                             : draw<7>(cfg.seed, g, t, sub, TAG_SMASK, (uint32_t)k);
+                            }, D, n_calls);
+#pragma unroll
+                            for (int i = 0; i < 6; ++i) D[i] &= vm;
+                            ctr.sub_floor(D, zero_s, top2);
+                            e += (8 << mi) - 1;
+                            continue;
+                        }
+                    }
                     if (ev == EV_T2) {  // type2_fb, kernel.cu:481-506
                         const uint32_t x = src.word<false>(b, sel_s[bl], w);
                         ctr.inc(~x & vm & ctr.below_top());
