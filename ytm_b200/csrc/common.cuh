@@ -199,8 +199,8 @@ __device__ __forceinline__ void run_counts(const ytm_config &cfg, int mi, DrawFn
 #pragma unroll
     for (int b = 0; b < 6; ++b) D[b] = 0u;
     const int m = 8 << mi;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
+#pragma unroll 1
+    for (int i = 0; i < 4; ++i) {  // not unrolled: keeps the feedback loop's code small
         const u32x4 r = drawi((uint32_t)i);
         ++calls;
         const uint32_t R[4] = {r.x, r.y, r.z, r.w};

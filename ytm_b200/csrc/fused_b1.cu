@@ -25,6 +25,9 @@ namespace ytm {
 // single-patch models, 16 for convolutional ones, whose per-clause patch scan
 // wants more blocks in flight (measured: config 3 17k -> 31k samples/s)
 constexpr int FB_WARPS = 8;
+#ifndef YTM_B1_CPB
+#define YTM_B1_CPB 64  // clauses per block of single-patch models (a multiple of 8)
+#endif
 
 
 B1Ws b1_ws_layout(const ytm_config *cfg) {
@@ -468,14 +471,14 @@ extern "C" ytm_status ytm_train_fit_b1(const ytm_config *cfg, uint32_t *state, i
     int32_t *ninc = (int32_t *)(ws + l.ninc);
     uint32_t *ring = cfg->input_images ? (uint32_t *)(ws + l.ring) : nullptr;
     if ((rc = cuda_check(cudaMemsetAsync(cs_ring, 0, 3 * (size_t)cfg->n_classes * 4, st), "memset"))) return rc;
-    const int cpb = cfg->patches > 1 ? 16 : 64;
+    const int cpb = cfg->patches > 1 ? 16 : YTM_B1_CPB;
     YTM_DISPATCH_PLANES(cfg->planes, {
         // bit images only come with several patches (16 clauses per block)
         rc = ring ? launch_b1<NB, 16, true>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel, ninc,
                                             patch_w, ring, st)
              : cpb == 16 ? launch_b1<NB, 16, false>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel,
                                                     ninc, patch_w, ring, st)
-                         : launch_b1<NB, 64, false>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel,
+                         : launch_b1<NB, YTM_B1_CPB, false>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel,
                                                     ninc, patch_w, ring, st);
         if (rc) return rc;
     });

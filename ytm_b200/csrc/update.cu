@@ -152,6 +152,22 @@ __global__ void k_batch_words(const LitSrc src, int64_t B, uint32_t *__restrict_
     }
 }
 
+// Optional per-phase cycle counts of the feedback kernel (measurement
+// builds with -DYTM_PHASE_TIMING only: counters[4..9] receive the cycles
+// thread 0 of each clause spent in each phase).
+#ifdef YTM_PHASE_TIMING
+#define YTM_PHASE_START() long long ph_last_ = clock64()
+#define YTM_PHASE(i)                                       \
+    do {                                                   \
+        const long long ph_now_ = clock64();               \
+        ph_cyc[i] += (unsigned long long)(ph_now_ - ph_last_); \
+        ph_last_ = ph_now_;                                \
+    } while (0)
+#else
+#define YTM_PHASE_START() ((void)0)
+#define YTM_PHASE(i) ((void)0)
+#endif
+
 template <bool WPC>
 __device__ __forceinline__ void block_sync() {
     if (WPC)
@@ -258,6 +274,9 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
     // measurement counters: (event, word) pairs applied, Philox4x32-7 calls
     // of the literal masks, state words streamed, events
     uint32_t n_units = 0, n_calls = 0, n_words = 0, n_events = 0;
+#ifdef YTM_PHASE_TIMING
+    unsigned long long ph_cyc[6] = {0, 0, 0, 0, 0, 0};
+#endif
     const uint32_t max_s = (uint32_t)(cfg.max_state + cfg.state_offset);
     const uint32_t zero_s = (uint32_t)cfg.state_offset;
     const bool top2 = NB >= 2 && (uint32_t)cfg.state_offset + 1u == (1u << (NB >= 2 ? NB - 2 : 0));
@@ -268,6 +287,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
     for (int kk = tid; kk < nk; kk += nt) wk[kk] = weights[(int64_t)c * K + k0 + kk];
 
     for (int b0 = 0; b0 < B; b0 += BC) {  // BC is a multiple of 32
+        YTM_PHASE_START();
         const int bc = min(BC, B - b0);
         for (int q0 = tid & ~31; q0 < bc; q0 += nt) {  // warp-uniform
             const int q = q0 + lane;
@@ -286,6 +306,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
             if (lane == 0) fm[q0 >> 5] = f;
         }
         block_sync<WPC>();
+        YTM_PHASE(0);
         // A class none of whose active samples fired the clause is simple:
         // its events are Type Ib or none, fixed by the weight's sign, and its
         // weight stays as it is for the chunk (kernel.cu:584-606).
@@ -296,6 +317,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
             simple[kk] = hit == 0u;
         }
         block_sync<WPC>();
+        YTM_PHASE(1);
         const int lo = cfg.coalesced ? row_off[b0] : 0, hi = cfg.coalesced ? row_off[b0 + bc] : 0;
         // 1a. the Q-selection and update draws of the active pairs, in
         //     parallel: 1 = update with target +1, 2 = with target -1; simple
@@ -316,6 +338,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                     evt[bl] = a;
                 }
         block_sync<WPC>();
+        YTM_PHASE(2);
         // 1b. feedback types, class-parallel and sample-sequential over the
         //     class's active samples (weights evolve)
         for (int kk = tid; kk < nk; kk += nt) {
@@ -349,10 +372,57 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
             wk[kk] = wv;
         }
         block_sync<WPC>();
+        YTM_PHASE(3);
         // 2. the events in feedback order: a lane per sample counts and then
         //    writes its events (classes in order; pytm's rules: the true
         //    class first); only active pairs hold event types
-        if (tid < 32) {  // WPC: the whole warp
+        if (!WPC && cfg.coalesced && !cfg.one_negative) {
+            // all threads: a thread per (sample, 32 classes) unit in feedback
+            // order, an exclusive scan of their event counts over the block,
+            // then each writes its events in class order
+            __shared__ int psum_s[8];
+            const int nwarp = nt >> 5, wid = tid >> 5;
+            const int units = bc * KWm;
+            int base = 0;
+            for (int u0 = 0; u0 < units; u0 += nt) {
+                const int u = u0 + tid;
+                uint32_t em = 0u;
+                int row = 0, m = 0;
+                if (u < units) {
+                    row = u / KWm;
+                    m = u - row * KWm;
+                    for (uint32_t v = amask[(int64_t)(b0 + row) * KWm + m]; v; v &= v - 1u) {
+                        const int bit = __ffs(v) - 1;
+                        if (evt[row * nk + m * 32 + bit] != EV_NONE) em |= 1u << bit;
+                    }
+                }
+                const int n = __popc(em);
+                int incl = n;
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                    if (lane >= o) incl += v;
+                }
+                if (lane == 31) psum_s[wid] = incl;
+                __syncthreads();
+                if (tid < 32) {
+                    int v = lane < nwarp ? psum_s[lane] : 0;
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const int x = __shfl_up_sync(0xFFFFFFFFu, v, o);
+                        if (lane >= o) v += x;
+                    }
+                    if (lane < nwarp) psum_s[lane] = v;
+                }
+                __syncthreads();
+                int pos = base + (wid ? psum_s[wid - 1] : 0) + incl - n;
+                for (uint32_t v = em; v; v &= v - 1u) {
+                    const int k = m * 32 + __ffs(v) - 1;
+                    list[pos++] = ((uint32_t)row << 24) | ((uint32_t)evt[row * nk + k] << 22) | (uint32_t)k;
+                }
+                base += psum_s[nwarp - 1];
+                __syncthreads();
+            }
+            if (tid == 0) cnt[0] = base;
+        } else if (tid < 32) {  // WPC: the whole warp
             int base = 0;
             for (int r0 = 0; r0 < bc; r0 += 32) {
                 const int row = r0 + lane;
@@ -395,6 +465,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
             if (lane == 0) cnt[0] = base;
         }
         block_sync<WPC>();
+        YTM_PHASE(4);
         const int nev = cnt[0];
         // 3. stream the literal words
         if (nev > 0) {
@@ -459,8 +530,13 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
             }
         }
         block_sync<WPC>();
+        YTM_PHASE(5);
     }
     for (int kk = tid; kk < nk; kk += nt) weights[(int64_t)c * K + k0 + kk] = wk[kk];
+#ifdef YTM_PHASE_TIMING
+    if (counters && tid == 0)
+        for (int i = 0; i < 6; ++i) atomicAdd(&counters[4 + i], ph_cyc[i]);
+#endif
     if (counters) {
         unsigned long long v[4] = {n_units, n_calls, n_words, n_events};
 #pragma unroll
