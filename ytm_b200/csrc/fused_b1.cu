@@ -21,12 +21,15 @@
 
 namespace ytm {
 
-// warps per block; clauses per block (CPB) is a template parameter: 64 for
-// single-patch models, 16 for convolutional ones, whose per-clause patch scan
-// wants more blocks in flight (measured: config 3 17k -> 31k samples/s)
+// warps per block; clauses per block (CPB) is a template parameter:
+// YTM_B1_CPB for single-patch models (measured on configuration 1: 48 clauses
+// 10.6 us per sample, 64 13.3, 32 13.2, 128 23.5 — 48 keeps the 417 blocks
+// of 20,000 clauses resident in one wave), 16 for convolutional ones, whose
+// per-clause patch scan wants more blocks in flight (measured: config 3 17k ->
+// 31k samples/s)
 constexpr int FB_WARPS = 8;
 #ifndef YTM_B1_CPB
-#define YTM_B1_CPB 64  // clauses per block of single-patch models (a multiple of 8)
+#define YTM_B1_CPB 48  // a multiple of FB_WARPS
 #endif
 
 
