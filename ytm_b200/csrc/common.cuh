@@ -204,6 +204,9 @@ __device__ __forceinline__ void run_counts(const ytm_config &cfg, int mi, DrawFn
         const u32x4 r = drawi((uint32_t)i);
         ++calls;
         const uint32_t R[4] = {r.x, r.y, r.z, r.w};
+        // the eight counts as nibbles (capped at 15; larger ones flagged),
+        // then transposed into four bit planes
+        uint32_t acc = 0u, big = 0u;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
             const uint32_t u = (R[q >> 1] >> (16 * (q & 1))) & 0xFFFFu;
@@ -212,8 +215,25 @@ __device__ __forceinline__ void run_counts(const ytm_config &cfg, int mi, DrawFn
             for (int e = 0; e < 6; ++e) d += u >= cfg.run_cdf16[mi][e] ? 1u : 0u;
             if (d == 6u)
                 while ((int)d < m && u >= cfg.run_cdf16[mi][d]) ++d;
+            acc |= (d > 15u ? 15u : d) << (4 * q);
+            big |= (d > 15u ? 1u : 0u) << q;
+        }
 #pragma unroll
-            for (int b = 0; b < 6; ++b) D[b] |= ((d >> b) & 1u) << (i * 8 + q);
+        for (int b = 0; b < 4; ++b) {
+            uint32_t x = (acc >> b) & 0x11111111u;
+            x = (x | (x >> 3)) & 0x03030303u;
+            x = (x | (x >> 6)) & 0x000F000Fu;
+            x = (x | (x >> 12)) & 0xFFu;
+            D[b] |= x << (8 * i);
+        }
+        for (; big; big &= big - 1u) {  // counts of 16 or more (rare)
+            const int q = __ffs(big) - 1;
+            const uint32_t u = (R[q >> 1] >> (16 * (q & 1))) & 0xFFFFu;
+            uint32_t d = 0;
+            while ((int)d < m && u >= cfg.run_cdf16[mi][d]) ++d;
+            const uint32_t bit = 1u << (i * 8 + q);
+#pragma unroll
+            for (int b = 0; b < 6; ++b) D[b] = (D[b] & ~bit) | (((d >> b) & 1u) ? bit : 0u);
         }
     }
 }

@@ -618,9 +618,10 @@ static ytm_status launch_cs_planes(const uint32_t *fired, const int32_t *ninc, c
     const int sms = sm_count();
     if (units < (int64_t)sms * 32 || CW >= 64) {
         // split the clause words so that about 16 warps per SM run; a segment
-        // keeps at least one word per lane
+        // keeps at least 4 words (batch 1 with 4000 clauses ran on 3 warps
+        // when segments kept one word per lane: 23 us instead of a few)
         int64_t segs = std::max<int64_t>(1, (int64_t)sms * 16 / units);
-        segs = std::min<int64_t>(segs, std::max<int64_t>(1, CW / 32));
+        segs = std::min<int64_t>(segs, std::max<int64_t>(1, CW / 4));
         const int seg_words = (int)cdiv(CW, segs);
         segs = cdiv(CW, seg_words);
         if (segs > 1) {
