@@ -635,6 +635,12 @@ def main():
                     "philox7_peak_calls_per_s": philox, "lop3_peak_per_s": lop3,
                     "op_model": "4*planes LOP3 per literal-word operation + Philox7 calls x (LOP3 peak / Philox peak)",
                     "t_min_ms": t_min * 1000.0,
+                    # the same kernel read by ncu (profiles/k_update_c5.md, 4096-clause capture of
+                    # this workload's shape and regime): the op model above leaves out the per-literal
+                    # count lookups of Type Ib run pieces and the decision draws, ncu counts every
+                    # instruction
+                    "ncu": {"issue_slots_busy": 0.777, "alu_pipe": 0.706, "lanes_per_instr": 31.7,
+                            "source": "profiles/k_update_c5.md"},
                     "hbm": {"algorithmic_bytes": state_bytes + B * W * 4 * cfg.patches,
                             "achieved_gbs": (state_bytes + B * W * 4 * cfg.patches) / upd_s / 1e9,
                             "peak_gbs": hbm_peak, "frac": (state_bytes + B * W * 4 * cfg.patches) / upd_s / 1e9
