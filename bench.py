@@ -550,7 +550,7 @@ def main():
         if fused:  # the path MultiClassTM.fit takes at batch 1: one fused launch per sample
             eng.train_fit_b1(lits[i * S:(i + 1) * S], Yd[i * S:(i + 1) * S], tm.sample_counter, None)
         else:  # the path MultiClassTM.fit takes at batch > 1: the C batch loop
-            par = tm._peer_ar(B * kw["n_classes"])
+            par = tm._peer_ar(B * kw["n_classes"])  # None above the peer kernel's size: NCCL
             eng.train_fit_batches(lits[i * S:(i + 1) * S], Yd[i * S:(i + 1) * S], B, tm.sample_counter, None,
                                   rank == 0, None if par is not None else tm._nccl(), par)
         tm.sample_counter += S
