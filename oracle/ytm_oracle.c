@@ -213,8 +213,9 @@ static inline void draw_r(const orc_cfg *c, uint32_t clause, uint64_t t, uint32_
     orc_philox4x32(ctr, key, rounds, out);
 }
 
-/* Decision draws use Philox4x32-10; the bulk literal-mask draws use the
- * 7-round variant, which Salmon et al. report as passing BigCrush. */
+/* The patch pick and pytm's other-class draw use Philox4x32-10; the per-class
+ * decision draws and the bulk literal-mask draws use the 7-round variant,
+ * which Salmon et al. report as passing BigCrush. */
 static inline void draw(const orc_cfg *c, uint32_t clause, uint64_t t, uint32_t sub, uint32_t tag,
                         uint32_t k, uint32_t out[4]) {
     draw_r(c, clause, t, sub, tag, k, 10, out);
@@ -657,10 +658,13 @@ void orc_train_update(const orc_cfg *c, int32_t lo, int32_t nc, uint32_t *ta, in
                     int32_t v = clip_cs(c, cs[(int64_t)b * K + k]);
                     int32_t y = Y[(int64_t)b * K + k];
                     int target = 1 - 2 * (v > y); /* kernel.cu:571 */
+                    /* decision uniforms: the Philox4x32-7 call of the class
+                     * pair k >> 1, words 0-1 for the even class, 2-3 for the odd */
                     uint32_t r[4];
-                    draw(c, g, t, 0, TAG_CLASS, (uint32_t)k, r);
-                    if (!c->one_negative && target == -1 && !((uint64_t)r[0] < c->q_thr)) continue; /* kernel.cu:573 */
-                    int upd = (uint64_t)r[1] < orc_update_threshold(y, v);   /* kernel.cu:582 */
+                    draw_r(c, g, t, 0, TAG_CLASS, (uint32_t)k >> 1, 7, r);
+                    const uint32_t uq = r[2 * (k & 1)], uu = r[2 * (k & 1) + 1];
+                    if (!c->one_negative && target == -1 && !((uint64_t)uq < c->q_thr)) continue; /* kernel.cu:573 */
+                    int upd = (uint64_t)uu < orc_update_threshold(y, v);   /* kernel.cu:582 */
                     int32_t *lw = &w[(int64_t)i * K + k];
                     int sign = (*lw >= 0) - (*lw < 0);
                     int ok = fired && ninc[i] <= c->max_included;

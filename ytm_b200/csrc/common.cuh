@@ -60,8 +60,9 @@ __device__ __forceinline__ u32x4 philox(uint32_t c0, uint32_t c1, uint32_t c2, u
 // sub-index, tag | class << 2); key = (seed low, seed high ^ sample high).
 enum : uint32_t { TAG_PATCH = 0, TAG_CLASS = 1, TAG_SMASK = 2, TAG_INIT = 3 };
 
-// Decision draws use Philox4x32-10; the bulk literal-mask draws use the
-// 7-round variant, which Salmon et al. report as passing BigCrush.
+// The patch pick and pytm's other-class draw use Philox4x32-10; the
+// per-class decision draws and the bulk literal-mask draws use the 7-round
+// variant, which Salmon et al. report as passing BigCrush.
 template <int R = 10>
 __device__ __forceinline__ u32x4 draw(uint64_t seed, uint32_t clause, uint64_t t, uint32_t sub, uint32_t tag,
                                       uint32_t k) {
@@ -249,6 +250,21 @@ __device__ __forceinline__ void run_counts(const ytm_config &cfg, int mi, DrawFn
             for (int b = 0; b < 6; ++b) D[b] = (D[b] & ~bit) | (((d >> b) & 1u) ? bit : 0u);
         }
     }
+}
+
+// The decision draws of class k for clause g at sample t: the Philox4x32-7
+// call of the class pair k >> 1 (counter sub-index 0, tag CLASS) gives words
+// (x, y) to the even class and (z, w) to the odd one; the first is the
+// negative-class selection uniform (kernel.cu:573), the second the update
+// uniform (kernel.cu:582).  Two classes share one call.
+__device__ __forceinline__ uint2 class_words(const u32x4 &r, uint32_t k) {
+    return (k & 1u) ? make_uint2(r.z, r.w) : make_uint2(r.x, r.y);
+}
+__device__ __forceinline__ u32x4 class_pair_draw_rk(const RoundKeys &rk, uint32_t g, uint64_t t, uint32_t k) {
+    return draw_rk<7>(rk, g, t, 0, TAG_CLASS, k >> 1);
+}
+__device__ __forceinline__ u32x4 class_pair_draw(uint64_t seed, uint32_t g, uint64_t t, uint32_t k) {
+    return draw<7>(seed, g, t, 0, TAG_CLASS, k >> 1);
 }
 
 // pytm's per-sample pick (pytm/base.py:139-141): the true class (the first

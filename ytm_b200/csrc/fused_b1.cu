@@ -146,12 +146,18 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
             const int k0 = cfg.coalesced ? 0 : (int)(g / (uint32_t)cfg.clauses_per_class);
             const bool fired = sel_cur[c] >= 0;
             const bool ok_inc = ninc_ws[c] <= cfg.max_included_literals;
+            u32x4 rp{};
+            int rp_pair = -1;  // the class pair whose decision call rp holds
             for (int kk = 0; kk < nk; ++kk) {
                 const int k = k0 + kk;
                 uint64_t th = thr_s[k];
                 const int target = (th >> 63) ? -1 : 1;
                 th &= ~(1ull << 63);
-                u32x4 r = draw_rk(rk, g, t, 0, TAG_CLASS, (uint32_t)k);
+                if ((k >> 1) != rp_pair) {
+                    rp = class_pair_draw_rk(rk, g, t, (uint32_t)k);
+                    rp_pair = k >> 1;
+                }
+                const uint2 r = class_words(rp, (uint32_t)k);
                 if (cfg.one_negative ? (k != pair_s[0] && k != pair_s[1])
                                      : (target == -1 && !((uint64_t)r.x < cfg.q_threshold)))
                     continue;  // kernel.cu:573

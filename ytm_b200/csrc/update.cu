@@ -201,19 +201,22 @@ __global__ void k_pairs(uint64_t seed, const int32_t *__restrict__ Y, int B, int
     }
 }
 
-// The Q-selection and update draws of clause g for the active pair (b, k):
-// 1 = update with target +1, 2 = with target -1, 0 = none.  Pairs reach here
-// only when active (under pytm's rules: one of the sample's two classes).
-__device__ __forceinline__ uint8_t decide(const ytm_config &cfg, const RoundKeys &rk, int rk_ok,
-                                          const uint64_t *__restrict__ thr, uint32_t g, uint64_t t0, int b, int k,
-                                          int K) {
+// The decision of clause g for the active pair (b, k) from its two decision
+// uniforms (class_words): 1 = update with target +1, 2 = with target -1, 0 =
+// none.  Pairs reach here only when active (under pytm's rules: one of the
+// sample's two classes).
+__device__ __forceinline__ uint8_t decide_words(const ytm_config &cfg, const uint64_t *__restrict__ thr, int b, int k,
+                                                int K, uint2 u) {
     uint64_t th = thr[(int64_t)b * K + k];
     const bool neg = (th >> 63) != 0;
     th &= ~(1ull << 63);
-    const uint64_t tb = t0 + (uint64_t)b;
-    const u32x4 r = rk_ok ? draw_rk(rk, g, tb, 0, TAG_CLASS, (uint32_t)k) : draw(cfg.seed, g, tb, 0, TAG_CLASS, (uint32_t)k);
-    const bool pass = cfg.one_negative || !(neg && !((uint64_t)r.x < cfg.q_threshold));  // kernel.cu:573
-    return (pass && (uint64_t)r.y < th) ? (neg ? 2 : 1) : 0;                             // kernel.cu:582
+    const bool pass = cfg.one_negative || !(neg && !((uint64_t)u.x < cfg.q_threshold));  // kernel.cu:573
+    return (pass && (uint64_t)u.y < th) ? (neg ? 2 : 1) : 0;                             // kernel.cu:582
+}
+
+__device__ __forceinline__ u32x4 pair_draw(const ytm_config &cfg, const RoundKeys &rk, int rk_ok, uint32_t g,
+                                           uint64_t tb, int k) {
+    return rk_ok ? class_pair_draw_rk(rk, g, tb, (uint32_t)k) : class_pair_draw(cfg.seed, g, tb, (uint32_t)k);
 }
 
 template <int NB, bool WPC>
@@ -323,17 +326,33 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
         //     parallel: 1 = update with target +1, 2 = with target -1; simple
         //     classes get their event type here (Ib when target and weight
         //     sign agree)
-        for (int idx = lo + tid; idx < hi; idx += nt) {  // coalesced: the chunk's pairs
-            const uint32_t e = alist[idx];
-            const int b = (int)(e / (uint32_t)K), k = (int)(e - (uint32_t)b * (uint32_t)K);
-            uint8_t a = decide(cfg, rk, rk_ok, thr, g, t0, b, k, K);
-            if (simple[k]) a = (a && ((a == 1) == (wk[k] >= 0))) ? EV_T1B : EV_NONE;
-            evt[(b - b0) * nk + k] = a;
+        // two consecutive list entries per thread: when they are the two
+        // classes of one class pair of one sample, one Philox call serves both
+        for (int i0 = lo + 2 * tid; i0 < hi; i0 += 2 * nt) {  // coalesced: the chunk's pairs
+            u32x4 r{};
+            int rb = -1, rp = -1;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int idx = i0 + j;
+                if (idx >= hi) break;
+                const uint32_t e = alist[idx];
+                const int b = (int)(e / (uint32_t)K), k = (int)(e - (uint32_t)b * (uint32_t)K);
+                if (b != rb || (k >> 1) != rp) {
+                    r = pair_draw(cfg, rk, rk_ok, g, t0 + (uint64_t)b, k);
+                    rb = b;
+                    rp = k >> 1;
+                }
+                uint8_t a = decide_words(cfg, thr, b, k, K, class_words(r, (uint32_t)k));
+                if (simple[k]) a = (a && ((a == 1) == (wk[k] >= 0))) ? EV_T1B : EV_NONE;
+                evt[(b - b0) * nk + k] = a;
+            }
         }
         if (!cfg.coalesced)
             for (int bl = tid; bl < bc; bl += nt)
                 if ((mycol[(b0 + bl) >> 5] >> ((b0 + bl) & 31)) & 1u) {
-                    uint8_t a = decide(cfg, rk, rk_ok, thr, g, t0, b0 + bl, k0, K);
+                    uint8_t a = decide_words(cfg, thr, b0 + bl, k0, K,
+                                             class_words(pair_draw(cfg, rk, rk_ok, g, t0 + (uint64_t)(b0 + bl), k0),
+                                                         (uint32_t)k0));
                     if (simple[0]) a = (a && ((a == 1) == (wk[0] >= 0))) ? EV_T1B : EV_NONE;
                     evt[bl] = a;
                 }
