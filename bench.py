@@ -55,7 +55,9 @@ L2_BYTES = 126 * 1024 * 1024
 # times it in, from one ncu capture of a reduced-clause model of the same
 # workload, scaled by clauses (the feedback's traffic is per clause); None
 # where no capture was made.
-TRAFFIC_PER_CLAUSE = {}
+# configuration 5: 223 MB read + 264 MB written by one k_update launch over
+# 4096 clauses (profiles/k_update_c5.md)
+TRAFFIC_PER_CLAUSE = {"c5": (223e6 + 264e6) / 4096}
 
 
 def load_peaks():
