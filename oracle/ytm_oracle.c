@@ -616,7 +616,7 @@ static void orc_pair(const orc_cfg *c, const int32_t *Yrow, uint64_t t, int *kt,
  * shard and every sample of the batch in order.  cs [B][K] are the summed class
  * sums, Y [B][K] the +-T targets, sel [B][nc] and ninc [nc] from part 1. */
 /* Feedback of a batch (clause_update, kernel.cu:531-613, per sample in
- * order).  Per clause, the events of each 32-sample window of the batch are
+ * order).  Per clause, the events of each 64-sample window of the batch are
  * decided first (the decisions read only the batch-start fired bits and
  * include counts, and the weights, which they update), then applied in
  * feedback order; maximal runs of consecutive Type Ib events inside a window
@@ -631,15 +631,15 @@ void orc_train_update(const orc_cfg *c, int32_t lo, int32_t nc, uint32_t *ta, in
     const int K = c->K, L = c->L, W = c->W, P = c->P;
 #pragma omp parallel
     {
-    orc_event *ev = (orc_event *)malloc(sizeof(orc_event) * 32 * (size_t)(K > 2 ? K : 2));
+    orc_event *ev = (orc_event *)malloc(sizeof(orc_event) * 64 * (size_t)(K > 2 ? K : 2));
 #pragma omp for schedule(dynamic, 4)
     for (int32_t i = 0; i < nc; ++i) {
         if (drop && drop[i] == 1) continue; /* kernel.cu:555 */
         uint32_t g = (uint32_t)(lo + i);
         uint32_t *st = ta + (int64_t)i * L;
-        for (int32_t b0 = 0; b0 < B; b0 += 32) {
+        for (int32_t b0 = 0; b0 < B; b0 += 64) {
             int nev = 0;
-            for (int32_t b = b0; b < B && b < b0 + 32; ++b) {
+            for (int32_t b = b0; b < B && b < b0 + 64; ++b) {
                 uint64_t t = t0 + (uint64_t)b;
                 int32_t sp = sel[(int64_t)b * nc + i];
                 int fired = sp > -1; /* kernel.cu:558 */

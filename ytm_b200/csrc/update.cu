@@ -29,6 +29,9 @@ namespace ytm {
 // samples per chunk at most (list entries hold 8-bit rows); 128 keeps the
 // event list small enough for ~16 clause CTAs per SM at 10 classes
 constexpr int UPD_BC_MAX = 128;
+// Type Ib runs are taken inside windows of this many samples of the batch
+// (batch-relative); every feedback chunk holds whole windows
+constexpr int RUN_WINDOW = 64;
 
 // One block prepares the batch's decisions, which every clause shares.
 //  * thr[b][k] = floor(p * 2^32) of the update probability, bit 63 set when
@@ -505,11 +508,11 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                     ++n_units;
                     if (ev == EV_T1B) {
                         // a run of consecutive Type Ib events inside this
-                        // 32-sample window: pieces of 32, 16, 8 from its start
+                        // 64-sample window: pieces of 32, 16, 8 from its start
                         int run = 1;
                         while (run < 32 && e + run < nev) {
                             const uint32_t en = list[e + run];
-                            if (((en >> 22) & 3u) != EV_T1B || ((en >> 24) >> 5) != ((uint32_t)bl >> 5)) break;
+                            if (((en >> 22) & 3u) != EV_T1B || ((en >> 24) >> 6) != ((uint32_t)bl >> 6)) break;
                             ++run;
                         }
                         if (run >= 8) {
@@ -609,10 +612,11 @@ extern "C" ytm_status ytm_train_update_counted(const ytm_config *cfg, uint32_t *
                                      row_off, alist);
     if ((rc = launch_check("update thresholds"))) return rc;
     const int nk = cfg->coalesced ? cfg->n_classes : 1;
-    // the largest chunk (multiple of 32, at most UPD_BC_MAX and the batch) whose
-    // event list fits 32 KB of shared memory (keeps several CTAs per SM)
-    int BC = std::min(UPD_BC_MAX, ((B + 31) / 32) * 32);
-    while (BC > 32 && update_smem(nk, BC) > 32 * 1024) BC -= 32;
+    // chunks hold whole 64-sample Type Ib run windows: the whole batch when
+    // B <= 64, else 128 samples, or 64 when the event list of 128 would not
+    // fit 32 KB of shared memory (keeps several CTAs per SM)
+    int BC = B <= RUN_WINDOW ? ((B + 31) / 32) * 32 : UPD_BC_MAX;
+    if (B > RUN_WINDOW && update_smem(nk, BC) > 32 * 1024) BC = RUN_WINDOW;
     const size_t smem = update_smem_total(nk, BC);
     if (smem > 227 * 1024) return fail(YTM_ERR_UNSUPPORTED, "too many classes for the feedback kernel");
     // round keys for the batch's samples when they share the counter's high word
