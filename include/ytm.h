@@ -81,7 +81,7 @@ typedef struct ytm_config {
                                   Binomial(32, 1/s); entry n = floor(2^32 *
                                   P(count <= n)), saturated at 2^32 - 1     */
     uint64_t q_threshold;      /* negative-class selection, thr / 2^32          */
-    uint32_t run_cdf16[3][33]; /* Type Ib runs of m = 8, 16, 32 events: per
+    uint32_t run_cdf16[4][65]; /* Type Ib runs of m = 8, 16, 32, 64 events: per
                                   literal decrement count Binomial(m, 1/s);
                                   entry d = floor(65536 * P(count <= d)),
                                   65536 from d = m on                        */

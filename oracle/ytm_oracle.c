@@ -45,7 +45,7 @@ typedef struct orc_cfg {
     int32_t max_state, half_state, state_top;
     uint32_t s_cdf[32];
     uint64_t q_thr;
-    uint32_t run_cdf16[3][33];
+    uint32_t run_cdf16[4][65];
     /* rule variants of the reference's CPU TM, pytm/base.py (0 = cutm rules) */
     int32_t one_negative; /* one uniformly chosen negative class per sample, true class first (base.py:139-143) */
     int32_t count_empty;  /* inference counts clauses without includes (base.py:59-67) */
@@ -79,20 +79,24 @@ static void count_cdf(double s, uint32_t cdf[32]) {
     }
 }
 
-/* Type Ib runs (see orc_train_update): for m = 8, 16, 32 events the number
+/* Type Ib runs are taken inside windows of 128 samples of the batch (64 when
+ * the clause sees more than 256 classes). */
+static int run_window(const orc_cfg *c) { return (c->coalesced ? c->K : 1) <= 256 ? 128 : 64; }
+
+/* Type Ib runs (see orc_train_update): for m = 8, 16, 32, 64 events the number
  * of decrements of one literal is Binomial(m, p), p = 1/s; entry d of row mi
  * is floor(65536 * P(count <= d)), 65536 from d = m on; the same pmf
  * recurrence in IEEE double. */
-static const int RUN_SIZES[3] = {8, 16, 32};
+static const int RUN_SIZES[4] = {8, 16, 32, 64};
 
-static void run_cdf(double s, uint32_t out[3][33]) {
+static void run_cdf(double s, uint32_t out[4][65]) {
     double p = 1.0 / s;
     if (!(p > 0.0)) p = 0.0;
     if (p > 1.0) p = 1.0;
     const double q = 1.0 - p;
-    for (int mi = 0; mi < 3; ++mi) {
+    for (int mi = 0; mi < 4; ++mi) {
         const int m = RUN_SIZES[mi];
-        for (int d = 0; d < 33; ++d) out[mi][d] = 65536u;
+        for (int d = 0; d < 65; ++d) out[mi][d] = 65536u;
         if (!(q > 0.0)) { /* p = 1: every event decrements */
             for (int d = 0; d < m; ++d) out[mi][d] = 0u;
             continue;
@@ -616,11 +620,11 @@ static void orc_pair(const orc_cfg *c, const int32_t *Yrow, uint64_t t, int *kt,
  * shard and every sample of the batch in order.  cs [B][K] are the summed class
  * sums, Y [B][K] the +-T targets, sel [B][nc] and ninc [nc] from part 1. */
 /* Feedback of a batch (clause_update, kernel.cu:531-613, per sample in
- * order).  Per clause, the events of each 64-sample window of the batch are
+ * order).  Per clause, the events of each 128-sample window (64 above 256 classes) of the batch are
  * decided first (the decisions read only the batch-start fired bits and
  * include counts, and the weights, which they update), then applied in
  * feedback order; maximal runs of consecutive Type Ib events inside a window
- * are applied in pieces of 32, 16 and 8 events (greedy, from the run's start)
+ * are applied in pieces of 64, 32, 16 and 8 events (greedy, from the run's start)
  * with type1b_run, the rest one by one. */
 enum { EV_T1A = 1, EV_T1B = 2, EV_T2 = 3 };
 typedef struct { int32_t b, k, type; } orc_event;
@@ -631,15 +635,16 @@ void orc_train_update(const orc_cfg *c, int32_t lo, int32_t nc, uint32_t *ta, in
     const int K = c->K, L = c->L, W = c->W, P = c->P;
 #pragma omp parallel
     {
-    orc_event *ev = (orc_event *)malloc(sizeof(orc_event) * 64 * (size_t)(K > 2 ? K : 2));
+    const int win = run_window(c);
+    orc_event *ev = (orc_event *)malloc(sizeof(orc_event) * (size_t)win * (size_t)(K > 2 ? K : 2));
 #pragma omp for schedule(dynamic, 4)
     for (int32_t i = 0; i < nc; ++i) {
         if (drop && drop[i] == 1) continue; /* kernel.cu:555 */
         uint32_t g = (uint32_t)(lo + i);
         uint32_t *st = ta + (int64_t)i * L;
-        for (int32_t b0 = 0; b0 < B; b0 += 64) {
+        for (int32_t b0 = 0; b0 < B; b0 += win) {
             int nev = 0;
-            for (int32_t b = b0; b < B && b < b0 + 64; ++b) {
+            for (int32_t b = b0; b < B && b < b0 + win; ++b) {
                 uint64_t t = t0 + (uint64_t)b;
                 int32_t sp = sel[(int64_t)b * nc + i];
                 int fired = sp > -1; /* kernel.cu:558 */
@@ -689,8 +694,8 @@ void orc_train_update(const orc_cfg *c, int32_t lo, int32_t nc, uint32_t *ta, in
                 const uint64_t t = t0 + (uint64_t)E->b;
                 if (E->type == EV_T1B) {
                     int run = 0;
-                    while (e + run < nev && run < 32 && ev[e + run].type == EV_T1B) ++run;
-                    const int mi = run >= 32 ? 2 : (run >= 16 ? 1 : (run >= 8 ? 0 : -1));
+                    while (e + run < nev && run < 64 && ev[e + run].type == EV_T1B) ++run;
+                    const int mi = run >= 64 ? 3 : (run >= 32 ? 2 : (run >= 16 ? 1 : (run >= 8 ? 0 : -1)));
                     if (mi >= 0) {
                         type1b_run(c, st, g, t, (uint32_t)E->k, mi);
                         e += RUN_SIZES[mi];

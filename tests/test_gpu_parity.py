@@ -104,7 +104,7 @@ TRAIN_CASES = {
                           patch_dim=(6, 6)), 4),
     # every negative class selected (q = K - 1): about a dozen events per
     # clause and sample, so runs of 8, 16 and 32 Type Ib events form inside
-    # the 64-sample windows (batch 40: one ragged window; batch 1:
+    # the run windows (batch 40: one ragged window; batch 1:
     # the fused kernel; batch 12: the warp-per-clause kernel)
     "runs_b40": (dict(number_of_clauses_per_class=30, T=400, s=4.0, dim=(40, 1, 1), n_classes=24, q=23.0), 40),
     "runs_b12": (dict(number_of_clauses_per_class=30, T=400, s=4.0, dim=(40, 1, 1), n_classes=24, q=23.0), 12),
@@ -384,13 +384,14 @@ def test_type1b_runs_take_the_run_path():
     assert events > 0 and calls < 0.75 * events * o.W, (calls, events)
 
 
-@pytest.mark.parametrize("K,bs", [(24, 150), (60, 100)])
+@pytest.mark.parametrize("K,bs", [(24, 150), (300, 100)])
 def test_type1b_runs_over_chunks(K, bs):
-    """Runs inside 64-sample windows when a batch spans several feedback
-    chunks: 24 classes, batch 150 (chunks of 128 and 22 samples, windows at
-    0, 64, 128); 60 classes, batch 100 (the event list of 128 samples would
-    pass 32 KB, so chunks of 64)."""
-    kw = dict(number_of_clauses_per_class=20, T=400, s=4.0, dim=(40, 1, 1), n_classes=K, q=float(K - 1))
+    """Runs inside their windows when a batch spans several feedback chunks:
+    24 classes, batch 150 (128-sample windows: chunks of 128 and 22); 300
+    classes, batch 100 (above 256 classes the windows and chunks are 64
+    samples: 64 and 36)."""
+    kw = dict(number_of_clauses_per_class=20 if K < 100 else 6, T=400, s=4.0, dim=(40, 1, 1), n_classes=K,
+              q=float(K - 1))
     o = O.Oracle(**oracle_kwargs(kw, 8))
     e = engine_for(kw, 8)
     rng = np.random.default_rng(13)

@@ -195,7 +195,7 @@ def test_type1b_run_counts(s):
     """Definition, and the count distribution Binomial(m, 1/s) of each run size."""
     from math import comb
     o = O.Oracle(number_of_clauses_per_class=4, T=10, s=s, dim=(4, 1, 1), n_classes=3, seed=3 + 2**36)
-    for mi in range(3):
+    for mi in range(4):
         m = 8 << mi
         assert list(o.run_counts(2, 2**32 + 5, 1, 7, mi)) == _run_spec(o, 2, 2**32 + 5, 1, 7, mi)
         d = np.concatenate([o.run_counts(c, t, 2, w, mi) for c in range(3) for t in range(60) for w in range(4)])

@@ -172,16 +172,16 @@ ytm_status ytm_config_init(ytm_config *cfg, int32_t clauses_per_class, int32_t T
         }
     }
     // Type Ib run tables: per literal Binomial(m, p) decrement counts for runs
-    // of m = 8, 16, 32 events; entry d = floor(65536 * P(count <= d)),
+    // of m = 8, 16, 32, 64 events; entry d = floor(65536 * P(count <= d)),
     // 65536 from d = m on, from the same pmf recurrence
     {
         double p = 1.0 / s;
         if (!(p > 0.0)) p = 0.0;
         if (p > 1.0) p = 1.0;
         const double qq = 1.0 - p;
-        for (int mi = 0; mi < 3; ++mi) {
+        for (int mi = 0; mi < 4; ++mi) {
             const int m = 8 << mi;
-            for (int d = 0; d < 33; ++d) cfg->run_cdf16[mi][d] = 65536u;
+            for (int d = 0; d < 65; ++d) cfg->run_cdf16[mi][d] = 65536u;
             if (!(qq > 0.0)) {
                 for (int d = 0; d < m; ++d) cfg->run_cdf16[mi][d] = 0u;
                 continue;

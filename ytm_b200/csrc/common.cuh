@@ -197,7 +197,7 @@ __device__ __forceinline__ uint32_t smask_word_rk(const ytm_config &cfg, const R
     return smask_place(cfg, [&](uint32_t j) { return draw_rk<7>(rk, g, t, w * 4u + j, TAG_SMASK, k); }, calls);
 }
 
-// A run of m = 8 << mi consecutive Type Ib events of one clause (type1b_fb,
+// A run of m = 8 << mi (8 to 64) consecutive Type Ib events of one clause (type1b_fb,
 // kernel.cu:453-470, applied by the reference one event at a time: each
 // decrements every literal with a positive state with probability 1/s).
 // Decrements with a floor at 0 commute, so the run leaves state - d clamped
@@ -205,13 +205,13 @@ __device__ __forceinline__ uint32_t smask_word_rk(const ytm_config &cfg, const R
 // inverse CDF from a 16-bit uniform: literal j of word w takes half j & 1 of
 // word (j >> 1) & 3 of the Philox4x32-7 call j >> 3, at sub-index
 // 0x40000000 | 4w | (j >> 3), keyed on the run's first event.  D receives
-// the counts as bit planes (d <= 32 needs 6).  The first six comparisons are
+// the counts as bit planes (d <= 64 needs 7).  The first six comparisons are
 // branch-free; only counts of 6 or more continue in the loop.
 template <typename DrawFn>
-__device__ __forceinline__ void run_counts(const ytm_config &cfg, int mi, DrawFn drawi, uint32_t (&D)[6],
+__device__ __forceinline__ void run_counts(const ytm_config &cfg, int mi, DrawFn drawi, uint32_t (&D)[7],
                                            uint32_t &calls) {
 #pragma unroll
-    for (int b = 0; b < 6; ++b) D[b] = 0u;
+    for (int b = 0; b < 7; ++b) D[b] = 0u;
     const int m = 8 << mi;
 #pragma unroll 1
     for (int i = 0; i < 4; ++i) {  // not unrolled: keeps the feedback loop's code small
@@ -247,7 +247,7 @@ __device__ __forceinline__ void run_counts(const ytm_config &cfg, int mi, DrawFn
             while ((int)d < m && u >= cfg.run_cdf16[mi][d]) ++d;
             const uint32_t bit = 1u << (i * 8 + q);
 #pragma unroll
-            for (int b = 0; b < 6; ++b) D[b] = (D[b] & ~bit) | (((d >> b) & 1u) ? bit : 0u);
+            for (int b = 0; b < 7; ++b) D[b] = (D[b] & ~bit) | (((d >> b) & 1u) ? bit : 0u);
         }
     }
 }
@@ -365,14 +365,14 @@ struct Counter {
         return ne(v);
     }
     // stored value := max(z, value - D) for the literals of D (bit planes,
-    // six of them): a run of Type Ib decrements with the floor at state 0
+    // seven of them): a run of Type Ib decrements with the floor at state 0
     // (stored value z = offset).  top2: z + 1 = 2^(NB-2), so a value is at
     // most z exactly when its two top planes are clear.
-    __device__ __forceinline__ void sub_floor(const uint32_t (&D)[6], uint32_t z, bool top2) {
+    __device__ __forceinline__ void sub_floor(const uint32_t (&D)[7], uint32_t z, bool top2) {
         uint32_t q[NB], br = 0u;
 #pragma unroll
         for (int i = 0; i < NB; ++i) {
-            const uint32_t d = i < 6 ? D[i] : 0u;
+            const uint32_t d = i < 7 ? D[i] : 0u;
             q[i] = p[i] ^ d ^ br;
             br = (~p[i] & (d | br)) | (d & br);
         }
@@ -520,6 +520,13 @@ __host__ __device__ inline LitSrc lit_src_dev(const ytm_config &cfg, const uint3
     return s;
 }
 inline LitSrc lit_src(const ytm_config *cfg, const uint32_t *lits) { return lit_src_dev(*cfg, lits); }
+
+// Type Ib runs are taken inside windows of this many samples of the batch
+// (batch-relative): 128, or 64 when a clause sees more than 256 classes (the
+// feedback kernel's event list of 128 samples would then not fit shared memory)
+__host__ __device__ inline int run_window(const ytm_config &c) {
+    return (c.coalesced ? c.n_classes : 1) <= 256 ? 128 : 64;
+}
 
 // Dispatch a templated launcher on the plane count.
 #define YTM_DISPATCH_PLANES(NBVAR, ...)                      \

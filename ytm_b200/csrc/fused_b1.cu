@@ -268,20 +268,20 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
                             uint32_t stop = (m1a | m2) & rem;
                             for (int kb2 = kb;;) {
                                 run += __popc(stop ? (rem & ((stop & (0u - stop)) - 1u)) : rem);
-                                if (stop || run >= 32 || ++kb2 >= KB) break;
+                                if (stop || run >= 64 || ++kb2 >= KB) break;
                                 rem = ev[kb2 * 3];
                                 stop = (ev[kb2 * 3 + 1] | ev[kb2 * 3 + 2]) & rem;
                             }
                         }
                         if (run >= 8) {
-                            const int mi = run >= 32 ? 2 : (run >= 16 ? 1 : 0);
+                            const int mi = run >= 64 ? 3 : (run >= 32 ? 2 : (run >= 16 ? 1 : 0));
                             const uint32_t kk = (uint32_t)(k0 + kb * 32 + b);
-                            uint32_t D[6];
+                            uint32_t D[7];
                             run_counts(cfg, mi, [&](uint32_t ii) {
                                 return draw_rk<7>(rk, g, t, 0x40000000u | ((uint32_t)w << 2) | ii, TAG_SMASK, kk);
                             }, D, n_calls);
 #pragma unroll
-                            for (int ii = 0; ii < 6; ++ii) D[ii] &= vm;
+                            for (int ii = 0; ii < 7; ++ii) D[ii] &= vm;
                             ctr.sub_floor(D, zero_s, top2);
                             skip = (8 << mi) - 1;
                             continue;

@@ -26,12 +26,10 @@
 
 namespace ytm {
 
-// samples per chunk at most (list entries hold 8-bit rows); 128 keeps the
-// event list small enough for ~16 clause CTAs per SM at 10 classes
+// samples per chunk at most: list entries hold 8-bit rows, and a chunk is at
+// most one Type Ib run window (run_window: 128 or 64 samples)
 constexpr int UPD_BC_MAX = 128;
-// Type Ib runs are taken inside windows of this many samples of the batch
-// (batch-relative); every feedback chunk holds whole windows
-constexpr int RUN_WINDOW = 64;
+static_assert(UPD_BC_MAX <= 256, "event list rows are 8 bits");
 
 // One block prepares the batch's decisions, which every clause shares.
 //  * thr[b][k] = floor(p * 2^32) of the update probability, bit 63 set when
@@ -277,6 +275,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
         }
     }
     int fired_count = 0;  // single-patch models: patch 0 picks of this clause (select_active, kernel.cu:305)
+    const uint32_t win_shift = run_window(cfg) == 128 ? 7u : 6u;  // Type Ib run windows
     // measurement counters: (event, word) pairs applied, Philox4x32-7 calls
     // of the literal masks, state words streamed, events
     uint32_t n_units = 0, n_calls = 0, n_words = 0, n_events = 0;
@@ -508,23 +507,24 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                     ++n_units;
                     if (ev == EV_T1B) {
                         // a run of consecutive Type Ib events inside this
-                        // 64-sample window: pieces of 32, 16, 8 from its start
+                        // run window: pieces of 64, 32, 16, 8 from its start
                         int run = 1;
-                        while (run < 32 && e + run < nev) {
+                        while (run < 64 && e + run < nev) {
                             const uint32_t en = list[e + run];
-                            if (((en >> 22) & 3u) != EV_T1B || ((en >> 24) >> 6) != ((uint32_t)bl >> 6)) break;
+                            if (((en >> 22) & 3u) != EV_T1B || ((en >> 24) >> win_shift) != ((uint32_t)bl >> win_shift))
+                                break;
                             ++run;
                         }
                         if (run >= 8) {
-                            const int mi = run >= 32 ? 2 : (run >= 16 ? 1 : 0);
-                            uint32_t D[6];
+                            const int mi = run >= 64 ? 3 : (run >= 32 ? 2 : (run >= 16 ? 1 : 0));
+                            uint32_t D[7];
                             run_counts(cfg, mi, [&](uint32_t i) {
                                 const uint32_t sub = 0x40000000u | ((uint32_t)w << 2) | i;
                                 return rk_ok ? draw_rk<7>(rk, g, t, sub, TAG_SMASK, (uint32_t)k)
                                              : draw<7>(cfg.seed, g, t, sub, TAG_SMASK, (uint32_t)k);
                             }, D, n_calls);
 #pragma unroll
-                            for (int i = 0; i < 6; ++i) D[i] &= vm;
+                            for (int i = 0; i < 7; ++i) D[i] &= vm;
                             ctr.sub_floor(D, zero_s, top2);
                             e += (8 << mi) - 1;
                             continue;
@@ -612,11 +612,10 @@ extern "C" ytm_status ytm_train_update_counted(const ytm_config *cfg, uint32_t *
                                      row_off, alist);
     if ((rc = launch_check("update thresholds"))) return rc;
     const int nk = cfg->coalesced ? cfg->n_classes : 1;
-    // chunks hold whole 64-sample Type Ib run windows: the whole batch when
-    // B <= 64, else 128 samples, or 64 when the event list of 128 would not
-    // fit 32 KB of shared memory (keeps several CTAs per SM)
-    int BC = B <= RUN_WINDOW ? ((B + 31) / 32) * 32 : UPD_BC_MAX;
-    if (B > RUN_WINDOW && update_smem(nk, BC) > 32 * 1024) BC = RUN_WINDOW;
+    // chunks hold whole Type Ib run windows: the whole batch when it is at
+    // most one window, else one window (128 samples, or 64 above 256 classes)
+    const int win = run_window(*cfg);
+    int BC = B <= win ? ((B + 31) / 32) * 32 : win;
     const size_t smem = update_smem_total(nk, BC);
     if (smem > 227 * 1024) return fail(YTM_ERR_UNSUPPORTED, "too many classes for the feedback kernel");
     // round keys for the batch's samples when they share the counter's high word
