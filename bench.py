@@ -55,9 +55,9 @@ L2_BYTES = 126 * 1024 * 1024
 # times it in, from one ncu capture of a reduced-clause model of the same
 # workload, scaled by clauses (the feedback's traffic is per clause); None
 # where no capture was made.
-# configuration 5: 223 MB read + 264 MB written by one k_update launch over
+# configuration 5: 223 MB read + 188 MB written by one k_update launch over
 # 4096 clauses (profiles/k_update_c5.md)
-TRAFFIC_PER_CLAUSE = {"c5": (223e6 + 264e6) / 4096}
+TRAFFIC_PER_CLAUSE = {"c5": (223e6 + 188e6) / 4096}
 
 
 def load_peaks():
@@ -619,34 +619,36 @@ def main():
     NB, W = cfg.planes, cfg.words
     if ctrs is not None:
         units, calls, words, events = (v / nb for v in ctrs)
-        # INT work of one feedback launch in LOP3-equivalent operations:
-        # 4 * planes logic ops per literal-word operation (a single event, or
-        # a Type Ib run piece: a ripple add, borrow or saturating subtraction
-        # over the planes plus the comparator that selects its literals) and
-        # each Philox4x32-7 call (literal masks, run counts) weighted by the
-        # measured LOP3 : Philox throughput ratio
-        ops = units * 4 * NB + calls * (lop3 / philox)
-        t_min = units * 4 * NB / lop3 + calls / philox
-        state_bytes = words * NB * 4 * 2
+        # Algorithmic INT work of one feedback launch (the per-unit figure of
+        # the hot-path survey: U * W * (ripple add ~ 2 * planes + Bernoulli
+        # mask ops)): every (event, literal word) pair of the reference's
+        # per-event algorithm costs a ripple add or borrow over the planes
+        # (2 * planes logic ops) and one Bernoulli(1/s) mask of 32 literals,
+        # priced as one Philox4x32-7 call at the measured LOP3 : Philox
+        # throughput ratio.  Type Ib runs do less than this per event, so the
+        # fraction can approach 1 without the kernel being at the pipe's limit;
+        # ncu's reading of the kernel is carried beside it.
+        event_words = events * W
+        mask_ops = lop3 / philox
+        ops = event_words * (2 * NB + mask_ops)
+        alg_bytes = cfg.clause_count * NB * W * 4 * 2 + B * W * 4 * cfg.patches  # one read + write of the planes
         roofline = {"bound": "int", "achieved": ops / upd_s / 1e9, "peak": lop3 / 1e9, "unit": "G int-ops/s",
                     "frac": ops / upd_s / lop3, "traffic": None, "kernel": "k_update (feedback)",
                     "peak_kind": "measured on this GPU (bench_probe.cu LOP3 probe)",
                     "launch_ms": upd_s * 1000.0, "launches_averaged": nb,
+                    "units_per_launch": {"event_word_pairs": event_words, "events": events},
+                    "op_model": "per (event, literal word): 2*planes LOP3 (ripple) + one Philox4x32-7 mask call "
+                                "x (LOP3 peak / Philox peak)",
                     "counters_per_launch": {"literal_word_ops": units, "philox7_calls": calls,
-                                            "state_words_streamed": words, "events": events},
+                                            "state_words_streamed": words},
                     "philox7_peak_calls_per_s": philox, "lop3_peak_per_s": lop3,
-                    "op_model": "4*planes LOP3 per literal-word operation + Philox7 calls x (LOP3 peak / Philox peak)",
-                    "t_min_ms": t_min * 1000.0,
                     # the same kernel read by ncu (profiles/k_update_c5.md, 4096-clause capture of
-                    # this workload's shape and regime): the op model above leaves out the per-literal
-                    # count lookups of Type Ib run pieces and the decision draws, ncu counts every
-                    # instruction
-                    "ncu": {"issue_slots_busy": 0.777, "alu_pipe": 0.706, "lanes_per_instr": 31.7,
-                            "source": "profiles/k_update_c5.md"},
-                    "hbm": {"algorithmic_bytes": state_bytes + B * W * 4 * cfg.patches,
-                            "achieved_gbs": (state_bytes + B * W * 4 * cfg.patches) / upd_s / 1e9,
-                            "peak_gbs": hbm_peak, "frac": (state_bytes + B * W * 4 * cfg.patches) / upd_s / 1e9
-                            / hbm_peak, "peak_kind": peak_kind}}
+                    # this workload's shape and regime)
+                    "ncu": {"source": "profiles/k_update_c5.md"},
+                    "hbm": {"algorithmic_bytes": alg_bytes, "achieved_gbs": alg_bytes / upd_s / 1e9,
+                            "peak_gbs": hbm_peak, "frac": alg_bytes / upd_s / 1e9 / hbm_peak,
+                            "peak_kind": peak_kind,
+                            "l2_bytes": words * NB * 4 * 2}}
         tpc = TRAFFIC_PER_CLAUSE.get(name)
         if tpc is not None and world == 1:
             roofline["traffic"] = tpc * cfg.clause_count

@@ -39,7 +39,7 @@ static_assert(UPD_BC_MAX <= 256, "event list rows are 8 bits");
 //    rules, k is one of the sample's two classes.  Once a model has converged
 //    most class sums sit at +-T and few pairs stay active.
 //  * amask[b][k / 32] and colm[k][b / 32] hold the active pairs as bits per
-//    sample and per class; alist lists them in feedback order (sample by
+//    sample and per class; alist lists them (sample << 16 | class) in feedback order (sample by
 //    sample; classes in order, or pytm's true class first) and row_off[b] is
 //    the position of sample b's first pair in it (row_off[B] = the count).
 __global__ void __launch_bounds__(1024) k_thresholds(const int32_t *__restrict__ cs, const int32_t *__restrict__ Y,
@@ -126,12 +126,12 @@ __global__ void __launch_bounds__(1024) k_thresholds(const int32_t *__restrict__
             if (one_neg) {
                 for (int q = 0; q < 2; ++q) {
                     const int k = pair[2 * row + q];
-                    if (k >= 0 && ((am[k >> 5] >> (k & 31)) & 1u)) alist[pos++] = (uint32_t)row * (uint32_t)K + k;
+                    if (k >= 0 && ((am[k >> 5] >> (k & 31)) & 1u)) alist[pos++] = ((uint32_t)row << 16) | (uint32_t)k;
                 }
             } else {
                 for (int m = 0; m < KWm; ++m)
                     for (uint32_t v = am[m]; v; v &= v - 1u)
-                        alist[pos++] = (uint32_t)row * (uint32_t)K + (uint32_t)(m * 32 + __ffs(v) - 1);
+                        alist[pos++] = ((uint32_t)row << 16) | (uint32_t)(m * 32 + __ffs(v) - 1);
             }
         }
         __syncthreads();
@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                 const int idx = i0 + j;
                 if (idx >= hi) break;
                 const uint32_t e = alist[idx];
-                const int b = (int)(e / (uint32_t)K), k = (int)(e - (uint32_t)b * (uint32_t)K);
+                const int b = (int)(e >> 16), k = (int)(e & 0xFFFFu);
                 if (b != rb || (k >> 1) != rp) {
                     r = pair_draw(cfg, rk, rk_ok, g, t0 + (uint64_t)b, k);
                     rb = b;
@@ -589,7 +589,9 @@ extern "C" ytm_status ytm_train_update_counted(const ytm_config *cfg, uint32_t *
     if (!state || !weights || !cs || !Y || !lits || !workspace) return fail(YTM_ERR_ARG, "null pointer");
     const int count_patch = single_patch_eval(cfg) ? 1 : 0;
     if (count_patch && !patch_w) return fail(YTM_ERR_ARG, "patch_w is NULL");
-    if (cfg->n_classes >= (1 << 22)) return fail(YTM_ERR_UNSUPPORTED, "too many classes");
+    // active-pair list entries hold (sample << 16 | class)
+    if (cfg->n_classes > 65535 || B > 65535)
+        return fail(YTM_ERR_UNSUPPORTED, "feedback handles at most 65,535 classes and 65,535 samples per batch");
     if ((int64_t)B * cfg->n_classes >= (1ll << 32)) return fail(YTM_ERR_UNSUPPORTED, "batch x classes above 2^32");
     cudaStream_t st = as_stream(stream);
     TrainWs l = train_ws_layout(cfg, B);
