@@ -240,7 +240,10 @@ ytm_status ytm_train_eval(const ytm_config *cfg, const uint32_t *state, const in
  * counting of picks (kernel.cu:305) to this call, which adds them here.
  * workspace: the one ytm_train_eval filled for this batch; without
  * sel_override this call reads the picks from it (single-patch models: the
- * clause outputs, kept there clause by clause). */
+ * clause outputs, kept there clause by clause).  Limits: at most 65,535
+ * classes and 65,535 samples per batch; for batches above 64 samples, at
+ * most about 700 classes (a chunk's event list lives in shared memory);
+ * beyond them YTM_ERR_UNSUPPORTED. */
 ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, int32_t *weights,
                             const int32_t *cs, const int32_t *Y, const uint32_t *drop,
                             const uint32_t *lits, int32_t B, uint64_t t0,
