@@ -49,7 +49,7 @@ class OrcCfg(ct.Structure):
         ("seed", ct.c_uint64),
         ("banks", ct.c_int32), ("C", ct.c_int32), ("L", ct.c_int32), ("W", ct.c_int32), ("P", ct.c_int32),
         ("max_state", ct.c_int32), ("half_state", ct.c_int32), ("state_top", ct.c_int32),
-        ("s_cdf", ct.c_uint32 * 32), ("q_thr", ct.c_uint64), ("q_cdf", ct.c_uint32 * 32), ("q_select", ct.c_int32), ("run_cdf16", (ct.c_uint32 * 65) * 4),
+        ("s_cdf", ct.c_uint32 * 32), ("q_thr", ct.c_uint64), ("run_cdf16", (ct.c_uint32 * 65) * 4),
         ("one_negative", ct.c_int32), ("count_empty", ct.c_int32),
     ]
 

@@ -178,12 +178,10 @@ __device__ __forceinline__ void block_sync() {
 }
 
 // Shared memory of one clause: weights [nk], picks [bc], count, event list
-// [bc*nk], fired samples [bc/32], negative-class selections [bc][nk/32],
-// event types [bc*nk], simple classes [nk].  update_smem() (without the last
-// two small arrays' padding) sizes the chunk.
+// [bc*nk], fired samples [bc/32], event types [bc*nk], simple classes [nk].
+// update_smem() (without the last two small arrays' padding) sizes the chunk.
 static __host__ __device__ inline size_t update_smem(int nk, int bc) {
-    return (size_t)nk * 4 + (size_t)bc * 4 + 4 + (size_t)bc * nk * 4 + (size_t)bc * ((nk + 31) / 32) * 4 +
-           (size_t)bc * nk + 16;
+    return (size_t)nk * 4 + (size_t)bc * 4 + 4 + (size_t)bc * nk * 4 + (size_t)bc * nk + 16;
 }
 static __host__ __device__ inline size_t update_smem_total(int nk, int bc) {
     return update_smem(nk, bc) + (size_t)(bc / 32) * 4 + (size_t)nk;
@@ -253,8 +251,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
     int32_t *cnt = sel_s + BC;                            // [1]
     uint32_t *list = (uint32_t *)(cnt + 1);               // [BC * nk]
     uint32_t *fm = list + BC * nk;                        // [BC / 32] samples whose clause output is 1
-    uint32_t *qsel = fm + BC / 32;                        // [BC][(nk+31)/32] negative classes selected (q_select)
-    uint8_t *evt = (uint8_t *)(qsel + BC * ((nk + 31) >> 5));  // [BC * nk], valid at active pairs only
+    uint8_t *evt = (uint8_t *)(fm + BC / 32);             // [BC * nk], valid at active pairs only
     uint8_t *simple = evt + BC * nk;                      // [nk] no active sample of the class fired
     const int tid = WPC ? (int)(threadIdx.x & 31) : (int)threadIdx.x, nt = WPC ? 32 : (int)blockDim.x;
     const int lane = tid & 31;
@@ -331,27 +328,8 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
         //     parallel: 1 = update with target +1, 2 = with target -1; simple
         //     classes get their event type here (Ib when target and weight
         //     sign agree)
-        // q_select: the chunk's negative-class selections, a thread per sample
-        const bool use_qsel = cfg.coalesced && cfg.q_select && !cfg.one_negative;
-        if (use_qsel) {
-            for (int bl = tid; bl < bc; bl += nt) {
-                uint32_t *row = qsel + bl * KWm;
-                for (int m = 0; m < KWm; ++m) row[m] = 0u;
-                const uint64_t tb = t0 + (uint64_t)(b0 + bl);
-                qselect(cfg, [&](uint32_t sub) {
-                    return rk_ok ? draw_rk<7>(rk, g, tb, sub, TAG_CLASS, 0) : draw<7>(cfg.seed, g, tb, sub, TAG_CLASS, 0);
-                }, [&](int v) {
-                    const uint32_t bit = 1u << (v & 31);
-                    if (row[v >> 5] & bit) return false;
-                    row[v >> 5] |= bit;
-                    return true;
-                });
-            }
-            block_sync<WPC>();
-        }
         // two consecutive list entries per thread: when they are the two
-        // classes of one class pair of one sample, one Philox call serves both;
-        // negative classes not selected (q_select) need no draw
+        // classes of one class pair of one sample, one Philox call serves both
         for (int i0 = lo + 2 * tid; i0 < hi; i0 += 2 * nt) {  // coalesced: the chunk's pairs
             u32x4 r{};
             int rb = -1, rp = -1;
@@ -361,20 +339,12 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                 if (idx >= hi) break;
                 const uint32_t e = alist[idx];
                 const int b = (int)(e >> 16), k = (int)(e & 0xFFFFu);
-                uint8_t a;
-                if (use_qsel && (thr[(int64_t)b * K + k] >> 63) &&
-                    !((qsel[(b - b0) * KWm + (k >> 5)] >> (k & 31)) & 1u)) {
-                    a = EV_NONE;  // not selected (kernel.cu:573)
-                } else {
-                    if (b != rb || (k >> 1) != rp) {
-                        r = pair_draw(cfg, rk, rk_ok, g, t0 + (uint64_t)b, k);
-                        rb = b;
-                        rp = k >> 1;
-                    }
-                    uint2 u = class_words(r, (uint32_t)k);
-                    if (use_qsel) u.x = 0u;  // selected: passes the Q test
-                    a = decide_words(cfg, thr, b, k, K, u);
+                if (b != rb || (k >> 1) != rp) {
+                    r = pair_draw(cfg, rk, rk_ok, g, t0 + (uint64_t)b, k);
+                    rb = b;
+                    rp = k >> 1;
                 }
+                uint8_t a = decide_words(cfg, thr, b, k, K, class_words(r, (uint32_t)k));
                 if (simple[k]) a = (a && ((a == 1) == (wk[k] >= 0))) ? EV_T1B : EV_NONE;
                 evt[(b - b0) * nk + k] = a;
             }
