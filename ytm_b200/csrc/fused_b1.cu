@@ -31,6 +31,19 @@ constexpr int FB_WARPS = 8;
 #ifndef YTM_B1_CPB
 #define YTM_B1_CPB 48  // a multiple of FB_WARPS
 #endif
+// resident blocks per SM the register budget is sized for: 3 (at most 80
+// registers) for single-patch models; 4 (64) for convolutional ones, whose
+// per-sample work is short and latency-bound (measured on configuration 3:
+// 28.6k -> 34.5k samples/s); above 14 planes 64 registers would spill
+#ifndef YTM_B1_MINB
+#define YTM_B1_MINB 3
+#endif
+#ifndef YTM_B1_MINB_CONV
+#define YTM_B1_MINB_CONV 4
+#endif
+#ifndef YTM_B1_CPB_CONV
+#define YTM_B1_CPB_CONV 16  // a multiple of FB_WARPS
+#endif
 
 
 B1Ws b1_ws_layout(const ytm_config *cfg) {
@@ -63,11 +76,12 @@ __global__ void k_patch_words(const LitSrc src, int64_t n, uint32_t *__restrict_
 // warp streams the words of its clauses (8 per warp), applying the events and
 // evaluating sample i+1.
 template <int NB, int CPB, bool IMG>
-__global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
+__global__ void __launch_bounds__(FB_WARPS * 32, (CPB == YTM_B1_CPB_CONV && NB <= 14) ? YTM_B1_MINB_CONV : YTM_B1_MINB) k_fused_b1(
     ytm_config cfg, uint32_t *__restrict__ state, int32_t *__restrict__ weights, const int32_t *__restrict__ bias,
     const uint32_t *__restrict__ drop, const uint32_t *__restrict__ lits, const int32_t *__restrict__ Y, int64_t i,
     int64_t N, uint64_t t0, int do_update, int32_t *__restrict__ cs_ring, int32_t *__restrict__ sel_pp,
-    int32_t *__restrict__ ninc_ws, int32_t *__restrict__ patch_w, const RoundKeys rk, uint32_t *__restrict__ ring) {
+    int32_t *__restrict__ ninc_ws, int32_t *__restrict__ patch_w, const RoundKeys rk, uint32_t *__restrict__ ring,
+    int stage) {
     extern __shared__ __align__(16) unsigned char smraw[];
     // Programmatic dependent launch: let launch i+1 be scheduled now, and
     // wait here until launch i-1 has completed and its writes are visible.
@@ -104,6 +118,11 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     uint32_t *lw_s = ev_s + CPB * KB * 3;              // [FB_WARPS][W] non-zero include words (P > 1)
     uint32_t *li_s = lw_s + FB_WARPS * W;                 // [FB_WARPS][W] their include masks
     uint32_t *mb_s = li_s + FB_WARPS * W;                 // [FB_WARPS][PW] patch match bits
+    // P > 1 and stage: the patch words of sample i+1, [P][SW] with an odd row
+    // stride (lane p reads row p: 32 distinct banks); without stage (too
+    // large for shared memory) they are read where they lie, stride W
+    const int SW = W | 1;
+    uint32_t *xs_s = mb_s + FB_WARPS * ((cfg.patches + 31) >> 5);
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int do_eval = (i + 1 < N) || !do_update;       // the prologue evaluates sample 0
     const int64_t e_next = do_update ? i + 1 : 0;        // sample evaluated by this launch
@@ -113,6 +132,16 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     int32_t *sel_next = sel_pp + (e_next & 1) * (int64_t)C;     // picks of sample i+1
     const int P = cfg.patches, PW = (P + 31) >> 5;
     const uint64_t t = t0 + (uint64_t)i;
+    if (P > 1 && do_eval && stage) {
+        // stage sample i+1's patch words (written by the previous launch or
+        // the prologue's k_patch_words when they come from bit images): the
+        // per-patch include tests then wait on shared memory, not on L2
+        const uint32_t *src = lits_of + (IMG ? e_next % 3 : e_next) * PWW;
+        for (int idx = threadIdx.x; idx < P * W; idx += blockDim.x) {
+            const int p = idx / W;
+            xs_s[p * SW + (idx - p * W)] = src[idx];
+        }
+    }
     // Block b owns clauses b, b + G, b + 2G, ... (G = grid size): every block
     // gets an even share of every clause bank, so the bank of the true class,
     // where most feedback lands, does not pile up on a few blocks.
@@ -341,7 +370,6 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
     //     pick one matching patch uniformly (select_active, kernel.cu:285-316)
     if (do_eval && P > 1) {
         uint32_t *lw = lw_s + wib * W, *li = li_s + wib * W, *mb = mb_s + wib * PW;
-        const uint32_t *xs = words_of(e_next);
         const uint64_t t_next = t0 + (uint64_t)e_next;
 #pragma unroll 1
         for (int q = 0; q < CPW; ++q) {
@@ -371,7 +399,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, 3) k_fused_b1(
                     const int p = p0 + lane;
                     bool ok = p < P;
                     if (ok) {
-                        const uint32_t *xp = xs + (int64_t)p * W;
+                        const uint32_t *xp = stage ? xs_s + p * SW : words_of(e_next) + (int64_t)p * W;
                         for (int j = 0; j < n; ++j)
                             if (li[j] & ~xp[lw[j]]) { ok = false; break; }
                     }
@@ -432,7 +460,12 @@ static ytm_status launch_b1(const ytm_config *cfg, uint32_t *state, int32_t *wei
     const int blocks = (int)cdiv(C, CPB);
     const int nk = cfg->coalesced ? cfg->n_classes : 1;
     size_t smem = (size_t)cfg->n_classes * 12 + (size_t)CPB * ((nk + 31) / 32) * 12 + 16;
-    if (cfg->patches > 1) smem += (size_t)FB_WARPS * (2 * cfg->words + (cfg->patches + 31) / 32) * 4;
+    // convolutional models stage each sample's patch words in shared memory
+    // when they take at most 64 KB
+    const size_t stage_bytes = (size_t)cfg->patches * (cfg->words | 1) * 4;
+    const int stage = cfg->patches > 1 && stage_bytes <= 64 * 1024;
+    if (cfg->patches > 1)
+        smem += (size_t)FB_WARPS * (2 * cfg->words + (cfg->patches + 31) / 32) * 4 + (stage ? stage_bytes : 0);
     if (smem > 200 * 1024) return fail(YTM_ERR_UNSUPPORTED, "ytm_train_fit_b1: literal vector too long");
     if (smem > 48 * 1024 &&
         (rc = cuda_check(cudaFuncSetAttribute(k_fused_b1<NB, CPB, IMG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -454,7 +487,7 @@ static ytm_status launch_b1(const ytm_config *cfg, uint32_t *state, int32_t *wei
         const int upd = i < 0 ? 0 : 1;
         const RoundKeys rk = round_keys(c.seed, (uint32_t)((t0 + (uint64_t)ii) >> 32));  // keys of sample ii
         if ((rc = cuda_check(cudaLaunchKernelEx(&lc, k_fused_b1<NB, CPB, IMG>, c, state, weights, bias, drop, lits, Y, ii,
-                                                N, t0, upd, cs_ring, sel, ninc, patch_w, rk, ring),
+                                                N, t0, upd, cs_ring, sel, ninc, patch_w, rk, ring, stage),
                              "fused b1 launch")))
             return rc;
     }
@@ -480,12 +513,12 @@ extern "C" ytm_status ytm_train_fit_b1(const ytm_config *cfg, uint32_t *state, i
     int32_t *ninc = (int32_t *)(ws + l.ninc);
     uint32_t *ring = cfg->input_images ? (uint32_t *)(ws + l.ring) : nullptr;
     if ((rc = cuda_check(cudaMemsetAsync(cs_ring, 0, 3 * (size_t)cfg->n_classes * 4, st), "memset"))) return rc;
-    const int cpb = cfg->patches > 1 ? 16 : YTM_B1_CPB;
+    const int cpb = cfg->patches > 1 ? YTM_B1_CPB_CONV : YTM_B1_CPB;
     YTM_DISPATCH_PLANES(cfg->planes, {
-        // bit images only come with several patches (16 clauses per block)
-        rc = ring ? launch_b1<NB, 16, true>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel, ninc,
+        // bit images only come with several patches
+        rc = ring ? launch_b1<NB, YTM_B1_CPB_CONV, true>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel, ninc,
                                             patch_w, ring, st)
-             : cpb == 16 ? launch_b1<NB, 16, false>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel,
+             : cpb == YTM_B1_CPB_CONV ? launch_b1<NB, YTM_B1_CPB_CONV, false>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel,
                                                     ninc, patch_w, ring, st)
                          : launch_b1<NB, YTM_B1_CPB, false>(cfg, state, weights, bias, drop, lits, Y, N, t0, cs_ring, sel,
                                                     ninc, patch_w, ring, st);

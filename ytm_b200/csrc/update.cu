@@ -179,6 +179,9 @@ __device__ __forceinline__ void block_sync() {
 
 // Shared memory of one clause: weights [nk], picks [bc], count, event list
 // [bc*nk], fired samples [bc/32], event types [bc*nk], simple classes [nk].
+// An event list entry is row << 24 | type << 22 | run piece << 19 | class
+// (piece: 0 for a single event, mi + 1 for the first event of a Type Ib run
+// piece of 8 << mi events).
 // update_smem() (without the last two small arrays' padding) sizes the chunk.
 static __host__ __device__ inline size_t update_smem(int nk, int bc) {
     return (size_t)nk * 4 + (size_t)bc * 4 + 4 + (size_t)bc * nk * 4 + (size_t)bc * nk + 16;
@@ -486,8 +489,34 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
             if (lane == 0) cnt[0] = base;
         }
         block_sync<WPC>();
-        YTM_PHASE(4);
         const int nev = cnt[0];
+        // 2b. Type Ib run pieces, once per chunk: the first event of each run
+        //     of consecutive Type Ib events inside a run window marks its
+        //     pieces (64, 32, 16, 8 from the run start, the rest single
+        //     events) with code mi + 1 in bits 19..21 of their first entry
+        for (int e = tid; e < nev; e += nt) {
+            const uint32_t ent = list[e];
+            if (((ent >> 22) & 3u) != EV_T1B) continue;
+            const uint32_t win = (ent >> 24) >> win_shift;
+            if (e > 0) {
+                const uint32_t ep = list[e - 1];
+                if (((ep >> 22) & 3u) == EV_T1B && ((ep >> 24) >> win_shift) == win) continue;  // not a run start
+            }
+            int run = 1;
+            while (e + run < nev) {
+                const uint32_t en = list[e + run];
+                if (((en >> 22) & 3u) != EV_T1B || ((en >> 24) >> win_shift) != win) break;
+                ++run;
+            }
+            for (int q = e; run >= 8;) {
+                const int mi = run >= 64 ? 3 : (run >= 32 ? 2 : (run >= 16 ? 1 : 0));
+                list[q] |= (uint32_t)(mi + 1) << 19;
+                q += 8 << mi;
+                run -= 8 << mi;
+            }
+        }
+        block_sync<WPC>();
+        YTM_PHASE(4);
         // 3. stream the literal words
         if (nev > 0) {
             if (counters && tid == 0) n_events += (uint32_t)nev;
@@ -501,22 +530,14 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                     const uint32_t ent = list[e];
                     const int bl = (int)(ent >> 24);
                     const uint32_t ev = (ent >> 22) & 3u;
-                    const int k = k0 + (int)(ent & 0x3FFFFFu);
+                    const int k = k0 + (int)(ent & 0x7FFFFu);
                     const int b = b0 + bl;
                     const uint64_t t = t0 + (uint64_t)b;
                     ++n_units;
-                    if (ev == EV_T1B) {
-                        // a run of consecutive Type Ib events inside this
-                        // run window: pieces of 64, 32, 16, 8 from its start
-                        int run = 1;
-                        while (run < 64 && e + run < nev) {
-                            const uint32_t en = list[e + run];
-                            if (((en >> 22) & 3u) != EV_T1B || ((en >> 24) >> win_shift) != ((uint32_t)bl >> win_shift))
-                                break;
-                            ++run;
-                        }
-                        if (run >= 8) {
-                            const int mi = run >= 64 ? 3 : (run >= 32 ? 2 : (run >= 16 ? 1 : 0));
+                    {
+                        const uint32_t piece = (ent >> 19) & 7u;
+                        if (piece) {  // a Type Ib run piece of 8 << mi events
+                            const int mi = (int)piece - 1;
                             uint32_t D[7];
                             run_counts(cfg, mi, [&](uint32_t i) {
                                 const uint32_t sub = 0x40000000u | ((uint32_t)w << 2) | i;
