@@ -83,8 +83,8 @@ typedef struct ytm_config {
     uint64_t q_threshold;      /* negative-class selection, thr / 2^32          */
     uint32_t run_cdf16[4][65]; /* Type Ib runs of m = 8, 16, 32, 64 events: per
                                   literal decrement count Binomial(m, 1/s);
-                                  entry d = floor(65536 * P(count <= d)),
-                                  65536 from d = m on                        */
+                                  entry d = 65536 * P(count <= d) rounded to
+                                  nearest, 65536 from d = m on               */
     /* clause shard held by this process */
     int32_t clause_lo;         /* first global clause index                     */
     int32_t clause_count;      /* clauses held (C above)                        */
@@ -104,6 +104,10 @@ typedef struct ytm_config {
                                   (models with several patches only)          */
     int32_t image_words;       /* ceil(dim0*dim1*dim2 / 32) + 1 (one padding
                                   word)                                        */
+    uint32_t run_range[4];     /* per run size: lo | hi << 16, run_cdf16
+                                  entries below lo are 0 and entries from hi
+                                  on are 65536 (the thresholds a draw tests
+                                  lie in [lo, hi))                             */
 } ytm_config;
 
 /* Fill *cfg.  Arguments mirror BaseTM.__init__ (base.py:42-92) and its defaults
@@ -241,7 +245,7 @@ ytm_status ytm_train_eval(const ytm_config *cfg, const uint32_t *state, const in
  * workspace: the one ytm_train_eval filled for this batch; without
  * sel_override this call reads the picks from it (single-patch models: the
  * clause outputs, kept there clause by clause).  Limits: at most 65,535
- * classes and 65,535 samples per batch; for batches above 64 samples, at
+ * classes and 32,767 samples per batch; for batches above 64 samples, at
  * most about 700 classes (a chunk's event list lives in shared memory);
  * beyond them YTM_ERR_UNSUPPORTED. */
 ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, int32_t *weights,

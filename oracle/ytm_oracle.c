@@ -105,7 +105,7 @@ static void run_cdf(double s, uint32_t out[4][65]) {
         for (int i = 0; i < m; ++i) pmf *= q;
         for (int d = 0; d < m; ++d) {
             acc += pmf;
-            const double v = floor(acc * 65536.0);
+            const double v = floor(acc * 65536.0 + 0.5); /* nearest: a tail below 2^-17 is never drawn */
             out[mi][d] = v >= 65536.0 ? 65536u : (uint32_t)v;
             pmf = pmf * (double)(m - d) / (double)(d + 1) * p / q;
         }
@@ -553,10 +553,18 @@ static void type1b(const orc_cfg *c, uint32_t *st, uint32_t g, uint64_t t, uint3
  * decrements every literal with st > 0 with probability 1/s).  Decrements
  * with a floor at 0 commute, so the run leaves st - d clamped at 0, d the
  * literal's number of successes, Binomial(m, 1/s): drawn per literal by
- * inverse CDF from a 16-bit uniform.  The uniforms of word w are the 16-bit
- * halves of four Philox4x32-7 calls at sub-indices 0x40000000 | 4w | i keyed
- * on the run's first event (t, k): literal j of the word takes half j & 1 of
- * word (j >> 1) & 3 of call j >> 3. */
+ * inverse CDF from a 16-bit uniform.  The uniforms of word w come from four
+ * Philox4x32-7 calls at sub-indices 0x40000000 | 4w | i keyed on the run's
+ * first event (t, k), as bit planes: bit b of literal j's uniform is bit j of
+ * word b & 3 of call b >> 2. */
+/* Literal j's 16-bit uniform from the four calls R of a word: bit b is bit j
+ * of word b & 3 of call b >> 2. */
+static uint32_t run_uniform(const uint32_t R[4][4], int j) {
+    uint32_t u = 0;
+    for (int b = 0; b < 16; ++b) u |= ((R[b >> 2][b & 3] >> j) & 1u) << b;
+    return u;
+}
+
 static void type1b_run(const orc_cfg *c, uint32_t *st, uint32_t g, uint64_t t, uint32_t k, int mi) {
     const int L = c->L, m = RUN_SIZES[mi];
     for (int w = 0; w * 32 < L; ++w) {
@@ -564,7 +572,7 @@ static void type1b_run(const orc_cfg *c, uint32_t *st, uint32_t g, uint64_t t, u
         for (uint32_t i = 0; i < 4; ++i)
             draw_r(c, g, t, 0x40000000u | ((uint32_t)w << 2) | i, TAG_SMASK, k, 7, R[i]);
         for (int j = 0; j < 32 && w * 32 + j < L; ++j) {
-            const uint32_t u = (R[j >> 3][(j >> 1) & 3] >> (16 * (j & 1))) & 0xFFFFu;
+            const uint32_t u = run_uniform(R, j);
             int d = 0;
             while (d < m && u >= c->run_cdf16[mi][d]) ++d;
             uint32_t *x = &st[w * 32 + j];
@@ -579,7 +587,7 @@ void orc_run_counts(const orc_cfg *c, uint32_t g, uint64_t t, uint32_t k, uint32
     uint32_t R[4][4];
     for (uint32_t i = 0; i < 4; ++i) draw_r(c, g, t, 0x40000000u | (w << 2) | i, TAG_SMASK, k, 7, R[i]);
     for (int j = 0; j < 32; ++j) {
-        const uint32_t u = (R[j >> 3][(j >> 1) & 3] >> (16 * (j & 1))) & 0xFFFFu;
+        const uint32_t u = run_uniform(R, j);
         int d = 0;
         while (d < m && u >= c->run_cdf16[mi][d]) ++d;
         out[j] = (uint32_t)d;

@@ -38,6 +38,12 @@ def test_config_matches_oracle(name):
     assert (cfg.clauses, cfg.literals, cfg.words, cfg.patches) == (o.C, o.L, o.W, o.P)
     assert cfg.state_top == o.state_top and cfg.half_state == o.half_state
     assert list(cfg.s_count_cdf) == list(o.cfg.s_cdf) and cfg.q_threshold == o.cfg.q_thr
+    for mi in range(4):
+        cdf = list(cfg.run_cdf16[mi])
+        assert cdf == list(o.cfg.run_cdf16[mi])
+        lo, hi = cfg.run_range[mi] & 0xFFFF, cfg.run_range[mi] >> 16
+        assert all(v == 0 for v in cdf[:lo]) and all(0 < v < 65536 for v in cdf[lo:hi])
+        assert all(v == 65536 for v in cdf[hi:])
     # include iff state > half  <=>  stored value has the top plane set
     assert cfg.half_state + 1 + cfg.state_offset == 1 << (cfg.planes - 1)
     assert cfg.state_top + cfg.state_offset == (1 << cfg.planes) - 1

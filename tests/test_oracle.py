@@ -170,10 +170,10 @@ def test_oracle_threads():
 
 
 def _run_spec(o, clause, t, k, w, mi):
-    """Type Ib run counts restated from their definition: literal j's 16-bit
-    uniform is half j & 1 of word (j >> 1) & 3 of the Philox4x32-7 call
-    j >> 3 at sub-index 0x40000000 | 4w | (j >> 3); its count is the first d
-    with u < cdf[d]."""
+    """Type Ib run counts restated from their definition: bit b of literal
+    j's 16-bit uniform is bit j of word b & 3 of the Philox4x32-7 call b >> 2
+    at sub-index 0x40000000 | 4w | (b >> 2); its count is the first d with
+    u < cdf[d]."""
     seed = o.cfg.seed
     key = [seed & 0xFFFFFFFF, ((seed >> 32) ^ (t >> 32)) & 0xFFFFFFFF]
     calls = [[int(v) for v in O.philox4x32([clause, t & 0xFFFFFFFF, 0x40000000 | (w << 2) | i, 2 | (k << 2)],
@@ -182,7 +182,7 @@ def _run_spec(o, clause, t, k, w, mi):
     m = 8 << mi
     out = []
     for j in range(32):
-        u = (calls[j >> 3][(j >> 1) & 3] >> (16 * (j & 1))) & 0xFFFF
+        u = sum(((calls[b >> 2][b & 3] >> j) & 1) << b for b in range(16))
         d = 0
         while d < m and u >= cdf[d]:
             d += 1

@@ -52,6 +52,7 @@ class Config(ct.Structure):
         ("clause_lo", ct.c_int32), ("clause_count", ct.c_int32),
         ("one_negative", ct.c_int32), ("count_empty", ct.c_int32),
         ("input_images", ct.c_int32), ("image_words", ct.c_int32),
+        ("run_range", ct.c_uint32 * 4),
     ]
 
 

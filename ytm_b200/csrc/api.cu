@@ -62,7 +62,7 @@ TrainWs train_ws_layout(const ytm_config *cfg, int64_t B) {
     l.amask = o; o = align_up(o + (uint64_t)B * cdiv(K, 32) * 4, 256);
     l.colm = o;  o = align_up(o + K * cdiv(B, 32) * 4, 256);
     l.row_off = o; o = align_up(o + ((uint64_t)B + 1) * 4, 256);
-    l.alist = o; o = align_up(o + (uint64_t)B * K * 4, 256);
+    l.alist = o; o = align_up(o + (uint64_t)B * K * 8, 256);
     l.pair = o;  o = align_up(o + (uint64_t)B * 2 * 4, 256);
     l.sparse = o; o = align_up(o + sparse_ws_bytes(cfg), 256);  // compacted include words (sparse patch match)
     l.pwords = o; o += batch_words_bytes(cfg, B);  // bit-image input: the batch's patch literal words
@@ -172,8 +172,10 @@ ytm_status ytm_config_init(ytm_config *cfg, int32_t clauses_per_class, int32_t T
         }
     }
     // Type Ib run tables: per literal Binomial(m, p) decrement counts for runs
-    // of m = 8, 16, 32, 64 events; entry d = floor(65536 * P(count <= d)),
-    // 65536 from d = m on, from the same pmf recurrence
+    // of m = 8, 16, 32, 64 events; entry d = P(count <= d) * 65536 rounded to
+    // the nearest integer, 65536 from d = m on, from the same pmf recurrence;
+    // run_range: entries below lo are 0 (those counts are certain), entries
+    // from hi on are 65536 (never exceeded)
     {
         double p = 1.0 / s;
         if (!(p > 0.0)) p = 0.0;
@@ -190,10 +192,16 @@ ytm_status ytm_config_init(ytm_config *cfg, int32_t clauses_per_class, int32_t T
             for (int i = 0; i < m; ++i) pmf *= qq;
             for (int d = 0; d < m; ++d) {
                 acc += pmf;
-                const double v = floor(acc * 65536.0);
+                const double v = floor(acc * 65536.0 + 0.5);  // nearest: a tail below 2^-17 is never drawn
                 cfg->run_cdf16[mi][d] = v >= 65536.0 ? 65536u : (uint32_t)v;
                 pmf = pmf * (double)(m - d) / (double)(d + 1) * p / qq;
             }
+        }
+        for (int mi = 0; mi < 4; ++mi) {
+            uint32_t lo = 0, hi = 0;
+            while (lo < 64 && cfg->run_cdf16[mi][lo] == 0u) ++lo;
+            while (hi < 64 && cfg->run_cdf16[mi][hi] < 65536u) ++hi;
+            cfg->run_range[mi] = lo | (hi << 16);
         }
     }
     {

@@ -202,53 +202,90 @@ __device__ __forceinline__ uint32_t smask_word_rk(const ytm_config &cfg, const R
 // decrements every literal with a positive state with probability 1/s).
 // Decrements with a floor at 0 commute, so the run leaves state - d clamped
 // at 0, with d the literal's number of successes, Binomial(m, 1/s), drawn by
-// inverse CDF from a 16-bit uniform: literal j of word w takes half j & 1 of
-// word (j >> 1) & 3 of the Philox4x32-7 call j >> 3, at sub-index
-// 0x40000000 | 4w | (j >> 3), keyed on the run's first event.  D receives
-// the counts as bit planes (d <= 64 needs 7).  The first six comparisons are
-// branch-free; only counts of 6 or more continue in the loop.
+// inverse CDF from a 16-bit uniform: d = #{e : u >= run_cdf16[mi][e]}.  The
+// uniforms of the 32 literals of word w come as bit planes: plane b (bit b of
+// every literal's uniform, literal j at bit j) is word b & 3 of the
+// Philox4x32-7 call b >> 2 at sub-index 0x40000000 | 4w | (b >> 2), keyed on
+// the run's first event.  So all 32 comparisons with one threshold c are one
+// bit-sliced carry chain: u >= c exactly when u + (65536 - c) carries out of
+// bit 15, and the carry through plane b is the majority of the plane, bit b
+// of the constant and the incoming carry (one LOP3 per plane).  The masks
+// "d >= j" are nested, so bit b of d is the parity of the masks of the j
+// divisible by 2^b; D receives the counts as bit planes (d <= 64 needs 7).
+// Thresholds outside run_range (0: certain, 65536: never) are not tested,
+// and the chain stops once no literal of the thread reaches the next one.
+__device__ __forceinline__ uint32_t maj3(uint32_t a, uint32_t b, uint32_t c) {
+    return (a & b) | (c & (a | b));
+}
+
+// The thresholds' plane masks (16 per threshold: all ones where the constant
+// 65536 - c has a one) for every run size, in shared memory: the table of run
+// size mi starts at threshold run_table_base(cfg, mi); a kernel that keeps it
+// saves the 32 instructions per threshold that forming the masks takes.
+__host__ __device__ inline int run_table_base(const ytm_config &cfg, int mi) {
+    int n = 0;
+    for (int i = 0; i < mi; ++i) n += (int)(cfg.run_range[i] >> 16) - (int)(cfg.run_range[i] & 0xFFFFu);
+    return n;
+}
+__host__ __device__ inline size_t run_table_bytes(const ytm_config &cfg) { return (size_t)run_table_base(cfg, 4) * 64; }
+__device__ inline void run_table_fill(const ytm_config &cfg, uint4 *tab, int tid, int nt) {
+    const int n = run_table_base(cfg, 4);
+    for (int i = tid; i < n * 4; i += nt) {
+        int e = i >> 2, mi = 0;
+        for (; mi < 3; ++mi) {
+            const int len = (int)(cfg.run_range[mi] >> 16) - (int)(cfg.run_range[mi] & 0xFFFFu);
+            if (e < len) break;
+            e -= len;
+        }
+        const int j = (int)(cfg.run_range[mi] & 0xFFFFu) + 1 + e;
+        const uint32_t k = 65536u - cfg.run_cdf16[mi][j - 1], q = (uint32_t)(i & 3) * 4u;
+        tab[i] = make_uint4(0u - ((k >> q) & 1u), 0u - ((k >> (q + 1)) & 1u), 0u - ((k >> (q + 2)) & 1u),
+                            0u - ((k >> (q + 3)) & 1u));
+    }
+}
+
+// km: the plane masks of run size mi (run_table_fill's table at
+// run_table_base(cfg, mi)), or nullptr to form them in registers.
 template <typename DrawFn>
 __device__ __forceinline__ void run_counts(const ytm_config &cfg, int mi, DrawFn drawi, uint32_t (&D)[7],
-                                           uint32_t &calls) {
+                                           uint32_t &calls, const uint4 *km) {
+    uint32_t R[16];
 #pragma unroll
-    for (int b = 0; b < 7; ++b) D[b] = 0u;
-    const int m = 8 << mi;
-#pragma unroll 1
-    for (int i = 0; i < 4; ++i) {  // not unrolled: keeps the feedback loop's code small
+    for (int i = 0; i < 4; ++i) {
         const u32x4 r = drawi((uint32_t)i);
-        ++calls;
-        const uint32_t R[4] = {r.x, r.y, r.z, r.w};
-        // the eight counts as nibbles (capped at 15; larger ones flagged),
-        // then transposed into four bit planes
-        uint32_t acc = 0u, big = 0u;
+        R[4 * i] = r.x;
+        R[4 * i + 1] = r.y;
+        R[4 * i + 2] = r.z;
+        R[4 * i + 3] = r.w;
+    }
+    calls += 4u;
+    const uint32_t rr = cfg.run_range[mi];
+    const int lo = (int)(rr & 0xFFFFu), hi = (int)(rr >> 16);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const uint32_t u = (R[q >> 1] >> (16 * (q & 1))) & 0xFFFFu;
-            uint32_t d = 0;
+    for (int b = 0; b < 7; ++b) D[b] = ((lo >> b) & 1) ? 0xFFFFFFFFu : 0u;  // d >= lo for every literal
+#pragma unroll 1
+    for (int j = lo + 1; j <= hi; ++j) {
+        uint32_t cy = 0u;
+        if (km) {
+            const uint4 *m = km + (j - lo - 1) * 4;
 #pragma unroll
-            for (int e = 0; e < 6; ++e) d += u >= cfg.run_cdf16[mi][e] ? 1u : 0u;
-            if (d == 6u)
-                while ((int)d < m && u >= cfg.run_cdf16[mi][d]) ++d;
-            acc |= (d > 15u ? 15u : d) << (4 * q);
-            big |= (d > 15u ? 1u : 0u) << q;
+            for (int q = 0; q < 4; ++q) {
+                const uint4 mm = m[q];
+                cy = maj3(R[4 * q], mm.x, cy);
+                cy = maj3(R[4 * q + 1], mm.y, cy);
+                cy = maj3(R[4 * q + 2], mm.z, cy);
+                cy = maj3(R[4 * q + 3], mm.w, cy);
+            }
+        } else {
+            const uint32_t k = 65536u - cfg.run_cdf16[mi][j - 1];
+#pragma unroll
+            for (int b = 0; b < 16; ++b) cy = maj3(R[b], 0u - ((k >> b) & 1u), cy);
         }
+        if (!cy) break;  // d < j for all 32 literals, and the masks are nested
+        const int tz = __ffs(j) - 1;
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            uint32_t x = (acc >> b) & 0x11111111u;
-            x = (x | (x >> 3)) & 0x03030303u;
-            x = (x | (x >> 6)) & 0x000F000Fu;
-            x = (x | (x >> 12)) & 0xFFu;
-            D[b] |= x << (8 * i);
-        }
-        for (; big; big &= big - 1u) {  // counts of 16 or more (rare)
-            const int q = __ffs(big) - 1;
-            const uint32_t u = (R[q >> 1] >> (16 * (q & 1))) & 0xFFFFu;
-            uint32_t d = 0;
-            while ((int)d < m && u >= cfg.run_cdf16[mi][d]) ++d;
-            const uint32_t bit = 1u << (i * 8 + q);
-#pragma unroll
-            for (int b = 0; b < 7; ++b) D[b] = (D[b] & ~bit) | (((d >> b) & 1u) ? bit : 0u);
-        }
+        for (int b = 0; b < 7; ++b)
+            if (b <= tz) D[b] ^= cy;
     }
 }
 

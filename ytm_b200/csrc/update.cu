@@ -39,14 +39,22 @@ static_assert(UPD_BC_MAX <= 256, "event list rows are 8 bits");
 //    rules, k is one of the sample's two classes.  Once a model has converged
 //    most class sums sit at +-T and few pairs stay active.
 //  * amask[b][k / 32] and colm[k][b / 32] hold the active pairs as bits per
-//    sample and per class; alist lists them (sample << 16 | class) in feedback order (sample by
-//    sample; classes in order, or pytm's true class first) and row_off[b] is
-//    the position of sample b's first pair in it (row_off[B] = the count).
+//    sample and per class; alist lists them in feedback order (sample by
+//    sample; classes in order, or pytm's true class first), each entry
+//    (threshold - 1) << 32 | negative << 31 | sample << 16 | class, so that the
+//    feedback reads a pair's decision inputs in one contiguous load; row_off[b]
+//    is the position of sample b's first pair in it (row_off[B] = the count).
+// An active pair's list entry (its threshold is at least 1, at most 2^32).
+__device__ __forceinline__ uint64_t pair_entry(const uint64_t *__restrict__ thr, int b, int k, int K) {
+    const uint64_t th = thr[(int64_t)b * K + k];
+    return (((th & ~(1ull << 63)) - 1ull) << 32) | ((th >> 63) << 31) | ((uint64_t)b << 16) | (uint64_t)k;
+}
+
 __global__ void __launch_bounds__(1024) k_thresholds(const int32_t *__restrict__ cs, const int32_t *__restrict__ Y,
                                                      int B, int K, int T, int one_neg,
                                                      const int32_t *__restrict__ pair, uint64_t *__restrict__ thr,
                                                      uint32_t *__restrict__ amask, uint32_t *__restrict__ colm,
-                                                     int32_t *__restrict__ row_off, uint32_t *__restrict__ alist) {
+                                                     int32_t *__restrict__ row_off, uint64_t *__restrict__ alist) {
     constexpr int AM_SMEM = 8192;  // words of amask kept in shared memory
     __shared__ uint32_t am_s[AM_SMEM];
     __shared__ int wsum[32];
@@ -126,12 +134,12 @@ __global__ void __launch_bounds__(1024) k_thresholds(const int32_t *__restrict__
             if (one_neg) {
                 for (int q = 0; q < 2; ++q) {
                     const int k = pair[2 * row + q];
-                    if (k >= 0 && ((am[k >> 5] >> (k & 31)) & 1u)) alist[pos++] = ((uint32_t)row << 16) | (uint32_t)k;
+                    if (k >= 0 && ((am[k >> 5] >> (k & 31)) & 1u)) alist[pos++] = pair_entry(thr, row, k, K);
                 }
             } else {
                 for (int m = 0; m < KWm; ++m)
                     for (uint32_t v = am[m]; v; v &= v - 1u)
-                        alist[pos++] = ((uint32_t)row << 16) | (uint32_t)(m * 32 + __ffs(v) - 1);
+                        alist[pos++] = pair_entry(thr, row, m * 32 + __ffs(v) - 1, K);
             }
         }
         __syncthreads();
@@ -236,11 +244,15 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                                                 int count_patch, const int32_t *__restrict__ pair,
                                                 const uint32_t *__restrict__ amask, const uint32_t *__restrict__ colm,
                                                 const int32_t *__restrict__ row_off,
-                                                const uint32_t *__restrict__ alist,
+                                                const uint64_t *__restrict__ alist,
                                                 const uint32_t *__restrict__ fcm,
                                                 unsigned long long *__restrict__ counters) {
     extern __shared__ __align__(16) unsigned char small[];
     const int C = cfg.clause_count, W = cfg.words, K = cfg.n_classes;
+    // the Type Ib run thresholds' plane masks, after the clauses' arrays
+    uint4 *kmt = (uint4 *)(small + (WPC ? (blockDim.x >> 5) : 1u) * update_smem_aligned(cfg.coalesced ? K : 1, BC));
+    run_table_fill(cfg, kmt, (int)threadIdx.x, (int)blockDim.x);
+    __syncthreads();
     const int c = WPC ? (int)(blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) : (int)blockIdx.x;
     if (c >= C) return;
     const uint32_t g = (uint32_t)(cfg.clause_lo + c);
@@ -331,23 +343,29 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
         //     parallel: 1 = update with target +1, 2 = with target -1; simple
         //     classes get their event type here (Ib when target and weight
         //     sign agree)
-        // two consecutive list entries per thread: when they are the two
-        // classes of one class pair of one sample, one Philox call serves both
-        for (int i0 = lo + 2 * tid; i0 < hi; i0 += 2 * nt) {  // coalesced: the chunk's pairs
-            u32x4 r{};
-            int rb = -1, rp = -1;
+        // four consecutive list entries per thread, loaded together; when two
+        // neighbours are the two classes of one class pair of one sample, one
+        // Philox call serves both
+        for (int i0 = lo + 4 * tid; i0 < hi; i0 += 4 * nt) {  // coalesced: the chunk's pairs
+            uint64_t ent[4];
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int idx = i0 + j;
-                if (idx >= hi) break;
-                const uint32_t e = alist[idx];
-                const int b = (int)(e >> 16), k = (int)(e & 0xFFFFu);
-                if (b != rb || (k >> 1) != rp) {
+            for (int j = 0; j < 4; ++j) ent[j] = i0 + j < hi ? alist[i0 + j] : 0ull;
+            u32x4 r{};
+            uint32_t rkey = 0xFFFFFFFFu;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (i0 + j >= hi) break;
+                const uint64_t e = ent[j];
+                const int b = (int)((e >> 16) & 0x7FFFu), k = (int)(e & 0xFFFFu);
+                const uint32_t key = ((uint32_t)e & 0x7FFFFFFFu) >> 1;  // (sample, class pair)
+                if (key != rkey) {
                     r = pair_draw(cfg, rk, rk_ok, g, t0 + (uint64_t)b, k);
-                    rb = b;
-                    rp = k >> 1;
+                    rkey = key;
                 }
-                uint8_t a = decide_words(cfg, thr, b, k, K, class_words(r, (uint32_t)k));
+                const uint2 u = class_words(r, (uint32_t)k);
+                const bool neg = (e >> 31) & 1u;
+                const bool pass = cfg.one_negative || !neg || (uint64_t)u.x < cfg.q_threshold;  // kernel.cu:573
+                uint8_t a = (pass && u.y <= (uint32_t)(e >> 32)) ? (neg ? 2 : 1) : 0;          // kernel.cu:582
                 if (simple[k]) a = (a && ((a == 1) == (wk[k] >= 0))) ? EV_T1B : EV_NONE;
                 evt[(b - b0) * nk + k] = a;
             }
@@ -543,7 +561,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                                 const uint32_t sub = 0x40000000u | ((uint32_t)w << 2) | i;
                                 return rk_ok ? draw_rk<7>(rk, g, t, sub, TAG_SMASK, (uint32_t)k)
                                              : draw<7>(cfg.seed, g, t, sub, TAG_SMASK, (uint32_t)k);
-                            }, D, n_calls);
+                            }, D, n_calls, kmt + 4 * run_table_base(cfg, mi));
 #pragma unroll
                             for (int i = 0; i < 7; ++i) D[i] &= vm;
                             ctr.sub_floor(D, zero_s, top2);
@@ -610,9 +628,9 @@ extern "C" ytm_status ytm_train_update_counted(const ytm_config *cfg, uint32_t *
     if (!state || !weights || !cs || !Y || !lits || !workspace) return fail(YTM_ERR_ARG, "null pointer");
     const int count_patch = single_patch_eval(cfg) ? 1 : 0;
     if (count_patch && !patch_w) return fail(YTM_ERR_ARG, "patch_w is NULL");
-    // active-pair list entries hold (sample << 16 | class)
-    if (cfg->n_classes > 65535 || B > 65535)
-        return fail(YTM_ERR_UNSUPPORTED, "feedback handles at most 65,535 classes and 65,535 samples per batch");
+    // active-pair list entries hold sample << 16 | class (and a sign bit above)
+    if (cfg->n_classes > 65535 || B > 32767)
+        return fail(YTM_ERR_UNSUPPORTED, "feedback handles at most 65,535 classes and 32,767 samples per batch");
     if ((int64_t)B * cfg->n_classes >= (1ll << 32)) return fail(YTM_ERR_UNSUPPORTED, "batch x classes above 2^32");
     cudaStream_t st = as_stream(stream);
     TrainWs l = train_ws_layout(cfg, B);
@@ -626,7 +644,7 @@ extern "C" ytm_status ytm_train_update_counted(const ytm_config *cfg, uint32_t *
     uint32_t *amask = (uint32_t *)(ws + l.amask);
     uint32_t *colm = (uint32_t *)(ws + l.colm);
     int32_t *row_off = (int32_t *)(ws + l.row_off);
-    uint32_t *alist = (uint32_t *)(ws + l.alist);
+    uint64_t *alist = (uint64_t *)(ws + l.alist);
     if (cfg->one_negative) {
         k_pairs<<<(unsigned)cdiv(B, 256), 256, 0, st>>>(cfg->seed, Y, B, cfg->n_classes, t0, pair);
         if ((rc = launch_check("class pairs"))) return rc;
@@ -639,7 +657,7 @@ extern "C" ytm_status ytm_train_update_counted(const ytm_config *cfg, uint32_t *
     // most one window, else one window (128 samples, or 64 above 256 classes)
     const int win = run_window(*cfg);
     int BC = B <= win ? ((B + 31) / 32) * 32 : win;
-    const size_t smem = update_smem_total(nk, BC);
+    const size_t smem = update_smem_aligned(nk, BC) + run_table_bytes(*cfg);
     if (smem > 227 * 1024) return fail(YTM_ERR_UNSUPPORTED, "too many classes for the feedback kernel");
     // round keys for the batch's samples when they share the counter's high word
     // the literal source of the feedback: the batch's patch literal words;
@@ -658,7 +676,7 @@ extern "C" ytm_status ytm_train_update_counted(const ytm_config *cfg, uint32_t *
     const int rk_ok = (t0 >> 32) == ((t0 + (uint64_t)B - 1) >> 32);
     const int W = cfg->words;
     // small batches: one warp per clause, 8 clauses per block
-    const size_t smem_wpc = 8 * update_smem_aligned(nk, 32);
+    const size_t smem_wpc = 8 * update_smem_aligned(nk, 32) + run_table_bytes(*cfg);
     if (B <= 32 && smem_wpc <= 48 * 1024) {
         YTM_DISPATCH_PLANES(cfg->planes, {
             k_update<NB, true><<<(unsigned)cdiv(cfg->clause_count, 8), 256, smem_wpc, st>>>(
