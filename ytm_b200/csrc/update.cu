@@ -186,7 +186,8 @@ __device__ __forceinline__ void block_sync() {
 }
 
 // Shared memory of one clause: weights [nk], picks [bc], count, event list
-// [bc*nk], fired samples [bc/32], event types [bc*nk], simple classes [nk].
+// [bc*nk], fired samples [bc/32], event types [bc*nk], simple classes [nk],
+// pairs with an event as bits [bc][ceil(nk/32)].
 // An event list entry is row << 24 | type << 22 | run piece << 19 | class
 // (piece: 0 for a single event, mi + 1 for the first event of a Type Ib run
 // piece of 8 << mi events).
@@ -195,7 +196,7 @@ static __host__ __device__ inline size_t update_smem(int nk, int bc) {
     return (size_t)nk * 4 + (size_t)bc * 4 + 4 + (size_t)bc * nk * 4 + (size_t)bc * nk + 16;
 }
 static __host__ __device__ inline size_t update_smem_total(int nk, int bc) {
-    return update_smem(nk, bc) + (size_t)(bc / 32) * 4 + (size_t)nk;
+    return update_smem(nk, bc) + (size_t)(bc / 32) * 4 + (size_t)nk + 4 + (size_t)bc * ((nk + 31) / 32) * 4;
 }
 static __host__ __device__ inline size_t update_smem_aligned(int nk, int bc) {
     return (update_smem_total(nk, bc) + 15) & ~(size_t)15;
@@ -268,6 +269,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
     uint32_t *fm = list + BC * nk;                        // [BC / 32] samples whose clause output is 1
     uint8_t *evt = (uint8_t *)(fm + BC / 32);             // [BC * nk], valid at active pairs only
     uint8_t *simple = evt + BC * nk;                      // [nk] no active sample of the class fired
+    uint32_t *enz = (uint32_t *)(((uintptr_t)(simple + nk) + 3) & ~(uintptr_t)3);  // [BC][KWm] pairs with an event
     const int tid = WPC ? (int)(threadIdx.x & 31) : (int)threadIdx.x, nt = WPC ? 32 : (int)blockDim.x;
     const int lane = tid & 31;
     // include count of the batch-start state (pack_clauses, kernel.cu:155-204):
@@ -303,6 +305,9 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
     // the stored maximum is 2^(NB-1) + 2^(NB-2) - 1 (power-of-two state counts)
     const bool max_pow2 = NB >= 3 && max_s == (1u << (NB - 1)) + (1u << (NB >= 2 ? NB - 2 : 0)) - 1u;
     const uint32_t *mycol = colm + (int64_t)k0 * BW;  // non-coalesced: the active samples of the bank's class
+    // the pairs holding an event, as bits kept by the decision phases (the
+    // compaction over all threads reads them)
+    const bool use_enz = !WPC && cfg.coalesced && !cfg.one_negative;
 
     for (int kk = tid; kk < nk; kk += nt) wk[kk] = weights[(int64_t)c * K + k0 + kk];
 
@@ -336,6 +341,8 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
             for (int gi = 0; gi < (bc + 31) >> 5; ++gi) hit |= cm[gi] & fm[gi];
             simple[kk] = hit == 0u;
         }
+        if (use_enz)
+            for (int i = tid; i < bc * KWm; i += nt) enz[i] = 0u;
         block_sync<WPC>();
         YTM_PHASE(1);
         const int lo = cfg.coalesced ? row_off[b0] : 0, hi = cfg.coalesced ? row_off[b0 + bc] : 0;
@@ -368,6 +375,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                 uint8_t a = (pass && u.y <= (uint32_t)(e >> 32)) ? (neg ? 2 : 1) : 0;          // kernel.cu:582
                 if (simple[k]) a = (a && ((a == 1) == (wk[k] >= 0))) ? EV_T1B : EV_NONE;
                 evt[(b - b0) * nk + k] = a;
+                if (use_enz && a) atomicOr(&enz[(b - b0) * KWm + (k >> 5)], 1u << (k & 31));
             }
         }
         if (!cfg.coalesced)
@@ -409,6 +417,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                         }
                     }
                     evt[bl * nk + kk] = ev;
+                    if (use_enz && a && ev == EV_NONE) atomicAnd(&enz[bl * KWm + (kk >> 5)], ~(1u << (kk & 31)));
                 }
             }
             wk[kk] = wv;
@@ -433,10 +442,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                 if (u < units) {
                     row = u / KWm;
                     m = u - row * KWm;
-                    for (uint32_t v = amask[(int64_t)(b0 + row) * KWm + m]; v; v &= v - 1u) {
-                        const int bit = __ffs(v) - 1;
-                        if (evt[row * nk + m * 32 + bit] != EV_NONE) em |= 1u << bit;
-                    }
+                    em = enz[row * KWm + m];
                 }
                 const int n = __popc(em);
                 int incl = n;
