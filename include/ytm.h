@@ -81,7 +81,7 @@ typedef struct ytm_config {
                                   Binomial(32, 1/s); entry n = floor(2^32 *
                                   P(count <= n)), saturated at 2^32 - 1     */
     uint64_t q_threshold;      /* negative-class selection, thr / 2^32          */
-    uint32_t run_cdf16[4][65]; /* Type Ib runs of m = 8, 16, 32, 64 events: per
+    uint32_t run_cdf16[8][65]; /* Type Ib runs of m = 8, 16, ..., 64 events: per
                                   literal decrement count Binomial(m, 1/s);
                                   entry d = 65536 * P(count <= d) rounded to
                                   nearest, 65536 from d = m on               */
@@ -104,7 +104,7 @@ typedef struct ytm_config {
                                   (models with several patches only)          */
     int32_t image_words;       /* ceil(dim0*dim1*dim2 / 32) + 1 (one padding
                                   word)                                        */
-    uint32_t run_range[4];     /* per run size: lo | hi << 16, run_cdf16
+    uint32_t run_range[8];     /* per run size: lo | hi << 16, run_cdf16
                                   entries below lo are 0 and entries from hi
                                   on are 65536 (the thresholds a draw tests
                                   lie in [lo, hi))                             */

@@ -49,7 +49,7 @@ class OrcCfg(ct.Structure):
         ("seed", ct.c_uint64),
         ("banks", ct.c_int32), ("C", ct.c_int32), ("L", ct.c_int32), ("W", ct.c_int32), ("P", ct.c_int32),
         ("max_state", ct.c_int32), ("half_state", ct.c_int32), ("state_top", ct.c_int32),
-        ("s_cdf", ct.c_uint32 * 32), ("q_thr", ct.c_uint64), ("run_cdf16", (ct.c_uint32 * 65) * 4),
+        ("s_cdf", ct.c_uint32 * 32), ("q_thr", ct.c_uint64), ("run_cdf16", (ct.c_uint32 * 65) * 8),
         ("one_negative", ct.c_int32), ("count_empty", ct.c_int32),
     ]
 
@@ -201,7 +201,7 @@ class Oracle:
         return int(lib().orc_smask_word(self._cfg(), clause, t, k, w))
 
     def run_counts(self, clause, t, k, w, mi):
-        """Per-literal decrement counts of a Type Ib run piece of 8 << mi
+        """Per-literal decrement counts of a Type Ib run piece of 8 (mi + 1)
         events for word w (u32 [32])."""
         out = np.zeros(32, np.uint32)
         lib().orc_run_counts(self._cfg(), clause, t, k, w, int(mi), _ptr(out))

@@ -45,7 +45,7 @@ typedef struct orc_cfg {
     int32_t max_state, half_state, state_top;
     uint32_t s_cdf[32];
     uint64_t q_thr;
-    uint32_t run_cdf16[4][65];
+    uint32_t run_cdf16[8][65];
     /* rule variants of the reference's CPU TM, pytm/base.py (0 = cutm rules) */
     int32_t one_negative; /* one uniformly chosen negative class per sample, true class first (base.py:139-143) */
     int32_t count_empty;  /* inference counts clauses without includes (base.py:59-67) */
@@ -83,18 +83,18 @@ static void count_cdf(double s, uint32_t cdf[32]) {
  * the clause sees more than 256 classes). */
 static int run_window(const orc_cfg *c) { return (c->coalesced ? c->K : 1) <= 256 ? 128 : 64; }
 
-/* Type Ib runs (see orc_train_update): for m = 8, 16, 32, 64 events the number
+/* Type Ib runs (see orc_train_update): for m = 8, 16, ..., 64 events the number
  * of decrements of one literal is Binomial(m, p), p = 1/s; entry d of row mi
- * is floor(65536 * P(count <= d)), 65536 from d = m on; the same pmf
- * recurrence in IEEE double. */
-static const int RUN_SIZES[4] = {8, 16, 32, 64};
+ * (m = 8 (mi + 1)) is 65536 * P(count <= d) rounded to nearest, 65536 from
+ * d = m on; the same pmf recurrence in IEEE double. */
+static const int RUN_SIZES[8] = {8, 16, 24, 32, 40, 48, 56, 64};
 
-static void run_cdf(double s, uint32_t out[4][65]) {
+static void run_cdf(double s, uint32_t out[8][65]) {
     double p = 1.0 / s;
     if (!(p > 0.0)) p = 0.0;
     if (p > 1.0) p = 1.0;
     const double q = 1.0 - p;
-    for (int mi = 0; mi < 4; ++mi) {
+    for (int mi = 0; mi < 8; ++mi) {
         const int m = RUN_SIZES[mi];
         for (int d = 0; d < 65; ++d) out[mi][d] = 65536u;
         if (!(q > 0.0)) { /* p = 1: every event decrements */
@@ -632,7 +632,8 @@ static void orc_pair(const orc_cfg *c, const int32_t *Yrow, uint64_t t, int *kt,
  * decided first (the decisions read only the batch-start fired bits and
  * include counts, and the weights, which they update), then applied in
  * feedback order; maximal runs of consecutive Type Ib events inside a window
- * are applied in pieces of 64, 32, 16 and 8 events (greedy, from the run's start)
+ * are applied in pieces of at most 64 events, each the longest multiple of 8
+ * events that the rest of the run holds (greedy, from the run's start),
  * with type1b_run, the rest one by one. */
 enum { EV_T1A = 1, EV_T1B = 2, EV_T2 = 3 };
 typedef struct { int32_t b, k, type; } orc_event;
@@ -703,7 +704,7 @@ void orc_train_update(const orc_cfg *c, int32_t lo, int32_t nc, uint32_t *ta, in
                 if (E->type == EV_T1B) {
                     int run = 0;
                     while (e + run < nev && run < 64 && ev[e + run].type == EV_T1B) ++run;
-                    const int mi = run >= 64 ? 3 : (run >= 32 ? 2 : (run >= 16 ? 1 : (run >= 8 ? 0 : -1)));
+                    const int mi = run / 8 - 1; /* the longest multiple of 8 events */
                     if (mi >= 0) {
                         type1b_run(c, st, g, t, (uint32_t)E->k, mi);
                         e += RUN_SIZES[mi];

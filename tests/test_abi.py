@@ -38,7 +38,7 @@ def test_config_matches_oracle(name):
     assert (cfg.clauses, cfg.literals, cfg.words, cfg.patches) == (o.C, o.L, o.W, o.P)
     assert cfg.state_top == o.state_top and cfg.half_state == o.half_state
     assert list(cfg.s_count_cdf) == list(o.cfg.s_cdf) and cfg.q_threshold == o.cfg.q_thr
-    for mi in range(4):
+    for mi in range(8):
         cdf = list(cfg.run_cdf16[mi])
         assert cdf == list(o.cfg.run_cdf16[mi])
         lo, hi = cfg.run_range[mi] & 0xFFFF, cfg.run_range[mi] >> 16

@@ -179,7 +179,7 @@ def _run_spec(o, clause, t, k, w, mi):
     calls = [[int(v) for v in O.philox4x32([clause, t & 0xFFFFFFFF, 0x40000000 | (w << 2) | i, 2 | (k << 2)],
                                             key, 7)] for i in range(4)]
     cdf = list(o.cfg.run_cdf16[mi])
-    m = 8 << mi
+    m = 8 * (mi + 1)
     out = []
     for j in range(32):
         u = sum(((calls[b >> 2][b & 3] >> j) & 1) << b for b in range(16))
@@ -195,8 +195,8 @@ def test_type1b_run_counts(s):
     """Definition, and the count distribution Binomial(m, 1/s) of each run size."""
     from math import comb
     o = O.Oracle(number_of_clauses_per_class=4, T=10, s=s, dim=(4, 1, 1), n_classes=3, seed=3 + 2**36)
-    for mi in range(4):
-        m = 8 << mi
+    for mi in range(8):
+        m = 8 * (mi + 1)
         assert list(o.run_counts(2, 2**32 + 5, 1, 7, mi)) == _run_spec(o, 2, 2**32 + 5, 1, 7, mi)
         d = np.concatenate([o.run_counts(c, t, 2, w, mi) for c in range(3) for t in range(60) for w in range(4)])
         if s == 1.0:

@@ -172,7 +172,7 @@ ytm_status ytm_config_init(ytm_config *cfg, int32_t clauses_per_class, int32_t T
         }
     }
     // Type Ib run tables: per literal Binomial(m, p) decrement counts for runs
-    // of m = 8, 16, 32, 64 events; entry d = P(count <= d) * 65536 rounded to
+    // of m = 8, 16, ..., 64 events; entry d = P(count <= d) * 65536 rounded to
     // the nearest integer, 65536 from d = m on, from the same pmf recurrence;
     // run_range: entries below lo are 0 (those counts are certain), entries
     // from hi on are 65536 (never exceeded)
@@ -181,8 +181,8 @@ ytm_status ytm_config_init(ytm_config *cfg, int32_t clauses_per_class, int32_t T
         if (!(p > 0.0)) p = 0.0;
         if (p > 1.0) p = 1.0;
         const double qq = 1.0 - p;
-        for (int mi = 0; mi < 4; ++mi) {
-            const int m = 8 << mi;
+        for (int mi = 0; mi < 8; ++mi) {
+            const int m = 8 * (mi + 1);
             for (int d = 0; d < 65; ++d) cfg->run_cdf16[mi][d] = 65536u;
             if (!(qq > 0.0)) {
                 for (int d = 0; d < m; ++d) cfg->run_cdf16[mi][d] = 0u;
@@ -197,7 +197,7 @@ ytm_status ytm_config_init(ytm_config *cfg, int32_t clauses_per_class, int32_t T
                 pmf = pmf * (double)(m - d) / (double)(d + 1) * p / qq;
             }
         }
-        for (int mi = 0; mi < 4; ++mi) {
+        for (int mi = 0; mi < 8; ++mi) {
             uint32_t lo = 0, hi = 0;
             while (lo < 64 && cfg->run_cdf16[mi][lo] == 0u) ++lo;
             while (hi < 64 && cfg->run_cdf16[mi][hi] < 65536u) ++hi;

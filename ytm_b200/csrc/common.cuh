@@ -197,7 +197,7 @@ __device__ __forceinline__ uint32_t smask_word_rk(const ytm_config &cfg, const R
     return smask_place(cfg, [&](uint32_t j) { return draw_rk<7>(rk, g, t, w * 4u + j, TAG_SMASK, k); }, calls);
 }
 
-// A run of m = 8 << mi (8 to 64) consecutive Type Ib events of one clause (type1b_fb,
+// A run of m = 8 (mi + 1) (8 to 64) consecutive Type Ib events of one clause (type1b_fb,
 // kernel.cu:453-470, applied by the reference one event at a time: each
 // decrements every literal with a positive state with probability 1/s).
 // Decrements with a floor at 0 commute, so the run leaves state - d clamped
@@ -227,12 +227,12 @@ __host__ __device__ inline int run_table_base(const ytm_config &cfg, int mi) {
     for (int i = 0; i < mi; ++i) n += (int)(cfg.run_range[i] >> 16) - (int)(cfg.run_range[i] & 0xFFFFu);
     return n;
 }
-__host__ __device__ inline size_t run_table_bytes(const ytm_config &cfg) { return (size_t)run_table_base(cfg, 4) * 64; }
+__host__ __device__ inline size_t run_table_bytes(const ytm_config &cfg) { return (size_t)run_table_base(cfg, 8) * 64; }
 __device__ inline void run_table_fill(const ytm_config &cfg, uint4 *tab, int tid, int nt) {
-    const int n = run_table_base(cfg, 4);
+    const int n = run_table_base(cfg, 8);
     for (int i = tid; i < n * 4; i += nt) {
         int e = i >> 2, mi = 0;
-        for (; mi < 3; ++mi) {
+        for (; mi < 7; ++mi) {
             const int len = (int)(cfg.run_range[mi] >> 16) - (int)(cfg.run_range[mi] & 0xFFFFu);
             if (e < len) break;
             e -= len;

@@ -303,7 +303,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, (CPB == YTM_B1_CPB_CONV && NB <
                             }
                         }
                         if (run >= 8) {
-                            const int mi = run >= 64 ? 3 : (run >= 32 ? 2 : (run >= 16 ? 1 : 0));
+                            const int mi = min(run, 64) / 8 - 1;
                             const uint32_t kk = (uint32_t)(k0 + kb * 32 + b);
                             uint32_t D[7];
                             run_counts(cfg, mi, [&](uint32_t ii) {
@@ -312,7 +312,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, (CPB == YTM_B1_CPB_CONV && NB <
 #pragma unroll
                             for (int ii = 0; ii < 7; ++ii) D[ii] &= vm;
                             ctr.sub_floor(D, zero_s, top2);
-                            skip = (8 << mi) - 1;
+                            skip = 8 * (mi + 1) - 1;
                             continue;
                         }
                     }

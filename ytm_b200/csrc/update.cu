@@ -188,9 +188,9 @@ __device__ __forceinline__ void block_sync() {
 // Shared memory of one clause: weights [nk], picks [bc], count, event list
 // [bc*nk], fired samples [bc/32], event types [bc*nk], simple classes [nk],
 // pairs with an event as bits [bc][ceil(nk/32)].
-// An event list entry is row << 24 | type << 22 | run piece << 19 | class
+// An event list entry is row << 24 | type << 22 | run piece << 18 | class
 // (piece: 0 for a single event, mi + 1 for the first event of a Type Ib run
-// piece of 8 << mi events).
+// piece of 8 (mi + 1) events).
 // update_smem() (without the last two small arrays' padding) sizes the chunk.
 static __host__ __device__ inline size_t update_smem(int nk, int bc) {
     return (size_t)nk * 4 + (size_t)bc * 4 + 4 + (size_t)bc * nk * 4 + (size_t)bc * nk + 16;
@@ -516,8 +516,10 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
         const int nev = cnt[0];
         // 2b. Type Ib run pieces, once per chunk: the first event of each run
         //     of consecutive Type Ib events inside a run window marks its
-        //     pieces (64, 32, 16, 8 from the run start, the rest single
-        //     events) with code mi + 1 in bits 19..21 of their first entry
+        //     pieces (from the run start, each the longest multiple of 8
+        //     events up to 64 that the rest holds; fewer than 8 remain
+        //     single events) with code mi + 1 in bits 18..21 of their first
+        //     entry
         for (int e = tid; e < nev; e += nt) {
             const uint32_t ent = list[e];
             if (((ent >> 22) & 3u) != EV_T1B) continue;
@@ -533,10 +535,10 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                 ++run;
             }
             for (int q = e; run >= 8;) {
-                const int mi = run >= 64 ? 3 : (run >= 32 ? 2 : (run >= 16 ? 1 : 0));
-                list[q] |= (uint32_t)(mi + 1) << 19;
-                q += 8 << mi;
-                run -= 8 << mi;
+                const int m = min(run, 64) & ~7;
+                list[q] |= (uint32_t)(m >> 3) << 18;
+                q += m;
+                run -= m;
             }
         }
         block_sync<WPC>();
@@ -554,13 +556,13 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                     const uint32_t ent = list[e];
                     const int bl = (int)(ent >> 24);
                     const uint32_t ev = (ent >> 22) & 3u;
-                    const int k = k0 + (int)(ent & 0x7FFFFu);
+                    const int k = k0 + (int)(ent & 0xFFFFu);
                     const int b = b0 + bl;
                     const uint64_t t = t0 + (uint64_t)b;
                     ++n_units;
                     {
-                        const uint32_t piece = (ent >> 19) & 7u;
-                        if (piece) {  // a Type Ib run piece of 8 << mi events
+                        const uint32_t piece = (ent >> 18) & 15u;
+                        if (piece) {  // a Type Ib run piece of 8 (mi + 1) events
                             const int mi = (int)piece - 1;
                             uint32_t D[7];
                             run_counts(cfg, mi, [&](uint32_t i) {
@@ -571,7 +573,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
 #pragma unroll
                             for (int i = 0; i < 7; ++i) D[i] &= vm;
                             ctr.sub_floor(D, zero_s, top2);
-                            e += (8 << mi) - 1;
+                            e += 8 * (mi + 1) - 1;
                             continue;
                         }
                     }
