@@ -482,7 +482,7 @@ def counted_feedback(tm, lits, Yd, B, base, nb, dev):
     count."""
     import torch
     eng = tm.engine
-    ctr = torch.zeros(4, dtype=torch.int64, device=dev)
+    ctr = torch.zeros(6, dtype=torch.int64, device=dev)
     for r in range(nb):
         j = (base + r) * B
         t = tm.sample_counter
@@ -618,28 +618,29 @@ def main():
     hbm_peak, peak_kind = load_peaks()
     NB, W = cfg.planes, cfg.words
     if ctrs is not None:
-        units, calls, words, events = (v / nb for v in ctrs)
-        # Algorithmic INT work of one feedback launch (the per-unit figure of
-        # the hot-path survey: U * W * (ripple add ~ 2 * planes + Bernoulli
-        # mask ops)): every (event, literal word) pair of the reference's
-        # per-event algorithm costs a ripple add or borrow over the planes
-        # (2 * planes logic ops) and one Bernoulli(1/s) mask of 32 literals,
-        # priced as one Philox4x32-7 call at the measured LOP3 : Philox
-        # throughput ratio.  Type Ib runs do less than this per event, so the
-        # fraction can approach 1 without the kernel being at the pipe's limit;
-        # ncu's reading of the kernel is carried beside it.
+        units, calls, words, events, dcalls, tests = (v / nb for v in ctrs)
+        # INT work one feedback launch executes, counted on the device: every
+        # Philox4x32-7 call (literal masks, Type Ib run counts, the decisions
+        # of the active pairs) priced at the measured LOP3 : Philox
+        # throughput ratio, a ripple add / bit-sliced subtraction over the
+        # planes (2 * planes logic ops) per literal-word operation, and a
+        # 16-plane carry chain (16 logic ops) per run-count threshold tested.
+        # The per-event view of the same work (every (event, literal word)
+        # pair of the reference's one-event-at-a-time algorithm) is carried
+        # as units_per_launch.event_word_pairs.
         event_words = events * W
         mask_ops = lop3 / philox
-        ops = event_words * (2 * NB + mask_ops)
+        ops = (calls + dcalls) * mask_ops + units * 2 * NB + tests * 16
         alg_bytes = cfg.clause_count * NB * W * 4 * 2 + B * W * 4 * cfg.patches  # one read + write of the planes
         roofline = {"bound": "int", "achieved": ops / upd_s / 1e9, "peak": lop3 / 1e9, "unit": "G int-ops/s",
                     "frac": ops / upd_s / lop3, "traffic": None, "kernel": "k_update (feedback)",
                     "peak_kind": "measured on this GPU (bench_probe.cu LOP3 probe)",
                     "launch_ms": upd_s * 1000.0, "launches_averaged": nb,
                     "units_per_launch": {"event_word_pairs": event_words, "events": events},
-                    "op_model": "per (event, literal word): 2*planes LOP3 (ripple) + one Philox4x32-7 mask call "
-                                "x (LOP3 peak / Philox peak)",
+                    "op_model": "executed, from device counters: Philox4x32-7 calls x (LOP3 peak / Philox peak) "
+                                "+ 2*planes LOP3 per literal-word operation + 16 LOP3 per run-count threshold",
                     "counters_per_launch": {"literal_word_ops": units, "philox7_calls": calls,
+                                            "decision_philox7_calls": dcalls, "run_thresholds": tests,
                                             "state_words_streamed": words},
                     "philox7_peak_calls_per_s": philox, "lop3_peak_per_s": lop3,
                     # the same kernel read by ncu (profiles/k_update_c5.md, 4096-clause capture of

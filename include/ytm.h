@@ -255,11 +255,13 @@ ytm_status ytm_train_update(const ytm_config *cfg, uint32_t *state, int32_t *wei
                             void *stream);
 
 /* ytm_train_update that also adds measurement counts of its feedback into
- * counters u64[4] (device memory, accumulated, never cleared here):
+ * counters u64[6] (device memory, accumulated, never cleared here):
  * [0] literal-word operations applied (one per word for each single event
  * and for each piece of a Type Ib run), [1] Philox4x32-7 calls made for
  * literal masks and run counts, [2] state words streamed (each a read and a
- * write of every bit plane), [3] feedback events.  Measurement variant with no reference
+ * write of every bit plane), [3] feedback events, [4] Philox4x32-7 calls
+ * made for the decisions of the active (sample, class) pairs, [5] run-count
+ * thresholds tested (each a 16-plane carry chain over 32 literals).  Measurement variant with no reference
  * counterpart; counters == NULL gives ytm_train_update. */
 ytm_status ytm_train_update_counted(const ytm_config *cfg, uint32_t *state, int32_t *weights,
                                     const int32_t *cs, const int32_t *Y, const uint32_t *drop,

@@ -363,7 +363,7 @@ def test_patch_match_on_random_states(case, p_inc):
 
 def test_type1b_runs_take_the_run_path():
     """On a case with long Type Ib runs the feedback's device counters show
-    run pieces (four Philox calls per word for a piece of 8 to 32 events
+    run pieces (four Philox calls per word for a piece of 8 to 64 events
     instead of one per event), and the state still equals the oracle's."""
     kw, bs = TRAIN_CASES["runs_b40"]
     o = O.Oracle(**oracle_kwargs(kw, 5))
@@ -374,7 +374,7 @@ def test_type1b_runs_take_the_run_path():
     lits_h = o.encode(X)
     ta, w, pw = o.init_state(), o.init_weights(), np.zeros((o.C, o.P), np.int32)
     lits, Yd = dev(lits_h), dev(Y, np.int32)
-    ctr = torch.zeros(4, dtype=torch.int64, device="cuda")
+    ctr = torch.zeros(6, dtype=torch.int64, device="cuda")
     for t in (0, 40):
         o.train_batch(ta, w, pw, lits_h, Y, t)
         cs = e.train_eval(lits, t, None, add_bias=True)

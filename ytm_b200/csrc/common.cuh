@@ -248,7 +248,7 @@ __device__ inline void run_table_fill(const ytm_config &cfg, uint4 *tab, int tid
 // run_table_base(cfg, mi)), or nullptr to form them in registers.
 template <typename DrawFn>
 __device__ __forceinline__ void run_counts(const ytm_config &cfg, int mi, DrawFn drawi, uint32_t (&D)[7],
-                                           uint32_t &calls, const uint4 *km) {
+                                           uint32_t &calls, uint32_t &tests, const uint4 *km) {
     uint32_t R[16];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -281,6 +281,7 @@ __device__ __forceinline__ void run_counts(const ytm_config &cfg, int mi, DrawFn
 #pragma unroll
             for (int b = 0; b < 16; ++b) cy = maj3(R[b], 0u - ((k >> b) & 1u), cy);
         }
+        ++tests;
         if (!cy) break;  // d < j for all 32 literals, and the masks are nested
         const int tz = __ffs(j) - 1;
 #pragma unroll

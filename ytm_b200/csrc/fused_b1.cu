@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(FB_WARPS * 32, (CPB == YTM_B1_CPB_CONV && NB <
                             uint32_t D[7];
                             run_counts(cfg, mi, [&](uint32_t ii) {
                                 return draw_rk<7>(rk, g, t, 0x40000000u | ((uint32_t)w << 2) | ii, TAG_SMASK, kk);
-                            }, D, n_calls, nullptr);
+                            }, D, n_calls, n_calls, nullptr);
 #pragma unroll
                             for (int ii = 0; ii < 7; ++ii) D[ii] &= vm;
                             ctr.sub_floor(D, zero_s, top2);

@@ -162,7 +162,7 @@ __global__ void k_batch_words(const LitSrc src, int64_t B, uint32_t *__restrict_
 }
 
 // Optional per-phase cycle counts of the feedback kernel (measurement
-// builds with -DYTM_PHASE_TIMING only: counters[4..9] receive the cycles
+// builds with -DYTM_PHASE_TIMING only: counters[6..11] receive the cycles
 // thread 0 of each clause spent in each phase).
 #ifdef YTM_PHASE_TIMING
 #define YTM_PHASE_START() long long ph_last_ = clock64()
@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
     const uint32_t win_shift = run_window(cfg) == 128 ? 7u : 6u;  // Type Ib run windows
     // measurement counters: (event, word) pairs applied, Philox4x32-7 calls
     // of the literal masks, state words streamed, events
-    uint32_t n_units = 0, n_calls = 0, n_words = 0, n_events = 0;
+    uint32_t n_units = 0, n_calls = 0, n_words = 0, n_events = 0, n_dcalls = 0, n_tests = 0;
 #ifdef YTM_PHASE_TIMING
     unsigned long long ph_cyc[6] = {0, 0, 0, 0, 0, 0};
 #endif
@@ -368,6 +368,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                 if (key != rkey) {
                     r = pair_draw(cfg, rk, rk_ok, g, t0 + (uint64_t)b, k);
                     rkey = key;
+                    ++n_dcalls;
                 }
                 const uint2 u = class_words(r, (uint32_t)k);
                 const bool neg = (e >> 31) & 1u;
@@ -386,6 +387,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                                                          (uint32_t)k0));
                     if (simple[0]) a = (a && ((a == 1) == (wk[0] >= 0))) ? EV_T1B : EV_NONE;
                     evt[bl] = a;
+                    ++n_dcalls;
                 }
         block_sync<WPC>();
         YTM_PHASE(2);
@@ -569,7 +571,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                                 const uint32_t sub = 0x40000000u | ((uint32_t)w << 2) | i;
                                 return rk_ok ? draw_rk<7>(rk, g, t, sub, TAG_SMASK, (uint32_t)k)
                                              : draw<7>(cfg.seed, g, t, sub, TAG_SMASK, (uint32_t)k);
-                            }, D, n_calls, kmt + 4 * run_table_base(cfg, mi));
+                            }, D, n_calls, n_tests, kmt + 4 * run_table_base(cfg, mi));
 #pragma unroll
                             for (int i = 0; i < 7; ++i) D[i] &= vm;
                             ctr.sub_floor(D, zero_s, top2);
@@ -604,12 +606,12 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
     for (int kk = tid; kk < nk; kk += nt) weights[(int64_t)c * K + k0 + kk] = wk[kk];
 #ifdef YTM_PHASE_TIMING
     if (counters && tid == 0)
-        for (int i = 0; i < 6; ++i) atomicAdd(&counters[4 + i], ph_cyc[i]);
+        for (int i = 0; i < 6; ++i) atomicAdd(&counters[6 + i], ph_cyc[i]);
 #endif
     if (counters) {
-        unsigned long long v[4] = {n_units, n_calls, n_words, n_events};
+        unsigned long long v[6] = {n_units, n_calls, n_words, n_events, n_dcalls, n_tests};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 6; ++i) {
             for (int o = 16; o; o >>= 1) v[i] += __shfl_xor_sync(0xFFFFFFFFu, v[i], o);
             if ((tid & 31) == 0 && v[i]) atomicAdd(&counters[i], v[i]);
         }

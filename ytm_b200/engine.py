@@ -229,7 +229,7 @@ class CudaEngine:
     def train_update(self, cs: torch.Tensor, Y_b: torch.Tensor, lits_b: torch.Tensor, t0: int,
                      drop: torch.Tensor | None, sel_override: torch.Tensor | None = None,
                      counters: torch.Tensor | None = None) -> None:
-        """Feedback of the batch.  counters: optional int64 [4] device tensor
+        """Feedback of the batch.  counters: optional int64 [6] device tensor
         that accumulates the measurement counts of ytm_train_update_counted."""
         c = self._cfg_for(lits_b)
         B = lits_b.shape[0]
