@@ -55,9 +55,9 @@ L2_BYTES = 126 * 1024 * 1024
 # times it in, from one ncu capture of a reduced-clause model of the same
 # workload, scaled by clauses (the feedback's traffic is per clause); None
 # where no capture was made.
-# configuration 5: 223 MB read + 188 MB written by one k_update launch over
+# configuration 5: 221 MB read + 178 MB written by one k_update launch over
 # 4096 clauses (profiles/k_update_c5.md)
-TRAFFIC_PER_CLAUSE = {"c5": (223e6 + 188e6) / 4096}
+TRAFFIC_PER_CLAUSE = {"c5": (221e6 + 178e6) / 4096}
 
 
 def load_peaks():
