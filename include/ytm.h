@@ -81,6 +81,13 @@ typedef struct ytm_config {
                                   Binomial(32, 1/s); entry n = floor(2^32 *
                                   P(count <= n)), saturated at 2^32 - 1     */
     uint64_t q_threshold;      /* negative-class selection, thr / 2^32          */
+    uint32_t q_count_cdf[32];  /* negative-class selection drawn per (clause,
+                                  sample) as a set (q_select): count of
+                                  selected classes among K, Binomial(K, Q);
+                                  entry n = floor(2^32 * P(count <= n)),
+                                  saturated at 2^32 - 1                     */
+    int32_t q_select;          /* 1: coalesced, K >= 32, K * Q <= 2 (the set is
+                                  drawn at once), 0: one draw per class       */
     uint32_t run_cdf16[8][65]; /* Type Ib runs of m = 8, 16, ..., 64 events: per
                                   literal decrement count Binomial(m, 1/s);
                                   entry d = 65536 * P(count <= d) rounded to

@@ -49,7 +49,7 @@ class OrcCfg(ct.Structure):
         ("seed", ct.c_uint64),
         ("banks", ct.c_int32), ("C", ct.c_int32), ("L", ct.c_int32), ("W", ct.c_int32), ("P", ct.c_int32),
         ("max_state", ct.c_int32), ("half_state", ct.c_int32), ("state_top", ct.c_int32),
-        ("s_cdf", ct.c_uint32 * 32), ("q_thr", ct.c_uint64), ("run_cdf16", (ct.c_uint32 * 65) * 8),
+        ("s_cdf", ct.c_uint32 * 32), ("q_thr", ct.c_uint64), ("q_cdf", ct.c_uint32 * 32), ("q_select", ct.c_int32), ("run_cdf16", (ct.c_uint32 * 65) * 8),
         ("one_negative", ct.c_int32), ("count_empty", ct.c_int32),
     ]
 
@@ -72,6 +72,7 @@ def _declare(L):
     L.orc_smask_word.argtypes = [ct.POINTER(OrcCfg), ct.c_uint32, _U64, ct.c_uint32, ct.c_uint32]
     L.orc_smask_word.restype = ct.c_uint32
     L.orc_run_counts.argtypes = [ct.POINTER(OrcCfg), ct.c_uint32, _U64, ct.c_uint32, ct.c_uint32, ct.c_int, _P]
+    L.orc_qselect_set.argtypes = [ct.POINTER(OrcCfg), ct.c_uint32, _U64, _P]
     L.orc_smask_count.argtypes = [ct.c_int]
     L.orc_smask_count.restype = ct.c_uint64
     L.orc_update_threshold.argtypes = [_I32, _I32]
@@ -206,6 +207,13 @@ class Oracle:
         out = np.zeros(32, np.uint32)
         lib().orc_run_counts(self._cfg(), clause, t, k, w, int(mi), _ptr(out))
         return out
+
+    def qselect_set(self, clause, t):
+        """The negative-class selection of (clause, sample t) drawn as a set
+        (configurations with q_select): bool [K]."""
+        out = np.zeros(self.cfg.K, np.uint8)
+        lib().orc_qselect_set(self._cfg(), clause, t, _ptr(out))
+        return out.astype(bool)
 
     @staticmethod
     def smask_count(on: bool) -> int:

@@ -45,6 +45,8 @@ typedef struct orc_cfg {
     int32_t max_state, half_state, state_top;
     uint32_t s_cdf[32];
     uint64_t q_thr;
+    uint32_t q_cdf[32];
+    int32_t q_select;
     uint32_t run_cdf16[8][65];
     /* rule variants of the reference's CPU TM, pytm/base.py (0 = cutm rules) */
     int32_t one_negative; /* one uniformly chosen negative class per sample, true class first (base.py:139-143) */
@@ -157,6 +159,23 @@ int orc_cfg_init(orc_cfg *c, int32_t clauses_per_class, int32_t T, double s, int
         if (qp >= 1.0) c->q_thr = 4294967296ull;
         else if (!(qp > 0.0)) c->q_thr = 0;
         else c->q_thr = (uint64_t)floor(qp * 4294967296.0);
+        /* coalesced models of at least 32 classes with K * Q <= 2 draw the selection as a set per
+         * (clause, sample); count ~ Binomial(K, Q) */
+        if (!(qp > 0.0)) qp = 0.0;
+        if (qp > 1.0) qp = 1.0;
+        c->q_select = (coalesced && K >= 32 && qp > 0.0 && qp < 1.0 && qp * K <= 2.0) ? 1 : 0;
+        for (int n = 0; n < 32; ++n) c->q_cdf[n] = 0xFFFFFFFFu;
+        if (c->q_select) {
+            const double qq = 1.0 - qp;
+            double pmf = 1.0, acc = 0.0;
+            for (int i = 0; i < K; ++i) pmf *= qq;
+            for (int n = 0; n < 32; ++n) {
+                acc += pmf;
+                const double v = floor(acc * 4294967296.0);
+                c->q_cdf[n] = v >= 4294967295.0 ? 0xFFFFFFFFu : (uint32_t)v;
+                pmf = n < K ? pmf * (double)(K - n) / (double)(n + 1) * qp / qq : 0.0;
+            }
+        }
     }
     if (c->W <= 0 || c->P <= 0 || c->C <= 0 || K <= 0) return 1;
     return 0;
@@ -627,6 +646,42 @@ static void orc_pair(const orc_cfg *c, const int32_t *Yrow, uint64_t t, int *kt,
 /* Part 2 of a batch: clause_update, kernel.cu:531-613, for every clause of the
  * shard and every sample of the batch in order.  cs [B][K] are the summed class
  * sums, Y [B][K] the +-T targets, sel [B][nc] and ninc [nc] from part 1. */
+/* The negative-class selection (kernel.cu:573: each class with target -1
+ * takes part with probability Q) drawn as a set for clause g at sample t
+ * when q_select: the Philox4x32-7 call at sub-index 2 (class field 0) gives
+ * in word 0 the count n of selected classes among all K, the smallest n with
+ * r0 < q_cdf[n] (min(K, 32) if none), i.e. Binomial(K, Q); then n distinct classes
+ * by rejection from b-bit fields (b = bits of K - 1, floor(32 / b) fields per
+ * word from bit 0) of words 1-3 and of all words of further calls at
+ * sub-indices 3, 4, ...: a value >= K or already drawn is skipped.  Every
+ * class is then selected independently with probability Q. */
+static void orc_qselect(const orc_cfg *c, uint32_t g, uint64_t t, uint8_t *sel) {
+    const int K = c->K;
+    memset(sel, 0, (size_t)K);
+    uint32_t R[4], sub = 2;
+    draw_r(c, g, t, sub, TAG_CLASS, 0, 7, R);
+    const uint32_t nmax = K < 32 ? (uint32_t)K : 32u;
+    uint32_t n = 0;
+    while (n < nmax && R[0] >= c->q_cdf[n]) ++n;
+    int b = 1;
+    while ((1 << b) < K) ++b;
+    const int per = 32 / b;
+    int wi = 1, f = 0;
+    while (n) {
+        if (f == per) {
+            f = 0;
+            if (++wi == 4) { draw_r(c, g, t, ++sub, TAG_CLASS, 0, 7, R); wi = 0; }
+        }
+        const uint32_t v = (R[wi] >> (b * f)) & ((1u << b) - 1u);
+        ++f;
+        if ((int)v < K && !sel[v]) { sel[v] = 1; --n; }
+    }
+}
+
+/* Test hook: the selected set of clause g at sample t as 0/1 per class
+ * (sel [K]); the configuration must have q_select. */
+void orc_qselect_set(const orc_cfg *c, uint32_t g, uint64_t t, uint8_t *sel) { orc_qselect(c, g, t, sel); }
+
 /* Feedback of a batch (clause_update, kernel.cu:531-613, per sample in
  * order).  Per clause, the events of each 128-sample window (64 above 256 classes) of the batch are
  * decided first (the decisions read only the batch-start fired bits and
@@ -646,6 +701,8 @@ void orc_train_update(const orc_cfg *c, int32_t lo, int32_t nc, uint32_t *ta, in
     {
     const int win = run_window(c);
     orc_event *ev = (orc_event *)malloc(sizeof(orc_event) * (size_t)win * (size_t)(K > 2 ? K : 2));
+    uint8_t *qsel = (uint8_t *)malloc((size_t)K);
+    const int use_qsel = c->q_select && !c->one_negative;
 #pragma omp for schedule(dynamic, 4)
     for (int32_t i = 0; i < nc; ++i) {
         if (drop && drop[i] == 1) continue; /* kernel.cu:555 */
@@ -667,6 +724,7 @@ void orc_train_update(const orc_cfg *c, int32_t lo, int32_t nc, uint32_t *ta, in
                     if (ko >= k0 && ko < k1) seq[nseq++] = ko;
                 }
                 int nk = c->one_negative ? nseq : k1 - k0;
+                if (use_qsel) orc_qselect(c, g, t, qsel);
                 for (int kq = 0; kq < nk; ++kq) { /* kernel.cu:563-568 */
                     const int k = c->one_negative ? seq[kq] : k0 + kq;
                     int32_t v = clip_cs(c, cs[(int64_t)b * K + k]);
@@ -677,7 +735,8 @@ void orc_train_update(const orc_cfg *c, int32_t lo, int32_t nc, uint32_t *ta, in
                     uint32_t r[4];
                     draw_r(c, g, t, 0, TAG_CLASS, (uint32_t)k >> 1, 7, r);
                     const uint32_t uq = r[2 * (k & 1)], uu = r[2 * (k & 1) + 1];
-                    if (!c->one_negative && target == -1 && !((uint64_t)uq < c->q_thr)) continue; /* kernel.cu:573 */
+                    if (!c->one_negative && target == -1 &&
+                        !(use_qsel ? qsel[k] : (uint64_t)uq < c->q_thr)) continue; /* kernel.cu:573 */
                     int upd = (uint64_t)uu < orc_update_threshold(y, v);   /* kernel.cu:582 */
                     int32_t *lw = &w[(int64_t)i * K + k];
                     int sign = (*lw >= 0) - (*lw < 0);
@@ -722,6 +781,7 @@ void orc_train_update(const orc_cfg *c, int32_t lo, int32_t nc, uint32_t *ta, in
         }
     }
     free(ev);
+    free(qsel);
     }
 }
 

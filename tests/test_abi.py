@@ -38,6 +38,7 @@ def test_config_matches_oracle(name):
     assert (cfg.clauses, cfg.literals, cfg.words, cfg.patches) == (o.C, o.L, o.W, o.P)
     assert cfg.state_top == o.state_top and cfg.half_state == o.half_state
     assert list(cfg.s_count_cdf) == list(o.cfg.s_cdf) and cfg.q_threshold == o.cfg.q_thr
+    assert cfg.q_select == o.cfg.q_select and list(cfg.q_count_cdf) == list(o.cfg.q_cdf)
     for mi in range(8):
         cdf = list(cfg.run_cdf16[mi])
         assert cdf == list(o.cfg.run_cdf16[mi])
@@ -95,3 +96,21 @@ def test_entry_points_reject_bad_arguments_without_a_gpu():
     assert lib.ytm_peer_allreduce_i32(None, None, 4, 0, None) == 1
     assert lib.ytm_infer(ct.byref(cfg), None, None, None, None, 0, None, None, None) == 0  # N = 0: nothing to do
     assert lib.ytm_last_error()  # the last failure left a message
+
+
+def test_negative_class_set_draw_table():
+    """The negative-class selection is drawn as a set only for coalesced
+    models of at least 32 classes with K * Q <= 2; its count table is the
+    Binomial(K, Q) CDF scaled to 2^32 (floor, saturated)."""
+    from scipy.stats import binom
+    cfg = _lib.make_config(clauses_per_class=8, T=10, s=3.0, dim=(16, 1, 1), n_classes=100, seed=1)
+    assert cfg.q_select == 1
+    Q = 1.0 / 99
+    for n in range(32):
+        want = min(int(binom.cdf(n, 100, Q) * 2**32), 2**32 - 1)
+        assert abs(int(cfg.q_count_cdf[n]) - want) <= 2, n
+    assert _lib.make_config(clauses_per_class=8, T=10, s=3.0, dim=(16, 1, 1), n_classes=10, seed=1).q_select == 0
+    assert _lib.make_config(clauses_per_class=8, T=10, s=3.0, dim=(16, 1, 1), n_classes=100, seed=1,
+                            coalesced=False).q_select == 0
+    assert _lib.make_config(clauses_per_class=8, T=10, s=3.0, dim=(16, 1, 1), n_classes=40, seed=1,
+                            q=39.0).q_select == 0

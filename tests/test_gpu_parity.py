@@ -109,6 +109,11 @@ TRAIN_CASES = {
     "runs_b40": (dict(number_of_clauses_per_class=30, T=400, s=4.0, dim=(40, 1, 1), n_classes=24, q=23.0), 40),
     "runs_b12": (dict(number_of_clauses_per_class=30, T=400, s=4.0, dim=(40, 1, 1), n_classes=24, q=23.0), 12),
     "runs_b1": (dict(number_of_clauses_per_class=30, T=400, s=4.0, dim=(40, 1, 1), n_classes=40, q=39.0), 1),
+    # negative-class selection drawn as a set (coalesced, K >= 32, K * Q <= 2):
+    # the CTA-per-clause, warp-per-clause and fused kernels
+    "qset_b40": (dict(number_of_clauses_per_class=12, T=40, s=5.0, dim=(40, 1, 1), n_classes=48, q=1.5), 40),
+    "qset_b12": (dict(number_of_clauses_per_class=12, T=40, s=5.0, dim=(40, 1, 1), n_classes=33), 12),
+    "qset_b1": (dict(number_of_clauses_per_class=12, T=40, s=5.0, dim=(40, 1, 1), n_classes=36, q=2.0), 1),
     "runs_conv_b3": (dict(number_of_clauses_per_class=16, T=300, s=6.0, dim=(8, 8, 1), n_classes=20, q=19.0,
                           patch_dim=(4, 4)), 3),
 }

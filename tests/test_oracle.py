@@ -207,3 +207,27 @@ def test_type1b_run_counts(s):
         for j in range(min(m, 12) + 1):
             want = comb(m, j) * p ** j * (1 - p) ** (m - j) * len(d)
             assert abs(hist[j] - want) < 5 * np.sqrt(want) + 6, (mi, j, hist[j], want)
+
+
+def test_negative_class_set_draw():
+    """Coalesced models of at least 32 classes with K * Q <= 2 draw each
+    (clause, sample)'s selected negative classes as a set: the count follows
+    Binomial(K, Q) and every class is selected with probability Q, as the
+    reference's per-class test u < Q (kernel.cu:573) gives."""
+    from scipy.stats import binom, chisquare
+    K = 40
+    o = O.Oracle(number_of_clauses_per_class=4, T=10, s=3.0, dim=(16, 1, 1), n_classes=K, seed=5)
+    assert o.cfg.q_select == 1
+    Q = 1.0 / (K - 1)
+    S = np.array([o.qselect_set(c, 2**32 - 3 + t) for c in range(8) for t in range(2500)])
+    n = S.sum(1)
+    obs = np.bincount(n, minlength=6)[:6].astype(float)
+    obs[5] += (n > 5).sum()
+    exp = binom.pmf(np.arange(6), K, Q) * len(n)
+    exp[5] = binom.sf(4, K, Q) * len(n)
+    assert chisquare(obs, exp).pvalue > 1e-3
+    per = S.sum(0).astype(float)
+    assert chisquare(per, np.full(K, per.sum() / K)).pvalue > 1e-3
+    assert abs(per.sum() / (len(n) * K) - Q) < 4 * np.sqrt(Q / (len(n) * K))
+    # the same (clause, sample) gives the same set
+    assert np.array_equal(o.qselect_set(3, 77), o.qselect_set(3, 77))

@@ -48,6 +48,7 @@ class Config(ct.Structure):
         ("max_state", ct.c_int32), ("half_state", ct.c_int32), ("planes", ct.c_int32),
         ("state_offset", ct.c_int32), ("state_top", ct.c_int32),
         ("s_count_cdf", ct.c_uint32 * 32), ("q_threshold", ct.c_uint64),
+        ("q_count_cdf", ct.c_uint32 * 32), ("q_select", ct.c_int32),
         ("run_cdf16", (ct.c_uint32 * 65) * 8),
         ("clause_lo", ct.c_int32), ("clause_count", ct.c_int32),
         ("one_negative", ct.c_int32), ("count_empty", ct.c_int32),

@@ -62,6 +62,7 @@ TrainWs train_ws_layout(const ytm_config *cfg, int64_t B) {
     l.amask = o; o = align_up(o + (uint64_t)B * cdiv(K, 32) * 4, 256);
     l.colm = o;  o = align_up(o + K * cdiv(B, 32) * 4, 256);
     l.row_off = o; o = align_up(o + ((uint64_t)B + 1) * 4, 256);
+    l.npos = o;  o = align_up(o + (uint64_t)B * 4, 256);  // target +1 pairs per sample (q_select)
     l.alist = o; o = align_up(o + (uint64_t)B * K * 8, 256);
     l.pair = o;  o = align_up(o + (uint64_t)B * 2 * 4, 256);
     l.sparse = o; o = align_up(o + sparse_ws_bytes(cfg), 256);  // compacted include words (sparse patch match)
@@ -209,6 +210,25 @@ ytm_status ytm_config_init(ytm_config *cfg, int32_t clauses_per_class, int32_t T
         if (qp >= 1.0) cfg->q_threshold = 4294967296ull;
         else if (!(qp > 0.0)) cfg->q_threshold = 0;
         else cfg->q_threshold = (uint64_t)floor(qp * 4294967296.0);
+        // the negative-class selection as a set per (clause, sample) for
+        // coalesced models of at least 32 classes whose expected selections
+        // K * Q are at most 2 (below 32 classes one draw per class pair is as cheap):
+        // count ~ Binomial(K, Q) (this table, IEEE double pmf recurrence)
+        if (!(qp > 0.0)) qp = 0.0;
+        if (qp > 1.0) qp = 1.0;
+        cfg->q_select = (coalesced && n_classes >= 32 && qp > 0.0 && qp < 1.0 && qp * n_classes <= 2.0) ? 1 : 0;
+        for (int n = 0; n < 32; ++n) cfg->q_count_cdf[n] = 0xFFFFFFFFu;
+        if (cfg->q_select) {
+            const double qq = 1.0 - qp;
+            double pmf = 1.0, acc = 0.0;
+            for (int i = 0; i < n_classes; ++i) pmf *= qq;
+            for (int n = 0; n < 32; ++n) {
+                acc += pmf;
+                const double v = floor(acc * 4294967296.0);
+                cfg->q_count_cdf[n] = v >= 4294967295.0 ? 0xFFFFFFFFu : (uint32_t)v;
+                pmf = n < n_classes ? pmf * (double)(n_classes - n) / (double)(n + 1) * qp / qq : 0.0;
+            }
+        }
     }
     cfg->clause_lo = 0;
     cfg->clause_count = cfg->clauses;

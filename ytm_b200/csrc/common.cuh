@@ -305,6 +305,46 @@ __device__ __forceinline__ u32x4 class_pair_draw(uint64_t seed, uint32_t g, uint
     return draw<7>(seed, g, t, 0, TAG_CLASS, k >> 1);
 }
 
+// The negative-class selection (kernel.cu:573: each class with target -1
+// takes part with probability Q) drawn as a set for clause g at sample t when
+// cfg.q_select: the Philox4x32-7 call at sub-index 2 (class field 0) gives in
+// word 0 the count n of selected classes among all K, the smallest n with
+// r0 < q_count_cdf[n] (min(K, 32) if none), i.e. Binomial(K, Q); then n distinct
+// classes by rejection from b-bit fields (b = bits of K - 1, floor(32 / b)
+// fields per word from bit 0) of words 1-3 and of all words of further calls
+// at sub-indices 3, 4, ...: a value >= K or already drawn is skipped.  take(v)
+// records class v and returns false when it was drawn before.
+template <typename DrawFn, typename TakeFn>
+__device__ __forceinline__ void qselect(const ytm_config &cfg, DrawFn drawsub, TakeFn take) {
+    const int K = cfg.n_classes;
+    uint32_t sub = 2;
+    u32x4 r = drawsub(sub);
+    // at most min(K, 32) classes: the saturated table entries would otherwise
+    // let a word of all ones ask for more distinct classes than exist
+    const uint32_t nmax = K < 32 ? (uint32_t)K : 32u;
+    uint32_t n = 0;
+    while (n < nmax && r.x >= cfg.q_count_cdf[n]) ++n;
+    if (!n) return;
+    const int b = 32 - __clz(K - 1);  // K >= 32
+    const int per = 32 / b;
+    const uint32_t fm = (1u << b) - 1u;
+    int wi = 1, f = 0;
+    uint32_t cur = r.y;
+    while (n) {
+        if (f == per) {
+            f = 0;
+            if (++wi == 4) {
+                r = drawsub(++sub);
+                wi = 0;
+            }
+            cur = wi == 0 ? r.x : (wi == 1 ? r.y : (wi == 2 ? r.z : r.w));
+        }
+        const uint32_t v = (cur >> (b * f)) & fm;
+        ++f;
+        if ((int)v < K && take((int)v)) --n;
+    }
+}
+
 // pytm's per-sample pick (pytm/base.py:139-141): the true class (the first
 // with a positive target, -1 if none) and one other class drawn uniformly
 // among the rest from the counter (clause 0xFFFFFFFF, t, 1, CLASS).
@@ -596,7 +636,7 @@ ytm_status check_cfg(const ytm_config *cfg);
 
 // Workspace carve-up (offsets in bytes, 256-aligned).
 struct TrainWs {
-    uint64_t ninc, mbits, sel, fired, fcm, thr, amask, colm, row_off, alist, pair, sparse, pwords, total;
+    uint64_t ninc, mbits, sel, fired, fcm, thr, amask, colm, row_off, npos, alist, pair, sparse, pwords, total;
 };
 TrainWs train_ws_layout(const ytm_config *cfg, int64_t B);
 // Bit-image input: the feedback reads the batch's patch literal words from a

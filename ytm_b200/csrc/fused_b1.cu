@@ -177,18 +177,36 @@ __global__ void __launch_bounds__(FB_WARPS * 32, (CPB == YTM_B1_CPB_CONV && NB <
             const bool ok_inc = ninc_ws[c] <= cfg.max_included_literals;
             u32x4 rp{};
             int rp_pair = -1;  // the class pair whose decision call rp holds
+            // q_select: the negative classes selected for this clause and sample
+            const bool use_qsel = cfg.coalesced && cfg.q_select && !cfg.one_negative;
+            uint16_t qs[32];
+            int nq = 0;
+            if (use_qsel)
+                qselect(cfg, [&](uint32_t sub) { return draw_rk<7>(rk, g, t, sub, TAG_CLASS, 0); }, [&](int v) {
+                    for (int j = 0; j < nq; ++j)
+                        if (qs[j] == (uint16_t)v) return false;
+                    qs[nq++] = (uint16_t)v;
+                    return true;
+                });
             for (int kk = 0; kk < nk; ++kk) {
                 const int k = k0 + kk;
                 uint64_t th = thr_s[k];
                 const int target = (th >> 63) ? -1 : 1;
                 th &= ~(1ull << 63);
+                if (!th) continue;  // inactive pair: no update whatever the draws (kernel.cu:582)
+                bool sel = true;
+                if (use_qsel && target == -1) {
+                    sel = false;
+                    for (int j = 0; j < nq; ++j) sel |= qs[j] == (uint16_t)k;
+                    if (!sel) continue;  // kernel.cu:573
+                }
                 if ((k >> 1) != rp_pair) {
                     rp = class_pair_draw_rk(rk, g, t, (uint32_t)k);
                     rp_pair = k >> 1;
                 }
                 const uint2 r = class_words(rp, (uint32_t)k);
                 if (cfg.one_negative ? (k != pair_s[0] && k != pair_s[1])
-                                     : (target == -1 && !((uint64_t)r.x < cfg.q_threshold)))
+                                     : (!use_qsel && target == -1 && !((uint64_t)r.x < cfg.q_threshold)))
                     continue;  // kernel.cu:573
                 if (!((uint64_t)r.y < th)) continue;                                // kernel.cu:582
                 int32_t *lw = &weights[(int64_t)c * K + k];

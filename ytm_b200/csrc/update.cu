@@ -44,6 +44,8 @@ static_assert(UPD_BC_MAX <= 256, "event list rows are 8 bits");
 //    (threshold - 1) << 32 | negative << 31 | sample << 16 | class, so that the
 //    feedback reads a pair's decision inputs in one contiguous load; row_off[b]
 //    is the position of sample b's first pair in it (row_off[B] = the count).
+//    With the negative-class selection drawn as a set (q_select), each
+//    sample's target +1 pairs come first and npos[b] counts them.
 // An active pair's list entry (its threshold is at least 1, at most 2^32).
 __device__ __forceinline__ uint64_t pair_entry(const uint64_t *__restrict__ thr, int b, int k, int K) {
     const uint64_t th = thr[(int64_t)b * K + k];
@@ -54,7 +56,8 @@ __global__ void __launch_bounds__(1024) k_thresholds(const int32_t *__restrict__
                                                      int B, int K, int T, int one_neg,
                                                      const int32_t *__restrict__ pair, uint64_t *__restrict__ thr,
                                                      uint32_t *__restrict__ amask, uint32_t *__restrict__ colm,
-                                                     int32_t *__restrict__ row_off, uint64_t *__restrict__ alist) {
+                                                     int32_t *__restrict__ row_off, uint64_t *__restrict__ alist,
+                                                     int qsel, int32_t *__restrict__ npos) {
     constexpr int AM_SMEM = 8192;  // words of amask kept in shared memory
     __shared__ uint32_t am_s[AM_SMEM];
     __shared__ int wsum[32];
@@ -136,6 +139,17 @@ __global__ void __launch_bounds__(1024) k_thresholds(const int32_t *__restrict__
                     const int k = pair[2 * row + q];
                     if (k >= 0 && ((am[k >> 5] >> (k & 31)) & 1u)) alist[pos++] = pair_entry(thr, row, k, K);
                 }
+            } else if (qsel) {  // the sample's target +1 pairs first, their count in npos
+                int np = 0;
+                for (int pass = 0; pass < 2; ++pass)
+                    for (int m = 0; m < KWm; ++m)
+                        for (uint32_t v = am[m]; v; v &= v - 1u) {
+                            const int k = m * 32 + __ffs(v) - 1;
+                            if ((int)(thr[(int64_t)row * K + k] >> 63) != pass) continue;
+                            alist[pos++] = pair_entry(thr, row, k, K);
+                            np += pass == 0;
+                        }
+                npos[row] = np;
             } else {
                 for (int m = 0; m < KWm; ++m)
                     for (uint32_t v = am[m]; v; v &= v - 1u)
@@ -247,6 +261,7 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
                                                 const int32_t *__restrict__ row_off,
                                                 const uint64_t *__restrict__ alist,
                                                 const uint32_t *__restrict__ fcm,
+                                                const int32_t *__restrict__ npos,
                                                 unsigned long long *__restrict__ counters) {
     extern __shared__ __align__(16) unsigned char small[];
     const int C = cfg.clause_count, W = cfg.words, K = cfg.n_classes;
@@ -308,6 +323,8 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
     // the pairs holding an event, as bits kept by the decision phases (the
     // compaction over all threads reads them)
     const bool use_enz = !WPC && cfg.coalesced && !cfg.one_negative;
+    // negative-class selection drawn as a set per (clause, sample)
+    const bool use_qsel = cfg.coalesced && cfg.q_select && !cfg.one_negative;
 
     for (int kk = tid; kk < nk; kk += nt) wk[kk] = weights[(int64_t)c * K + k0 + kk];
 
@@ -350,10 +367,67 @@ __global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, ui
         //     parallel: 1 = update with target +1, 2 = with target -1; simple
         //     classes get their event type here (Ib when target and weight
         //     sign agree)
-        // four consecutive list entries per thread, loaded together; when two
-        // neighbours are the two classes of one class pair of one sample, one
-        // Philox call serves both
-        for (int i0 = lo + 4 * tid; i0 < hi; i0 += 4 * nt) {  // coalesced: the chunk's pairs
+        if (use_qsel) {
+            // the negative-class selection drawn as a set per sample
+            // (kernel.cu:573); only events are written, so the chunk's event
+            // types start cleared
+            const int nb = bc * nk;
+            for (int i = tid; i < (nb >> 2); i += nt) ((uint32_t *)evt)[i] = 0u;
+            for (int i = (nb & ~3) + tid; i < nb; i += nt) evt[i] = 0;
+            if (tid == 0) cnt[0] = 0;  // the candidate count (the event count later)
+            block_sync<WPC>();
+            // (a) a thread per (sample, task): the sample's selected classes
+            //     with target -1 and an active pair, or its target +1 pairs,
+            //     into a candidate list (the event list's space, unused until
+            //     the compaction; candidates are distinct pairs of the chunk)
+            for (int x = tid; x < 2 * bc; x += nt) {
+                const int bl = x >> 1, b = b0 + bl;
+                const int lo_b = row_off[b], hi_b = row_off[b + 1], np = npos[b];
+                if (x & 1) {  // target +1: no selection (kernel.cu:573)
+                    for (int i = lo_b; i < lo_b + np; ++i)
+                        list[atomicAdd(cnt, 1)] = ((uint32_t)bl << 16) | (uint32_t)(alist[i] & 0xFFFFu);
+                } else if (hi_b - lo_b > np) {  // some target -1 pair is active
+                    const uint64_t tb = t0 + (uint64_t)b;
+                    uint16_t qs[32];
+                    int nq = 0;
+                    qselect(cfg, [&](uint32_t sub) {
+                        ++n_dcalls;
+                        return rk_ok ? draw_rk<7>(rk, g, tb, sub, TAG_CLASS, 0)
+                                     : draw<7>(cfg.seed, g, tb, sub, TAG_CLASS, 0);
+                    }, [&](int v) {
+                        for (int j = 0; j < nq; ++j)
+                            if (qs[j] == (uint16_t)v) return false;
+                        qs[nq++] = (uint16_t)v;
+                        const uint64_t th = thr[(int64_t)b * K + v];
+                        if ((th >> 63) && (th & ~(1ull << 63)))  // target -1, active
+                            list[atomicAdd(cnt, 1)] = ((uint32_t)bl << 16) | (uint32_t)v;
+                        return true;
+                    });
+                }
+            }
+            block_sync<WPC>();
+            // (b) a thread per candidate pair: its update draw (kernel.cu:582)
+            const int ncand = cnt[0];
+            for (int j = tid; j < ncand; j += nt) {
+                const uint32_t ce = list[j];
+                const int bl = (int)(ce >> 16), k = (int)(ce & 0xFFFFu);
+                const uint64_t th = thr[(int64_t)(b0 + bl) * K + k];
+                const uint2 u = class_words(pair_draw(cfg, rk, rk_ok, g, t0 + (uint64_t)(b0 + bl), k), (uint32_t)k);
+                ++n_dcalls;
+                if ((uint64_t)u.y < (th & ~(1ull << 63))) {
+                    uint8_t a = (th >> 63) ? 2 : 1;
+                    if (simple[k]) a = ((a == 1) == (wk[k] >= 0)) ? EV_T1B : EV_NONE;
+                    if (a) {
+                        evt[bl * nk + k] = a;
+                        if (use_enz) atomicOr(&enz[bl * KWm + (k >> 5)], 1u << (k & 31));
+                    }
+                }
+            }
+        }
+        // otherwise four consecutive list entries per thread, loaded together;
+        // when two neighbours are the two classes of one class pair of one
+        // sample, one Philox call serves both
+        for (int i0 = lo + 4 * tid; !use_qsel && i0 < hi; i0 += 4 * nt) {  // coalesced: the chunk's pairs
             uint64_t ent[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) ent[j] = i0 + j < hi ? alist[i0 + j] : 0ull;
@@ -659,8 +733,10 @@ extern "C" ytm_status ytm_train_update_counted(const ytm_config *cfg, uint32_t *
         k_pairs<<<(unsigned)cdiv(B, 256), 256, 0, st>>>(cfg->seed, Y, B, cfg->n_classes, t0, pair);
         if ((rc = launch_check("class pairs"))) return rc;
     }
+    const int qsel = cfg->coalesced && cfg->q_select && !cfg->one_negative;
+    int32_t *npos = (int32_t *)(ws + l.npos);
     k_thresholds<<<1, 1024, 0, st>>>(cs, Y, B, cfg->n_classes, cfg->T, cfg->one_negative, pair, thr, amask, colm,
-                                     row_off, alist);
+                                     row_off, alist, qsel, npos);
     if ((rc = launch_check("update thresholds"))) return rc;
     const int nk = cfg->coalesced ? cfg->n_classes : 1;
     // chunks hold whole Type Ib run windows: the whole batch when it is at
@@ -692,7 +768,7 @@ extern "C" ytm_status ytm_train_update_counted(const ytm_config *cfg, uint32_t *
             k_update<NB, true><<<(unsigned)cdiv(cfg->clause_count, 8), 256, smem_wpc, st>>>(
                 *cfg, state, weights, thr, drop, src, B, t0, sel, patch_w, 32, rk, rk_ok, count_patch, pair, amask,
                 colm, row_off,
-                alist, fcm, ctrs);
+                alist, fcm, npos, ctrs);
         });
         return launch_check("feedback");
     }
@@ -707,7 +783,7 @@ extern "C" ytm_status ytm_train_update_counted(const ytm_config *cfg, uint32_t *
         k_update<NB, false><<<cfg->clause_count, tpb, smem, st>>>(*cfg, state, weights, thr, drop, src, B,
                                                                   t0, sel,
                                                                   patch_w, BC, rk, rk_ok, count_patch, pair,
-                                                                  amask, colm, row_off, alist, fcm, ctrs);
+                                                                  amask, colm, row_off, alist, fcm, npos, ctrs);
     });
     return launch_check("feedback");
 }
