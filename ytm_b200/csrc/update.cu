@@ -250,7 +250,13 @@ template <int NB, bool WPC>
 #ifndef YTM_UPD_MINB
 #define YTM_UPD_MINB 4  // 64 registers: measured fastest (no spills)
 #endif
-__global__ void __launch_bounds__(256, YTM_UPD_MINB) k_update(ytm_config cfg, uint32_t *__restrict__ state,
+#ifndef YTM_UPD_MINB_WIDE
+// 12 planes and more: 80 registers (no spills); such models' event lists
+// (at least 4096 states go with wide, many-class workloads) mostly leave
+// shared memory for 3 CTAs of 256 threads anyway
+#define YTM_UPD_MINB_WIDE 3
+#endif
+__global__ void __launch_bounds__(256, (NB >= 12 ? YTM_UPD_MINB_WIDE : YTM_UPD_MINB)) k_update(ytm_config cfg, uint32_t *__restrict__ state,
                                                 int32_t *__restrict__ weights, const uint64_t *__restrict__ thr,
                                                 const uint32_t *__restrict__ drop,
                                                 const LitSrc src, int B, uint64_t t0,
