@@ -55,9 +55,9 @@ L2_BYTES = 126 * 1024 * 1024
 # times it in, from one ncu capture of a reduced-clause model of the same
 # workload, scaled by clauses (the feedback's traffic is per clause); None
 # where no capture was made.
-# configuration 5: 221 MB read + 178 MB written by one k_update launch over
+# configuration 5: 223 MB read + 179 MB written by one k_update launch over
 # 4096 clauses (profiles/k_update_c5.md)
-TRAFFIC_PER_CLAUSE = {"c5": (221e6 + 178e6) / 4096}
+TRAFFIC_PER_CLAUSE = {"c5": (223e6 + 179e6) / 4096}
 
 
 def load_peaks():
@@ -446,9 +446,12 @@ def run_target_c1(args, dev, flush, clk_rows=None):
     ms = sum(a.elapsed_time(b) for a, b in ev)
     value = K * S / (ms / 1000.0)
     launches = count_launches(lambda: eng.train_fit_b1(lits[:S], Yd[:S], 0, None))
-    # e2e from the same state
-    snap.restore()
+    # e2e from the same state, after one untimed call of the same API path
+    # (its host-side set-up happens once, as in any repeated fit)
     Xh = torch.from_numpy(X.view(np.int32)).pin_memory()
+    tm.fit(Xh[:S], y[:S], batch_size=1)
+    tm.last_class_sums.cpu()
+    snap.restore()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
@@ -662,7 +665,12 @@ def main():
 
     # end to end through the public API from the same state: pinned host
     # inputs copied in every step, class sums of the step's last batch read back
+    # (after one untimed call of the same path: its host-side set-up happens
+    # once, as in any repeated fit; then the snapshot's state again)
     Xh = torch.from_numpy(X.view(np.int32)).pin_memory()
+    tm.fit(Xh[:S], y[:S], batch_size=B)
+    tm.last_class_sums.cpu()
+    snap.restore()
     barrier()
     a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
