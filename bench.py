@@ -722,7 +722,8 @@ def main():
                       "chunking": "MultiClassTM._score_device chunks of at most 2^31 bytes of literals + fired bits",
                       "dense_word_tests_per_s": word_tests / (infer_ms / 1000.0),
                       "lop3_peak_per_s": lop3,
-                      "int_pipe_frac": None if sparse else word_tests / (infer_ms / 1000.0) / lop3,
+                      # samples are sharded over the GPUs: against the ceiling of all of them
+                      "int_pipe_frac": None if sparse else word_tests / (infer_ms / 1000.0) / (lop3 * world),
                       "kernel": ("k_match_sparse<any> (compacted include words; dense-equivalent rate)" if sparse
                                  else "k_match<0> (one LOP3 per word test)")},
             "clocks": clk.summary(),

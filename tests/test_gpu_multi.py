@@ -71,6 +71,47 @@ def test_two_gpu_sharding_equals_one_gpu(tmp_path, allreduce):
         np.testing.assert_array_equal(a[k], b[k])
 
 
+ENCODE = r"""
+import os, sys, numpy as np, torch, torch.distributed as dist
+sys.path.insert(0, sys.argv[1])
+rank = int(os.environ["RANK"]); world = int(os.environ["WORLD_SIZE"])
+torch.cuda.set_device(rank)
+if world > 1:
+    dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
+from ytm_b200.cutm import MultiClassTM
+from ytm_b200 import synthetic
+X, y = synthetic.prototypes(101, seed=4)
+out = {}
+for name, pd in (("single", (28, 28)), ("conv", (10, 10))):
+    tm = MultiClassTM(number_of_clauses_per_class=20, T=10, s=5.0, dim=(28, 28, 1), n_classes=10, patch_dim=pd,
+                      seed=2)
+    for n in (101, 3, 2):  # ragged shares, the last one padded; one row per rank
+        out[f"{name}_{n}"] = tm._literals_device(X[:n], False).cpu().numpy()
+        out[f"{name}_{n}_pinned"] = tm._literals_device(torch.from_numpy(X[:n].view(np.int32)).pin_memory(),
+                                                        False).cpu().numpy()
+if rank == world - 1:
+    np.savez(sys.argv[2], **out)
+if world > 1:
+    dist.destroy_process_group()
+"""
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_host_input_rows_sharded(tmp_path):
+    """Host inputs on 2 GPUs: each rank copies and encodes half of the rows and
+    the encoded rows are all-gathered; the result equals one GPU's encoding
+    of all rows (literal words and packed bit images, ragged row counts)."""
+    s1, s2 = tmp_path / "e1.py", tmp_path / "e2.py"
+    s1.write_text(ENCODE)
+    s2.write_text(ENCODE)
+    _run(1, tmp_path / "one.npz", tmp_path, script=s1)
+    _run(2, tmp_path / "two.npz", tmp_path, script=s2)
+    a, b = np.load(tmp_path / "one.npz"), np.load(tmp_path / "two.npz")
+    assert set(a.files) == set(b.files)
+    for k in a.files:
+        np.testing.assert_array_equal(a[k], b[k])
+
+
 PEER = r"""
 import os, sys, ctypes as ct, numpy as np, torch, torch.distributed as dist
 sys.path.insert(0, sys.argv[1])

@@ -139,21 +139,6 @@ __global__ void __launch_bounds__(1024) k_thresholds(const int32_t *__restrict__
                     const int k = pair[2 * row + q];
                     if (k >= 0 && ((am[k >> 5] >> (k & 31)) & 1u)) alist[pos++] = pair_entry(thr, row, k, K);
                 }
-            } else if (qsel) {  // the sample's target +1 pairs first, their count in npos
-                int np = 0;
-                for (int pass = 0; pass < 2; ++pass)
-                    for (int m = 0; m < KWm; ++m)
-                        for (uint32_t v = am[m]; v; v &= v - 1u) {
-                            const int k = m * 32 + __ffs(v) - 1;
-                            if ((int)(thr[(int64_t)row * K + k] >> 63) != pass) continue;
-                            alist[pos++] = pair_entry(thr, row, k, K);
-                            np += pass == 0;
-                        }
-                npos[row] = np;
-            } else {
-                for (int m = 0; m < KWm; ++m)
-                    for (uint32_t v = am[m]; v; v &= v - 1u)
-                        alist[pos++] = pair_entry(thr, row, m * 32 + __ffs(v) - 1, K);
             }
         }
         __syncthreads();
@@ -161,6 +146,26 @@ __global__ void __launch_bounds__(1024) k_thresholds(const int32_t *__restrict__
         __syncthreads();
     }
     if (threadIdx.x == 0) row_off[B] = base_s;
+    if (one_neg) return;
+    // the pair lists: a warp per sample, 32 classes per ballot, classes in
+    // ascending order (with qsel: the target +1 pairs, then the target -1
+    // ones); row_off was written by this block before the barrier above
+    for (int row = wid; row < B; row += nw) {
+        int pos = row_off[row], np = 0;
+        const uint32_t *am = am_all + (int64_t)row * KWm;
+        for (int pass = 0; pass < (qsel ? 2 : 1); ++pass) {
+            for (int m = 0; m < KWm; ++m) {
+                const int k = m * 32 + lane;
+                bool a = (am[m] >> lane) & 1u;
+                if (a && qsel) a = (int)(thr[(int64_t)row * K + k] >> 63) == pass;
+                const uint32_t bal = __ballot_sync(0xFFFFFFFFu, a);
+                if (a) alist[pos + __popc(bal & ((1u << lane) - 1u))] = pair_entry(thr, row, k, K);
+                pos += __popc(bal);
+                if (pass == 0) np += __popc(bal);
+            }
+        }
+        if (qsel && lane == 0) npos[row] = np;
+    }
 }
 
 // Patch literal words u32 [B][P][W] of samples 0..B-1 of the bit images.

@@ -312,7 +312,37 @@ class BaseTM:
         self.engine.reset_weights()
 
     # -- encoding (base.py:224-263) ----------------------------------------------------
+    def _host_rows_sharded(self, X) -> bool:
+        """Host inputs on a multi-GPU NCCL group: each rank copies only its
+        share of the rows and the encoded rows are all-gathered over NVLink."""
+        on_host = not isinstance(X, torch.Tensor) or X.device.type == "cpu"
+        return (on_host and self.world > 1 and self.device.type == "cuda" and X.shape[0] >= self.world
+                and dist.get_backend(self._pg) == "nccl")
+
+    def _sharded_input(self, X, fn) -> torch.Tensor:
+        """fn(device rows) for all rows of host input X: rank r copies rows
+        [r * n, (r + 1) * n) (n = ceil(N / world); the last share padded with
+        zero rows), encodes them, and the encoded shares are all-gathered.
+        Every rank ends with the same tensor as fn(all rows) gives, while the
+        host-to-device traffic per rank is 1/world of the input."""
+        N = X.shape[0]
+        n = -(-N // self.world)
+        lo, hi = min(N, self.rank * n), min(N, (self.rank + 1) * n)
+        part = self._to_device(X[lo:hi])
+        if hi - lo < n:
+            part = torch.cat([part, part.new_zeros((n - (hi - lo),) + tuple(part.shape[1:]))])
+        mine = fn(part).contiguous()
+        full = torch.empty((n * self.world,) + tuple(mine.shape[1:]), dtype=mine.dtype, device=mine.device)
+        dist.all_gather_into_tensor(full, mine, group=self._pg)
+        return full[:N]
+
     def _encode_device(self, X) -> torch.Tensor:
+        if not isinstance(X, torch.Tensor):
+            assert X.ndim == 2, "X must be a 2D array (samples, dim0 * dim1 * dim2)."
+            assert X.dtype == np.uint32, "X must be of type np.uint32."
+        if self._host_rows_sharded(X):
+            assert X.shape[1] == self.dim[0] * self.dim[1] * self.dim[2], "X has the wrong number of features."
+            return self._sharded_input(X, self.engine.encode)
         if isinstance(X, torch.Tensor):
             Xd = X.to(self.device).to(torch.int32).contiguous()
             assert Xd.dim() == 2, "X must be a 2D array (samples, dim0 * dim1 * dim2)."
@@ -330,6 +360,12 @@ class BaseTM:
         sample), per-patch literal words [N, 1, W] for single-patch models."""
         if self.number_of_patches == 1:
             return self._encode_device(X)
+        if not isinstance(X, torch.Tensor):
+            assert X.ndim == 2, "X must be a 2D array (samples, dim0 * dim1 * dim2)."
+            assert X.dtype == np.uint32, "X must be of type np.uint32."
+        if self._host_rows_sharded(X):
+            assert X.shape[1] == self.dim[0] * self.dim[1] * self.dim[2], "X has the wrong number of features."
+            return self._sharded_input(X, self.engine.pack_images)
         if isinstance(X, torch.Tensor):
             Xd = X.to(self.device).to(torch.int32).contiguous()
             assert Xd.dim() == 2, "X must be a 2D array (samples, dim0 * dim1 * dim2)."
