@@ -391,6 +391,19 @@ def max_over_ranks(v, world, dev):
     return float(t.item())
 
 
+def match_counts():
+    """(tiles, chunks) of the dense clause match on the current device since
+    the previous call (ytm_match_counters reads and clears them)."""
+    import ctypes as ct
+
+    import torch
+    from ytm_b200 import _lib
+    out = (ct.c_uint64 * 2)()
+    _lib.check(_lib.load().ytm_match_counters(out, ct.c_void_p(torch.cuda.current_stream().cuda_stream)),
+               "ytm_match_counters")
+    return int(out[0]), int(out[1])
+
+
 def device_lits(name, tm, n, dev, seed=777):
     """The engine input of n synthetic samples (literals [n, 1, W], or packed
     bit images for convolutional models), generated and encoded in chunks
@@ -692,6 +705,7 @@ def main():
     lits_i = device_lits(name, tm, ni, dev)
     for _ in range(2):  # warm-up at the chunk size the timed call uses (its workspace is then allocated)
         tm._score_device(lits_i[:min(ni, 262144)])
+    match_counts()  # clears the device's match counters
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     flush.zero_()
@@ -700,6 +714,13 @@ def main():
     e1.record()
     barrier()
     infer_ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    tiles, chunks = match_counts()  # executed by this rank's timed call
+    if world > 1:
+        import torch.distributed as dist
+        tc = torch.tensor([tiles, chunks], dtype=torch.float64, device=dev)
+        dist.all_reduce(tc)
+        tiles, chunks = int(tc[0].item()), int(tc[1].item())
+    executed_tests = chunks * 64 * 64 * 32  # a chunk: 32 words x 64 x 64 (row, clause) pairs, one LOP3 each
     infer_value = ni / (infer_ms / 1000.0)
     word_tests = ni * cfg.clauses * cfg.patches * cfg.words  # all clauses (every rank scores its sample slice)
     sparse = cfg.patches > 1 and cfg.words * 129 * 4 <= 220 * 1024
@@ -722,10 +743,19 @@ def main():
                       "chunking": "MultiClassTM._score_device chunks of at most 2^31 bytes of literals + fired bits",
                       "dense_word_tests_per_s": word_tests / (infer_ms / 1000.0),
                       "lop3_peak_per_s": lop3,
-                      # samples are sharded over the GPUs: against the ceiling of all of them
-                      "int_pipe_frac": None if sparse else word_tests / (infer_ms / 1000.0) / (lop3 * world),
+                      # executed: the 32-word chunks the match tiles processed (device
+                      # counters; a tile stops at the chunk after which every pair has a
+                      # violation); dense-equivalent: W word tests per (sample, clause)
+                      # pair, which can exceed the ceiling; samples are sharded over the
+                      # GPUs, so both against the ceiling of all of them
+                      "executed_word_tests_per_s": executed_tests / (infer_ms / 1000.0),
+                      "match_tiles": tiles, "match_chunks": chunks,
+                      "chunks_per_tile": chunks / tiles if tiles else None,
+                      "int_pipe_frac": None if sparse else executed_tests / (infer_ms / 1000.0) / (lop3 * world),
+                      "dense_equiv_frac": word_tests / (infer_ms / 1000.0) / (lop3 * world),
                       "kernel": ("k_match_sparse<any> (compacted include words; dense-equivalent rate)" if sparse
-                                 else "k_match<0> (one LOP3 per word test)")},
+                                 else "k_match<0> (64 x 64 tiles, one LOP3 per word test, early exit "
+                                      "once every pair of the tile is violated; dense-equivalent rate)")},
             "clocks": clk.summary(),
         }
         if target is not None:

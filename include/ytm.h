@@ -345,6 +345,14 @@ ytm_status ytm_infer_noalloc(const ytm_config *cfg, const uint32_t *state, const
                              const int32_t *bias, const uint32_t *lits, int64_t N, int32_t *cs,
                              void *stream);
 
+/* Executed work of the dense clause match (inference and transforms of the
+ * current device) since the previous call: out[0] = 64 x 64 (row, clause)
+ * tiles, out[1] = 32-word chunks they processed (a tile stops after the chunk
+ * at which every one of its pairs has a violation).  Reads and clears the
+ * counts; synchronizes the stream.  Measurement entry point with no
+ * reference counterpart. */
+ytm_status ytm_match_counters(uint64_t *out, void *stream);
+
 /* Message of the last failing call on this thread ("" if none). */
 const char *ytm_last_error(void);
 

@@ -193,3 +193,44 @@ def test_empty_and_single_sample_inputs():
     assert tm.sample_counter == 2
     assert tm.transform(X1).shape == (1, tm.number_of_clauses)
     assert tm.transform_patchwise(X1).shape == (1, tm.number_of_clauses, tm.number_of_patches)
+
+
+def test_match_early_exit_counts_and_parity():
+    """The dense match tiles stop once every (sample, clause) pair of a tile has
+    a violation: clauses 0..127 include a literal that is 0 in every sample
+    and sits in the first 32-word chunk, so their tiles stop after one of the
+    four chunks; the other clauses match often and run to the end.  Class sums
+    equal the oracle's, and the device counters show the skipped chunks."""
+    import ctypes as ct
+
+    import torch
+    from ytm_b200 import _lib
+    kw = dict(number_of_clauses_per_class=200, T=20, s=4.0, dim=(2048, 1, 1), n_classes=4, seed=5)
+    tm = MultiClassTM(**kw)
+    rng = np.random.default_rng(1)
+    N = 200
+    X = (rng.random((N, 2048)) < 0.9).astype(np.uint32)
+    X[:, :32] = 0
+    C, L = tm.engine.C, 2 * 2048
+    assert C == 200
+    ta = rng.integers(0, 128, size=(C, L), dtype=np.uint32)  # 8-bit states: include at >= 128
+    for c in range(C):
+        if c < 128:
+            ta[c, c % 32] = 200  # x_(c mod 32), always 0: violated in word 0
+        else:
+            ta[c, rng.integers(100, 1024, size=2)] = 200  # mostly 1
+    tm.engine.set_ta_state(ta)
+    tm._model_version += 1
+    lib = _lib.load()
+    out = (ct.c_uint64 * 2)()
+    st = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
+    _lib.check(lib.ytm_match_counters(out, st))
+    _, cs = tm.predict(X)
+    _lib.check(lib.ytm_match_counters(out, st))
+    tiles, chunks = int(out[0]), int(out[1])
+    o = O.Oracle(**kw)
+    np.testing.assert_array_equal(cs, o.infer(ta, o.init_weights(), o.encode(X)).astype(np.float32))
+    row_tiles, clause_tiles = -(-N // 64), -(-C // 64)
+    assert tiles == row_tiles * clause_tiles
+    # clause tiles 0 and 1 hold clauses 0..127: one chunk each; the rest run all 4
+    assert chunks == row_tiles * (2 * 1 + (clause_tiles - 2) * 4)

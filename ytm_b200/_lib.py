@@ -25,7 +25,7 @@ EXPORTS = (
     "ytm_pack_images_thermometer",
     "ytm_encode_thermometer", "ytm_nccl_unique_id", "ytm_nccl_comm_init", "ytm_nccl_comm_destroy",
     "ytm_train_fit_batches", "ytm_peer_ar_create", "ytm_peer_ar_open", "ytm_peer_allreduce_i32",
-    "ytm_peer_ar_status", "ytm_peer_ar_destroy", "ytm_config_size",
+    "ytm_peer_ar_status", "ytm_peer_ar_destroy", "ytm_config_size", "ytm_match_counters",
 )
 
 
@@ -83,6 +83,7 @@ _SIGS = {
     "ytm_train_selection": ([_CFG, _I32, _P, _P, _P], ct.c_int),
     "ytm_train_fit_b1": ([_CFG, _P, _P, _P, _P, _P, _P, _I64, _U64, _P, _P, _P], ct.c_int),
     "ytm_infer_noalloc": ([_CFG, _P, _P, _P, _P, _I64, _P, _P], ct.c_int),
+    "ytm_match_counters": ([_P, _P], ct.c_int),
     "ytm_infer_include": ([_CFG, _P, _P, _P, _P, _I64, _P, _P, _P], ct.c_int),
     "ytm_encode_thermometer": ([_CFG, _P, _I64, _I32, _P, _P, _P], ct.c_int),
     "ytm_nccl_unique_id": ([_P], ct.c_int),

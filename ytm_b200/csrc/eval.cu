@@ -27,7 +27,7 @@ constexpr int RT = 64, CT = 64, KW = 32, XS = RT + 4;
 // owns in the 64 x 64 tile at (row0, c0); 32-word chunks staged in shared
 // memory, no work on words past W.
 template <bool IMG>
-__device__ __forceinline__ void tile_violations(const uint32_t *__restrict__ inc, const LitSrc &src,
+__device__ __forceinline__ int tile_violations(const uint32_t *__restrict__ inc, const LitSrc &src,
                                                 int64_t R, int C, int W, int64_t row0, int c0,
                                                 uint32_t (*xs)[XS], uint32_t (*is)[XS], uint32_t (&v)[4][4]) {
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -35,6 +35,7 @@ __device__ __forceinline__ void tile_violations(const uint32_t *__restrict__ inc
     for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) v[i][j] = 0u;
+    int nch = 0;
     for (int w0 = 0; w0 < W; w0 += KW) {
         const int kwn = min(KW, W - w0);  // no work on words past W
 #pragma unroll
@@ -68,9 +69,24 @@ __device__ __forceinline__ void tile_violations(const uint32_t *__restrict__ inc
 #pragma unroll
                 for (int j = 0; j < 4; ++j) v[i][j] |= ia[j] & ~xa[i];
         }
-        __syncthreads();
+        // early exit: once every in-range (row, clause) pair of the tile has a
+        // violation, the remaining words cannot make any of them match (only
+        // v == 0 is read by the callers)
+        uint32_t alive = 0u;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                alive |= (uint32_t)(v[i][j] == 0u && row0 + ty * 4 + i < R && c0 + tx * 4 + j < C);
+        ++nch;
+        if (!__syncthreads_or((int)alive)) break;
     }
+    return nch;
 }
+
+// Executed work of the inference / transform match: [0] tiles, [1] 32-word
+// chunks those tiles processed (read and cleared by ytm_match_counters).
+static __device__ unsigned long long g_match_counts[2];
 
 template <int MODE, bool IMG>
 __global__ void __launch_bounds__(256) k_match(const uint32_t *__restrict__ inc, const LitSrc src,
@@ -81,7 +97,11 @@ __global__ void __launch_bounds__(256) k_match(const uint32_t *__restrict__ inc,
     const int64_t row0 = (int64_t)blockIdx.x * RT;
     const int c0 = blockIdx.y * CT;
     uint32_t v[4][4];
-    tile_violations<IMG>(inc, src, R, C, W, row0, c0, xs, is, v);
+    const int nch = tile_violations<IMG>(inc, src, R, C, W, row0, c0, xs, is, v);
+    if (tid == 0) {
+        atomicAdd(&g_match_counts[0], 1ull);
+        atomicAdd(&g_match_counts[1], (unsigned long long)nch);
+    }
 
     const int cb = c0 + tx * 4;
 #pragma unroll
@@ -832,6 +852,24 @@ ytm_status ytm_train_selection(const ytm_config *cfg, int32_t B, const void *wor
     return cuda_check(cudaMemcpyAsync(sel, (const char *)workspace + l.sel, (size_t)B * cfg->clause_count * 4,
                                       cudaMemcpyDeviceToDevice, as_stream(stream)),
                       "selection copy");
+}
+
+ytm_status ytm_match_counters(uint64_t *out, void *stream) {
+    if (!out) return fail(YTM_ERR_ARG, "bad argument");
+    cudaStream_t st = as_stream(stream);
+    unsigned long long h[2] = {0ull, 0ull};
+    ytm_status rc = cuda_check(cudaMemcpyFromSymbolAsync(h, g_match_counts, sizeof h, 0, cudaMemcpyDeviceToHost, st),
+                               "match counters");
+    if (!rc) rc = cuda_check(cudaStreamSynchronize(st), "match counters");
+    if (rc) return rc;
+    const unsigned long long z[2] = {0ull, 0ull};
+    if ((rc = cuda_check(cudaMemcpyToSymbolAsync(g_match_counts, z, sizeof z, 0, cudaMemcpyHostToDevice, st),
+                         "match counters")))
+        return rc;
+    if ((rc = cuda_check(cudaStreamSynchronize(st), "match counters"))) return rc;
+    out[0] = h[0];
+    out[1] = h[1];
+    return YTM_OK;
 }
 
 }  // extern "C"
