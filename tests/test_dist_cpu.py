@@ -180,3 +180,42 @@ def test_seed_none_is_shared_by_ranks(tmp_path):
     mp.spawn(_seed_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
     keys = [int(open(tmp_path / f"k{r}").read()) for r in range(2)]
     assert keys[0] == keys[1]
+
+
+def _shard_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from ytm_b200.cutm import MultiClassTM
+        tm = MultiClassTM(_engine_factory=OracleShardEngine, **KW)
+        X = np.arange(7 * 5, dtype=np.uint32).reshape(7, 5)
+        calls = []
+
+        def enc(t):  # stands in for the engine's encode: rows -> [rows, 2, 3]
+            calls.append(t.shape[0])
+            return (t[:, :3].unsqueeze(1).repeat(1, 2, 1) * 2 + 1).contiguous()
+        res = {}
+        for n in (7, 2, 3):  # shares 4+3 (last padded), 1+1, 2+1
+            out = tm._sharded_input(X[:n], enc)
+            res[f"n{n}"] = out.numpy()
+            res[f"c{n}"] = np.array(calls[-1:])
+        # host inputs on a gloo group are not sharded (the NCCL path only)
+        res["sharded_on_gloo"] = np.array([tm._host_rows_sharded(X)])
+        np.savez(os.path.join(out_dir, f"s{rank}.npz"), **res)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_sharded_host_input_gathers_all_rows(tmp_path):
+    """BaseTM._sharded_input on 2 gloo ranks: each rank encodes ceil(N/2)
+    rows (the last share padded with zero rows) and every rank ends with the
+    encoding of all N rows in order."""
+    mp.spawn(_shard_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    X = np.arange(7 * 5, dtype=np.int32).reshape(7, 5)
+    for r in range(2):
+        got = np.load(tmp_path / f"s{r}.npz")
+        for n in (7, 2, 3):
+            want = np.repeat(X[:n, None, :3], 2, axis=1) * 2 + 1
+            np.testing.assert_array_equal(got[f"n{n}"], want)
+            assert got[f"c{n}"][0] == -(-n // 2)
+        assert not got["sharded_on_gloo"][0]
