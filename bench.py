@@ -404,6 +404,54 @@ def match_counts():
     return int(out[0]), int(out[1])
 
 
+def planted_infer(tm, lits_i, ni, dev, world, flush, lop3, barrier, rule_seed=1005, n_features=16384):
+    """Configuration-5 inference on a model whose clauses are the planted
+    rules (clause g includes the 8 literals of rule g mod 1000, the table of
+    synthetic.rules_torch): the clauses fire on the samples of their rule, so
+    nearly every 64 x 64 match tile holds a matching pair and runs all its
+    chunks, the converged-model counterpart of the early-training figure.
+    Replaces the model's states (the last leg of the run)."""
+    import torch
+    eng = tm.engine
+    C, W, NB = eng.C, eng.W, eng.NB
+    rng = np.random.default_rng(rule_seed)
+    feat = rng.integers(0, n_features, (100, 10, 8))
+    pol = rng.random((100, 10, 8)) < 0.5
+    rule = (tm.clause_lo + np.arange(C)) % 1000
+    cls, r = rule // 10, rule % 10
+    lit = np.where(pol[cls, r], feat[cls, r], n_features + feat[cls, r])  # [C, 8] literal indices
+    top = np.zeros(C * W, np.uint32)
+    np.bitwise_or.at(top, (np.arange(C)[:, None] * W + lit // 32).reshape(-1),
+                     (np.uint32(1) << (lit % 32).astype(np.uint32)).reshape(-1))
+    # the include mask is the top bit plane; the other planes are cleared
+    eng.state.zero_()
+    eng.state.view(NB, C * W)[NB - 1].copy_(torch.from_numpy(top.view(np.int32)))
+    tm._model_version += 1
+    tm._score_device(lits_i[:min(ni, 262144)])  # warm-up (include masks, caches)
+    match_counts()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    flush.zero_()
+    e0.record()
+    cs = tm._score_device(lits_i)
+    e1.record()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    tiles, chunks = match_counts()
+    nz = int((cs != 0).any(dim=1).sum().item())  # samples with a fired clause
+    if world > 1:
+        import torch.distributed as dist
+        tc = torch.tensor([tiles, chunks], dtype=torch.float64, device=dev)
+        dist.all_reduce(tc)
+        tiles, chunks = int(tc[0].item()), int(tc[1].item())
+    executed = chunks * 64 * 64 * 32
+    return {"value": ni / (ms / 1000.0), "unit": "samples/s", "samples": ni,
+            "model": "clause g includes the 8 literals of planted rule g mod 1000 (rules_torch table)",
+            "samples_with_nonzero_class_sums": nz,
+            "match_tiles": tiles, "match_chunks": chunks, "chunks_per_tile": chunks / tiles if tiles else None,
+            "int_pipe_frac": executed / (ms / 1000.0) / (lop3 * world)}
+
+
 def device_lits(name, tm, n, dev, seed=777):
     """The engine input of n synthetic samples (literals [n, 1, W], or packed
     bit images for convolutional models), generated and encoded in chunks
@@ -724,6 +772,12 @@ def main():
     infer_value = ni / (infer_ms / 1000.0)
     word_tests = ni * cfg.clauses * cfg.patches * cfg.words  # all clauses (every rank scores its sample slice)
     sparse = cfg.patches > 1 and cfg.words * 129 * 4 <= 220 * 1024
+    planted = None
+    if name == "c5" and world == 1:  # one rank: a failed leg cannot leave others waiting at a barrier
+        try:
+            planted = planted_infer(tm, lits_i, ni, dev, world, flush, lop3, barrier)
+        except Exception as e:  # a measurement leg: the main line stands without it
+            planted = {"error": f"{type(e).__name__}: {e}"}
     del lits_i
 
     target = None
@@ -755,7 +809,8 @@ def main():
                       "dense_equiv_frac": word_tests / (infer_ms / 1000.0) / (lop3 * world),
                       "kernel": ("k_match_sparse<any> (compacted include words; dense-equivalent rate)" if sparse
                                  else "k_match<0> (64 x 64 tiles, one LOP3 per word test, early exit "
-                                      "once every pair of the tile is violated; dense-equivalent rate)")},
+                                      "once every pair of the tile is violated; dense-equivalent rate)"),
+                      "planted_rules_model": planted},
             "clocks": clk.summary(),
         }
         if target is not None:
