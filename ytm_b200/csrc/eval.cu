@@ -31,10 +31,12 @@ __device__ __forceinline__ int tile_violations(const uint32_t *__restrict__ inc,
                                                 int64_t R, int C, int W, int64_t row0, int c0,
                                                 uint32_t (*xs)[XS], uint32_t (*is)[XS], uint32_t (&v)[4][4]) {
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    // out-of-range pairs start violated (callers bounds-check before reading
+    // v), so that the exit test below is the minimum of the 16 words
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) v[i][j] = 0u;
+        for (int j = 0; j < 4; ++j) v[i][j] = (row0 + ty * 4 + i < R && c0 + tx * 4 + j < C) ? 0u : 0xFFFFFFFFu;
     int nch = 0;
     for (int w0 = 0; w0 < W; w0 += KW) {
         const int kwn = min(KW, W - w0);  // no work on words past W
@@ -72,14 +74,13 @@ __device__ __forceinline__ int tile_violations(const uint32_t *__restrict__ inc,
         // early exit: once every in-range (row, clause) pair of the tile has a
         // violation, the remaining words cannot make any of them match (only
         // v == 0 is read by the callers)
-        uint32_t alive = 0u;
+        uint32_t m = v[0][0];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                alive |= (uint32_t)(v[i][j] == 0u && row0 + ty * 4 + i < R && c0 + tx * 4 + j < C);
+            for (int j = 0; j < 4; ++j) m = min(m, v[i][j]);
         ++nch;
-        if (!__syncthreads_or((int)alive)) break;
+        if (!__syncthreads_or((int)(m == 0u))) break;
     }
     return nch;
 }
